@@ -1,0 +1,352 @@
+#!/usr/bin/env python3
+"""OLMoE-1B-7B 4-bit batched decode benchmark on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--batch B] [--kv-len L]
+    python bench.py --impl reference ...      # the CPU reference arm
+
+A step is one decode token for each of B requests through the full 16-layer
+random-init OLMoE-1B-7B (4-bit MLX-affine weights, group 64) with an fp16 KV
+cache pre-filled with N(0, 1) to length L.  Requests are data parallel: each
+rank holds a full replica and its own B requests, no collective on the data
+path ("scaling": "weak").  `value` is whole-job tokens/s with inputs resident
+in HBM; `e2e` is the same metric through the C-ABI session call with host
+token ids in and host fp32 logits out (copies inside the timed region).
+The KV cache (B x 16 layers x 2 x 16 x L x 128 x 2 B; 34 GB at B=64) is far
+larger than L2, so no flush is needed between steps.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "OLMoE-4bit decode & prefill tok/s per B200; MoE GB/s vs HBM peak"
+FALLBACK_HBM_GBS = 6650.0
+
+# Algorithmic bytes per launch of each traced phase (per layer), batch B, KV
+# length L (keys read per request = L + 1 including this step's slot).
+H, W, I, E, K_TOP, V = 2048, 2048, 1024, 64, 8, 50304
+EXPERT_PROJ_BYTES = I * H // 2 + I * (H // 64) * 4  # one expert projection: 1,179,648 B
+
+
+def phase_bytes(phase, B, L):
+    act = 2
+    if phase == "attention":
+        return B * 16 * (L + 1) * 128 * 2 * 2 + B * 3 * W * act + B * W * act
+    if phase == "qkv_proj":
+        return 3 * (W * H // 2 + W * (H // 64) * 4) + B * H * act + B * 3 * W * act
+    if phase == "o_proj":
+        return (H * W // 2 + H * (W // 64) * 4) + B * (W + 2 * H) * act
+    if phase in ("moe_gate_up", "moe_down"):
+        unique = E * (1 - (1 - K_TOP / E) ** B)
+        mult = 2 if phase == "moe_gate_up" else 1
+        return unique * mult * EXPERT_PROJ_BYTES
+    if phase == "lm_head":
+        return V * H // 2 + V * (H // 64) * 4 + B * V * 4
+    return None
+
+
+def env_rank():
+    return (int(os.environ.get("RANK", 0)), int(os.environ.get("LOCAL_RANK", 0)),
+            int(os.environ.get("WORLD_SIZE", 1)))
+
+
+def measured_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            d = json.loads(p.read_text())
+            return float(d["hbm_gbs"]), "measured"
+        except Exception:
+            pass
+    return FALLBACK_HBM_GBS, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms."""
+    FIELDS = ("index,uuid,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, uuid):
+        self.uuid = uuid
+        self.proc = None
+        self.path = Path("/tmp") / f"tf_clocks_{os.getpid()}.csv"
+
+    def start(self):
+        try:
+            self.f = open(self.path, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-lms", "200"], stdout=self.f, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if not self.proc:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        self.f.close()
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.path.read_text().splitlines():
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 10:
+                continue
+            if self.uuid and self.uuid not in parts[1]:
+                continue
+            try:
+                sm.append(float(parts[2]))
+                mx.append(float(parts[3]))
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[6:10]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def build_model(B, L, cap, device):
+    import torch
+
+    from trifuse_b200.model import Config, Model, Session
+    from trifuse_b200.quant import synthetic_olmoe
+    cfg = Config(capacity=cap)
+    w = synthetic_olmoe(cfg, seed=20260102, device=f"cuda:{device}")
+    model = Model(cfg, w, device=device)
+    del w
+    torch.cuda.empty_cache()
+    sess = Session(model, max_batch=B, capacity=cap)
+    g = torch.Generator(device=f"cuda:{device}")
+    g.manual_seed(20260103)
+    for layer in range(cfg.layers):
+        k, v = sess.kv_tensors(layer)
+        for t in (k, v):
+            for b0 in range(0, B, 16):
+                t[b0:b0 + 16, :, :L].normal_(generator=g)
+    torch.cuda.synchronize()
+    return cfg, model, sess
+
+
+def time_steps(sess, ids, logits, steps, warmup, L, B, stream, barrier):
+    import torch
+    sess.set_lengths([L] * B)
+    for i in range(warmup):
+        sess.decode(ids[i], logits=logits)
+    torch.cuda.synchronize()
+    barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(steps):
+        sess.decode(ids[warmup + i], logits=logits)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    return e0.elapsed_time(e1) / steps
+
+
+def cpu_sample(B, L, seed=5):
+    """One decode layer of the oracle for B requests at KV length L, plus the
+    lm_head; returns (seconds for the extrapolated 16-layer step, details)."""
+    import numpy as np
+
+    import oracle
+    rng = np.random.default_rng(seed)
+    cfg = oracle.OLMoEConfig(act="f16")
+
+    def rand_affine(shape):
+        *lead, rows, cols = shape
+        q = rng.integers(0, 2 ** 32, size=(*lead, rows, cols // 8), dtype=np.uint32)
+        s = (rng.random((*lead, rows, cols // 64)) * 0.004 + 0.001).astype(np.float16)
+        b = (-7.5 * s.astype(np.float32)).astype(np.float16)
+        return q, s, b
+
+    norm = lambda n: (1 + 0.1 * rng.standard_normal(n)).astype(np.float16)  # noqa: E731
+    layer = dict(input_norm=norm(H), post_norm=norm(H), q_norm=norm(W), k_norm=norm(W),
+                 q=rand_affine((W, H)), k=rand_affine((W, H)), v=rand_affine((W, H)), o=rand_affine((H, W)),
+                 router=rand_affine((E, H)),
+                 experts={"gate": rand_affine((E, I, H)), "up": rand_affine((E, I, H)),
+                          "down": rand_affine((E, H, I))})
+    head = rand_affine((V, H))
+    # One N(0,1) K and V block shared by every request: the timed math is the
+    # same per request and host memory stays bounded.
+    k1 = rng.standard_normal((16, L + 1, 128), dtype=np.float32).astype(np.float16).astype(np.float32)
+    v1 = rng.standard_normal((16, L + 1, 128), dtype=np.float32).astype(np.float16).astype(np.float32)
+    kc = [k1] * B
+    vc = [v1] * B
+    h = oracle.round_f16(rng.standard_normal((B, H)).astype(np.float32))
+    t0 = time.perf_counter()
+    out = oracle.decode_layer_batched(h, layer, cfg, kc, vc, [L] * B, fast=True)
+    t1 = time.perf_counter()
+    oracle.affine_qmm(oracle.rms_norm(out, norm(H), 1e-5, "f16"), *head, "f16")
+    t2 = time.perf_counter()
+    step = 16 * (t1 - t0) + (t2 - t1)
+    return step, {"layer_s": t1 - t0, "head_s": t2 - t1}
+
+
+def cpu_threads():
+    try:
+        import threadpoolctl
+        info = threadpoolctl.threadpool_info()
+        n = max((i.get("num_threads", 1) for i in info), default=1)
+        return int(n)
+    except Exception:
+        return os.cpu_count() or 1
+
+
+def run_reference(args, rank, world):
+    """CPU reference arm: the oracle port of the reference's operators on the
+    host cores, same metric/config; rank 0 only."""
+    if rank != 0:
+        return
+    samples = []
+    for _ in range(args.warmup):
+        cpu_sample(args.batch, args.kv_len)
+    for _ in range(args.steps):
+        s, _d = cpu_sample(args.batch, args.kv_len)
+        samples.append(s)
+    step_s = sum(samples) / len(samples)
+    value = args.batch / step_s
+    cores = cpu_threads()
+    line = {"metric": METRIC, "impl": "reference", "value": value, "unit": "tok/s", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": step_s * 1000,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
+            "data": "synthetic",
+            "config": {"workload": f"decode B={args.batch} L={args.kv_len} OLMoE-1B-7B 4-bit (config 2)",
+                       "batch": args.batch, "kv_len": args.kv_len, "layers": 16},
+            "cpu_baseline": {"value": value, "unit": "tok/s", "cores": cores, "kind": "port",
+                             "sample": f"one of 16 decode layers + lm_head for {args.batch} requests at "
+                                       f"L={args.kv_len}, numpy oracle, step time = 16 x layer + head"},
+            "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--batch", type=int, default=64)
+    ap.add_argument("--kv-len", type=int, default=4096)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    rank, local_rank, world = env_rank()
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+        return
+
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+
+    from trifuse_b200 import lib
+    assert args.warmup >= 1
+    torch.cuda.set_device(local_rank)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300),
+                                device_id=torch.device(f"cuda:{local_rank}"))
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    B, L = args.batch, args.kv_len
+    cap = L + 2 * (args.warmup + args.steps) + 8
+    cfg, model, sess = build_model(B, L, cap, local_rank)
+    stream = torch.cuda.current_stream()
+    g = torch.Generator(device="cuda")
+    g.manual_seed(20260104 + rank)
+    n_ids = args.warmup + args.steps
+    ids = torch.randint(0, cfg.vocab, (n_ids, B), device="cuda", generator=g, dtype=torch.int64)
+    logits = torch.empty((B, cfg.vocab), dtype=torch.float32, device="cuda")
+
+    uuid = None
+    try:
+        uuid = str(torch.cuda.get_device_properties(local_rank).uuid)
+    except Exception:
+        pass
+    clocks = ClockSampler(uuid)
+
+    # 1) device-resident throughput
+    launches0 = lib().tf_launch_count()
+    clocks.start()
+    ms = time_steps(sess, ids, logits, args.steps, args.warmup, L, B, stream, barrier)
+    clk = clocks.stop()
+    launches = (lib().tf_launch_count() - launches0) // (args.steps + args.warmup)
+    if world > 1:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    value = B * world / (ms / 1000.0)
+
+    # 2) phase trace of the same workload (roofline of the dominant kernel)
+    sess.trace(True)
+    time_steps(sess, ids, logits, min(args.steps, 4), 1, L, B, stream, barrier)
+    sess.trace(False)
+    phases = sess.trace_read()
+    sess.trace_read()
+    dom = max(phases, key=lambda p: phases[p][0])
+    peak, peak_kind = measured_peaks()
+    tot, cnt = phases[dom]
+    roof = None
+    nbytes = phase_bytes(dom, B, L)
+    if nbytes and cnt:
+        avg_ms = tot / cnt
+        achieved = nbytes / (avg_ms / 1000.0) / 1e9
+        roof = {"bound": "hbm", "kernel": dom, "achieved": achieved, "peak": peak, "unit": "GB/s",
+                "frac": achieved / peak, "peak_source": peak_kind, "traffic": None,
+                "algorithmic_bytes_per_launch": nbytes, "avg_launch_ms": avg_ms}
+    step_phase_ms = {p: round(v[0] / max(1, min(args.steps, 4)), 4) for p, v in phases.items() if v[1]}
+
+    # 3) end to end through the C-ABI call with host buffers
+    ids_host = ids.cpu().pin_memory()
+    logits_host = torch.empty((B, cfg.vocab), dtype=torch.float32, pin_memory=True)
+    e2e_ms = time_steps(sess, ids_host, logits_host, args.steps, args.warmup, L, B, stream, barrier)
+    if world > 1:
+        t = torch.tensor([e2e_ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    e2e = {"value": B * world / (e2e_ms / 1000.0), "unit": "tok/s", "h2d_bytes_per_step": B * (8 + 4),
+           "d2h_bytes_per_step": B * cfg.vocab * 4, "ms_per_step": e2e_ms}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        step_s, det = cpu_sample(B, L)
+        cpu = {"value": B / step_s, "unit": "tok/s", "cores": cpu_threads(), "kind": "port",
+               "sample": f"one of 16 decode layers + lm_head for {B} requests at L={L} (numpy oracle, "
+                         f"layer {det['layer_s']:.2f}s, head {det['head_s']:.2f}s), step = 16 x layer + head"}
+
+    if rank == 0:
+        line = {"metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": "f16", "data": "synthetic (random-init weights, N(0,1) KV)",
+                "config": {"workload": f"decode B={B}/GPU L={L} OLMoE-1B-7B 4-bit (config 2)",
+                           "batch_per_gpu": B, "global_batch": B * world, "kv_len": L, "layers": 16,
+                           "parallelism": f"dp{world} replicas", "l2": "inputs larger than L2 (KV cache)"},
+                "e2e": e2e, "gpu_launches": int(launches), "roofline": roof, "cpu_baseline": cpu,
+                "clocks": clk, "phase_ms_per_step": step_phase_ms}
+        print(json.dumps(line), flush=True)
+    sess.close()
+    model.close()
+    if world > 1:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

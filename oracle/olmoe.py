@@ -26,8 +26,23 @@ Operations are split into two classes.
 from __future__ import annotations
 
 import math
+import os
+from concurrent.futures import ThreadPoolExecutor
 
 import numpy as np
+
+_POOL = None
+
+
+def _pmap(fn, items):
+    """Map over host threads (numpy releases the GIL inside its kernels)."""
+    global _POOL
+    items = list(items)
+    if len(items) <= 1:
+        return [fn(i) for i in items]
+    if _POOL is None:
+        _POOL = ThreadPoolExecutor(max_workers=os.cpu_count() or 1)
+    return list(_POOL.map(fn, items))
 
 F16 = "f16"
 BF16 = "bf16"
@@ -150,8 +165,17 @@ def affine_qmm(x, q, scales, biases, act):
 
     Restates ``native_affine_ops.py:39-45`` (``native_affine_qmm``) and the
     adapter's ``linear`` (``MLXNativeGraniteMoEPrefill.h:539-541``)."""
-    w = dequantize(q, scales, biases)
-    return to_act(f32(x) @ w.T, act)
+    x = f32(x)
+    rows = q.shape[0]
+    step = max(256, -(-rows // (os.cpu_count() or 1)))
+    y = np.empty((*x.shape[:-1], rows), np.float32)
+
+    def part(r0):
+        w = dequantize(q[r0:r0 + step], scales[r0:r0 + step], biases[r0:r0 + step])
+        y[..., r0:r0 + step] = x @ w.T
+
+    _pmap(part, range(0, rows, step))
+    return to_act(y, act)
 
 
 def gather_qmm(x_rows, q, scales, biases, indices, act):
@@ -164,10 +188,13 @@ def gather_qmm(x_rows, q, scales, biases, indices, act):
     indices = np.asarray(indices).astype(np.int64)
     out_dim = q.shape[-2]
     y = np.zeros((x_rows.shape[0], out_dim), dtype=np.float32)
-    for e in np.unique(indices):
+
+    def one(e):
         sel = np.nonzero(indices == e)[0]
         w = dequantize(q[e], scales[e], biases[e])
         y[sel] = x_rows[sel] @ w.T
+
+    _pmap(one, np.unique(indices))
     return to_act(y, act)
 
 
@@ -440,8 +467,9 @@ def rope(x, positions, theta, act):
     return to_act(np.concatenate([o1, o2], axis=-1), act)
 
 
-def sdpa(q, K, V, scale, act, causal_offset=None):
-    """softmax(q K^T * scale) V in fp32, output rounded to act.
+def sdpa(q, K, V, scale, act, causal_offset=None, fast=False):
+    """softmax(q K^T * scale) V, output rounded to act.  float64 math by
+    default; ``fast`` uses float32 BLAS (the timed CPU-baseline variant).
 
     q [Tq, Hh, D]; K, V [Hh, L, D] (float16 cache values).  With
     ``causal_offset`` = absolute position of q row 0, key j is visible to row
@@ -453,6 +481,17 @@ def sdpa(q, K, V, scale, act, causal_offset=None):
     V = f32(V)
     Tq, Hh, D = q.shape
     L = K.shape[1]
+    if fast:
+        s = np.matmul(q.transpose(1, 0, 2), K.transpose(0, 2, 1)) * np.float32(scale)  # [Hh, Tq, L]
+        if causal_offset is not None:
+            t = np.arange(Tq)[:, None]
+            j = np.arange(L)[None, :]
+            s = np.where(j <= causal_offset + t, s, -np.inf)
+        s = s - s.max(axis=-1, keepdims=True)
+        p = np.exp(s)
+        p /= p.sum(axis=-1, keepdims=True)
+        o = np.matmul(p, V).transpose(1, 0, 2)
+        return to_act(o.astype(np.float32), act)
     s = np.einsum("thd,hld->htl", q.astype(np.float64), K.astype(np.float64)) * scale
     if causal_offset is not None:
         t = np.arange(Tq)[:, None]
@@ -523,6 +562,38 @@ def attention_block(h, layer, cfg, k_cache, v_cache, positions):
              causal_offset=start if T > 1 else None)
     proj = affine_qmm(o.reshape(T, Hh * D), *layer["o"], act)
     return to_act(f32(h) + proj, act)
+
+
+def decode_layer_batched(h, layer, cfg, k_caches, v_caches, positions, fast=False):
+    """One layer of batched decode: request b has one new token at absolute
+    position positions[b] and its own cache k_caches[b] / v_caches[b]
+    ([Hh, cap, D], f16 values, updated in place).  Projections and the MoE
+    block run over the batch; attention runs per request.  Same math as
+    ``layer_forward`` applied to each request (MLXNativeGraniteMoEPrefill.h:
+    433-487 with T = 1)."""
+    act = cfg.act
+    B = h.shape[0]
+    D, Hh = cfg.head_dim, cfg.heads
+    W = D * Hh
+    xn = rms_norm(h, layer["input_norm"], cfg.rms_eps, act)
+    q = affine_qmm(xn, *layer["q"], act)
+    k = affine_qmm(xn, *layer["k"], act)
+    v = affine_qmm(xn, *layer["v"], act)
+    q = rms_norm(q, layer["q_norm"], cfg.rms_eps, act)
+    k = rms_norm(k, layer["k_norm"], cfg.rms_eps, act)
+    o = np.zeros((B, W), np.float32)
+    for b in range(B):
+        p = int(positions[b])
+        qb = rope(q[b].reshape(1, Hh, D), [p], cfg.rope_theta, act)
+        kb = rope(k[b].reshape(1, Hh, D), [p], cfg.rope_theta, act)
+        k_caches[b][:, p] = round_f16(kb[0])
+        v_caches[b][:, p] = round_f16(v[b].reshape(Hh, D))
+        o[b] = sdpa(qb, k_caches[b][:, :p + 1], v_caches[b][:, :p + 1], cfg.attn_scale, act,
+                    fast=fast).reshape(-1)
+    h = to_act(f32(h) + affine_qmm(o, *layer["o"], act), act)
+    post = rms_norm(h, layer["post_norm"], cfg.rms_eps, act)
+    out, _ = moe_block(post, h, ("affine",) + tuple(layer["router"]), layer["experts"], cfg.top_k, act)
+    return out
 
 
 def layer_forward(h, layer, cfg, k_cache, v_cache, positions):

@@ -1,0 +1,100 @@
+"""End-to-end parity of the device-resident model and session (C ABI
+tf_model_* / tf_session_*) against the oracle's model_forward, on a small
+random-init OLMoE, plus the session's admission / cancellation rules."""
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from tests.gpu_util import host
+from tests.parity import assert_close
+
+pytestmark = pytest.mark.gpu
+
+
+def tiny_cfg(act=torch.float16):
+    from trifuse_b200.model import Config
+    return Config(layers=2, hidden=256, heads=2, kv_heads=2, head_dim=128, intermediate=128, vocab=512,
+                  experts=8, top_k=2, capacity=64, act=act)
+
+
+def oracle_weights(w, cfg):
+    n = lambda k: host(w[k])  # noqa: E731
+    aff = lambda p: (n(p + ".weight"), n(p + ".scales").astype(np.float16), n(p + ".biases").astype(np.float16))  # noqa: E731
+    layers = []
+    for l in range(cfg.layers):
+        p = f"model.layers.{l}."
+        layers.append(dict(
+            input_norm=n(p + "input_layernorm.weight"), post_norm=n(p + "post_attention_layernorm.weight"),
+            q_norm=n(p + "self_attn.q_norm.weight"), k_norm=n(p + "self_attn.k_norm.weight"),
+            q=aff(p + "self_attn.q_proj"), k=aff(p + "self_attn.k_proj"), v=aff(p + "self_attn.v_proj"),
+            o=aff(p + "self_attn.o_proj"), router=aff(p + "mlp.gate"),
+            experts={e: aff(p + f"mlp.switch_mlp.{e}_proj") for e in ("gate", "up", "down")}))
+    return dict(embed=aff("model.embed_tokens"), lm_head=aff("lm_head"), final_norm=n("model.norm.weight"),
+                layers=layers)
+
+
+@pytest.fixture(scope="module")
+def tiny():
+    from trifuse_b200.model import Model, Session
+    from trifuse_b200.quant import synthetic_olmoe
+    cfg = tiny_cfg()
+    w = synthetic_olmoe(cfg, seed=7, device="cuda")
+    model = Model(cfg, w)
+    sess = Session(model, max_batch=2, capacity=64, max_prefill_tokens=32)
+    ocfg = oracle.OLMoEConfig(layers=cfg.layers, hidden=cfg.hidden, heads=cfg.heads, head_dim=cfg.head_dim,
+                              intermediate=cfg.intermediate, vocab=cfg.vocab, experts=cfg.experts,
+                              top_k=cfg.top_k, capacity=64, act="f16")
+    yield cfg, model, sess, oracle_weights(w, cfg), ocfg
+    sess.close()
+    model.close()
+
+
+def test_prefill_then_decode_matches_oracle(tiny):
+    cfg, model, sess, ow, ocfg = tiny
+    sess.reset()
+    rng = np.random.default_rng(0)
+    prompts = [rng.integers(0, cfg.vocab, size=5), rng.integers(0, cfg.vocab, size=9)]
+    caches = [([np.zeros((cfg.heads, 64, cfg.head_dim), np.float32) for _ in range(cfg.layers)],
+               [np.zeros((cfg.heads, 64, cfg.head_dim), np.float32) for _ in range(cfg.layers)])
+              for _ in range(2)]
+    logits = host(sess.prefill([0, 1], prompts))
+    for r in range(2):
+        ref = oracle.model_forward(prompts[r], ow, ocfg, caches[r][0], caches[r][1], 0)
+        assert_close(logits[r], ref)
+    assert sess.lengths(2) == [5, 9]
+    # three decode steps, both requests at once, device-side token ids
+    for step in range(3):
+        toks = rng.integers(0, cfg.vocab, size=2)
+        lg = host(sess.decode(torch.tensor(toks, dtype=torch.int64, device="cuda")))
+        for r in range(2):
+            start = len(prompts[r]) + step
+            ref = oracle.model_forward(toks[r:r + 1], ow, ocfg, caches[r][0], caches[r][1], start)
+            assert_close(lg[r], ref)
+    assert sess.lengths(2) == [8, 12]
+    # host inputs / host output through the same call
+    lg = sess.decode(torch.tensor([1, 2], dtype=torch.int64))
+    assert lg.device.type == "cpu" and lg.shape == (2, cfg.vocab)
+
+
+def test_session_admission_rules(tiny):
+    from trifuse_b200 import TriFuseError
+    cfg, model, sess, ow, ocfg = tiny
+    sess.reset()
+    sess.set_lengths([3, 3])
+    ids = torch.tensor([1, 2], dtype=torch.int64, device="cuda")
+    with pytest.raises(ValueError, match="invalid absolute position"):
+        sess.decode(ids, positions=[3, 4])
+    assert sess.lengths(2) == [3, 3]
+    sess.set_lengths([64, 3])
+    with pytest.raises(TriFuseError, match="CAPACITY"):
+        sess.decode(ids)
+    sess.set_lengths([3, 3])
+    sess.cancel()
+    with pytest.raises(TriFuseError, match="CANCELLED"):
+        sess.decode(ids)
+    assert sess.lengths(2) == [3, 3]
+    sess.reset()
+    assert sess.lengths(2) == [0, 0]
+    out = sess.decode(ids)
+    assert torch.isfinite(out).all()

@@ -1,0 +1,57 @@
+// Weighted top-k combine + residual.
+//
+// Restates MLXNativeGraniteMoEPrefill.h:688-695 (out[inverse], multiply by the
+// gates and sum over k, each in the activation dtype) and the layer residual
+// (tools/export/export_native_olmoe_target.py:218, 227):
+//   out = act(residual + act(sum_k act(y_k * g_k)))
+// with the fp32 sum taken in k order starting from the k = 0 product
+// (bit-identical to oracle/olmoe.py: combine).
+#include "common.cuh"
+#include "internal.h"
+
+namespace tf {
+
+template <typename T>
+__global__ void __launch_bounds__(256)
+    combine_kernel(const T* __restrict__ y, const int32_t* __restrict__ inverse,
+                   const T* __restrict__ gates, const T* __restrict__ residual, int K, int H,
+                   T* __restrict__ out) {
+  const int64_t t = blockIdx.y;
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;  // 8-element chunk
+  if (8 * c >= H) return;
+  float acc[8];
+  for (int k = 0; k < K; ++k) {
+    const int64_t slot = inverse[t * K + k];
+    const float g = to_f(gates[t * K + k]);
+    float v[8];
+    unpack8<T>(ld_v4(y + slot * H + 8 * c), v);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float pr = round_act<T>(__fmul_rn(v[i], g));
+      acc[i] = k == 0 ? pr : __fadd_rn(acc[i], pr);
+    }
+  }
+  float r[8];
+  unpack8<T>(ld_v4(residual + t * H + 8 * c), r);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) acc[i] = __fadd_rn(r[i], round_act<T>(acc[i]));
+  *reinterpret_cast<uint4*>(out + t * H + 8 * c) = pack8<T>(acc);
+}
+
+tf_status launch_combine(const void* y_sorted, const int32_t* inverse, const void* gates,
+                         const void* residual, int64_t tokens, int k, int hidden, int act,
+                         void* out, cudaStream_t s) {
+  if (tokens == 0) return TF_OK;
+  dim3 grid((hidden / 8 + 255) / 256, (unsigned)tokens);
+  if (act == TF_DTYPE_F16)
+    combine_kernel<__half><<<grid, 256, 0, s>>>((const __half*)y_sorted, inverse,
+                                                (const __half*)gates, (const __half*)residual, k,
+                                                hidden, (__half*)out);
+  else
+    combine_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>(
+        (const __nv_bfloat16*)y_sorted, inverse, (const __nv_bfloat16*)gates,
+        (const __nv_bfloat16*)residual, k, hidden, (__nv_bfloat16*)out);
+  return check_launch("combine");
+}
+
+}  // namespace tf

@@ -1,0 +1,171 @@
+// Host-side launcher interface shared by the C ABI (capi.cu), the model
+// (model.cu) and the kernel translation units.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#include <string>
+
+#include "../../include/trifuse_b200.h"
+
+namespace tf {
+
+// ---------------------------------------------------------------- errors
+tf_status set_error(tf_status status, const char* fmt, ...);
+void clear_error();
+tf_status check_launch(const char* what);
+
+#define TF_TRY(expr)                          \
+  do {                                        \
+    tf_status _s = (expr);                    \
+    if (_s != TF_OK) return _s;               \
+  } while (0)
+
+#define TF_CUDA(expr)                                                          \
+  do {                                                                         \
+    cudaError_t _e = (expr);                                                   \
+    if (_e != cudaSuccess)                                                     \
+      return ::tf::set_error(TF_ERR_CUDA, "%s: %s", #expr, cudaGetErrorString(_e)); \
+  } while (0)
+
+inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+// ---------------------------------------------------------------- tracing
+// Phases of one forward; a session with profiling on records a CUDA event
+// pair around each phase on the launching stream.
+enum Phase {
+  PH_EMBED = 0, PH_INPUT_NORM, PH_QKV, PH_ATTENTION, PH_O_PROJ, PH_POST_NORM, PH_ROUTER, PH_SORT,
+  PH_GATE_UP, PH_DOWN, PH_COMBINE, PH_FINAL_NORM, PH_LM_HEAD, PH_COUNT
+};
+extern const char* const kPhaseNames[PH_COUNT];
+struct Tracer {
+  virtual void mark(int phase, bool begin, cudaStream_t s) = 0;
+  virtual ~Tracer() = default;
+};
+// Tracer of the current call on this thread (nullptr = off).
+extern thread_local Tracer* g_tracer;
+inline void trace(int phase, bool begin, cudaStream_t s) {
+  if (g_tracer) g_tracer->mark(phase, begin, s);
+}
+// Kernels launched by this library since load (all threads).
+void count_launch();
+
+// Bump allocator over a caller-provided workspace.
+struct Carve {
+  char* base;
+  size_t cap;
+  size_t used = 0;
+  Carve(void* b, size_t c) : base(static_cast<char*>(b)), cap(c) {}
+  template <typename P>
+  P* take(size_t bytes) {
+    used = align_up(used, 256);
+    P* p = reinterpret_cast<P*>(base ? base + used : nullptr);
+    used += bytes;
+    return p;
+  }
+  bool ok() const { return used <= cap; }
+};
+
+inline int act_bytes(int dtype) { return dtype == TF_DTYPE_F32 ? 4 : 2; }
+inline bool act_ok(int dtype) { return dtype == TF_DTYPE_F16 || dtype == TF_DTYPE_BF16; }
+
+// ---------------------------------------------------------------- norm
+tf_status launch_rms_norm(const void* x, int64_t rows, int width, const void* w, float eps,
+                          int act, void* y, cudaStream_t s);
+tf_status launch_embedding(const int64_t* ids, int64_t n, const tf_affine_weight& t, int out,
+                           void* y, cudaStream_t s);
+
+// ---------------------------------------------------------------- router
+tf_status launch_router(const void* x, int64_t tokens, int hidden, const tf_router_weight& r,
+                        int experts, int k, int act, void* logits, int32_t* idx, void* gates,
+                        cudaStream_t s);
+tf_status launch_route(const void* logits, int64_t tokens, int experts, int k, int act,
+                       void* probs, int32_t* idx, void* gates, cudaStream_t s);
+tf_status launch_topk(const void* probs, int64_t rows, int experts, int k, int act,
+                      int32_t* idx, cudaStream_t s);
+tf_status launch_take_along(const void* x, int64_t rows, int width, const int32_t* idx, int k,
+                            int act, void* out, cudaStream_t s);
+
+// Stable counting sort of n expert ids.  Outputs order/inverse [n],
+// offsets [E+1], active [E] (ids of experts with routes, ascending) and
+// active_count [1].  Workspace from sort_workspace_bytes.
+size_t sort_workspace_bytes(int64_t n, int experts);
+tf_status launch_route_sort(const int32_t* ids, int64_t n, int experts, int32_t* order,
+                            int32_t* inverse, int32_t* offsets, int32_t* active,
+                            int32_t* active_count, void* ws, size_t ws_bytes, cudaStream_t s);
+// dst[i] = src[perm[i]] / div
+tf_status launch_gather_index(const int32_t* src, const int32_t* perm, int64_t n, int div,
+                              int32_t* dst, cudaStream_t s);
+
+// ---------------------------------------------------------------- 4-bit QMM
+enum QmmMode { QMM_DENSE = 0, QMM_GROUPED = 1, QMM_PER_ROUTE = 2 };
+// EPI_F32: y is float and holds the act-rounded result (fp32 logits).
+enum QmmEpilogue { EPI_PLAIN = 0, EPI_SWIGLU = 1, EPI_RESIDUAL = 2, EPI_F32 = 3 };
+
+struct QmmProblem {
+  int mode = QMM_DENSE;
+  int epilogue = EPI_PLAIN;
+  int act = TF_DTYPE_F16;
+  // input rows: slot n reads x row  x_index ? x_index[n] / x_div : n / rows_per_x
+  const void* x = nullptr;
+  int64_t x_stride = 0;
+  const int32_t* x_index = nullptr;
+  int x_div = 1;
+  int rows_per_x = 1;
+  int64_t n = 0;  // slots (output rows)
+  // QMM_PER_ROUTE: expert of slot n; QMM_GROUPED: offsets/active/active_count
+  const int32_t* indices = nullptr;
+  const int32_t* offsets = nullptr;
+  const int32_t* active = nullptr;
+  const int32_t* active_count = nullptr;
+  // weights: w0 (and w1 = up projection for EPI_SWIGLU, w0 = gate)
+  tf_affine_weight w0{};
+  tf_affine_weight w1{};
+  // output
+  void* y = nullptr;
+  int64_t y_stride = 0;
+  const void* residual = nullptr;  // EPI_RESIDUAL, indexed like y
+  int64_t residual_stride = 0;
+};
+tf_status launch_qmm(const QmmProblem& p, cudaStream_t s);
+
+// ---------------------------------------------------------------- combine
+tf_status launch_combine(const void* y_sorted, const int32_t* inverse, const void* gates,
+                         const void* residual, int64_t tokens, int k, int hidden, int act,
+                         void* out, cudaStream_t s);
+
+// ---------------------------------------------------------------- MoE block
+size_t moe_workspace_bytes(const tf_moe_args* a);
+// Runs the block on a workspace of at least moe_workspace_bytes(a).
+tf_status moe_run(const tf_moe_args* a, void* ws, size_t ws_bytes, cudaStream_t s);
+
+// ---------------------------------------------------------------- attention
+// Row r (one query token) of request req[r] (r when req == NULL) at absolute
+// position pos[r]: append its k/v at slot pos[r], attend slots 0..pos[r].
+struct AttnProblem {
+  const void* qkv = nullptr;  // act [rows][3 * heads * head_dim]
+  int64_t rows = 0;
+  int heads = 0;
+  int head_dim = 0;
+  const void* q_norm = nullptr;  // f16 [heads * head_dim]
+  const void* k_norm = nullptr;
+  float eps = 1e-5f;
+  float theta = 10000.f;
+  const int32_t* pos = nullptr;  // device [rows]
+  const int32_t* req = nullptr;  // device [rows] or NULL
+  int max_len = 0;               // >= pos[r] + 1 for every row (host bound)
+  void* k_cache = nullptr;       // f16 [requests][heads][capacity][head_dim]
+  void* v_cache = nullptr;
+  int capacity = 0;
+  float scale = 1.f;
+  int act = TF_DTYPE_F16;
+  void* out = nullptr;  // act [rows][heads * head_dim]
+  void* ws = nullptr;
+  size_t ws_bytes = 0;
+};
+size_t attention_ws_bytes(int64_t rows, int heads, int capacity, int act);
+tf_status launch_attention(const AttnProblem& a, cudaStream_t s);
+
+}  // namespace tf

@@ -1,0 +1,680 @@
+// Device-resident OLMoE model and the per-request session (KV cache +
+// scratch) driving the decode / prefill forward.
+//
+// Restates NativeGraniteMoEPrefill (MLXNativeGraniteMoEPrefill.h:155-493) for
+// architecture OLMoE: the constructor's name binding and geometry checks
+// (157-330) become tf_model_create / tf_model_bind / tf_model_finalize, and
+// run() (347-493) becomes forward_rows(): embedding -> L x (input RMSNorm,
+// fused q|k|v QMM, attention, o-proj + residual, post RMSNorm, MoE block) ->
+// final RMSNorm of each request's last row -> lm_head (fp32 logits).
+//
+// Layout in HBM: all weights live in one arena.  The q, k and v projections
+// of a layer are stored back to back as one [3W][H] packed matrix so the three
+// projections are one launch.  KV caches are f16
+// [max_batch][kv_heads][capacity][head_dim] per layer (BHSD, as the
+// reference's Pool, patches/executorch.patch:1834-2094).
+#include <atomic>
+#include <map>
+#include <string>
+#include <vector>
+
+#include "common.cuh"
+#include "internal.h"
+
+using namespace tf;
+
+namespace {
+
+struct Role {
+  char* ptr = nullptr;
+  size_t bytes = 0;
+  bool bound = false;
+};
+
+struct LayerW {
+  const __half* input_norm;
+  const __half* post_norm;
+  const __half* q_norm;
+  const __half* k_norm;
+  tf_affine_weight qkv;
+  tf_affine_weight o;
+  tf_affine_weight router;
+  tf_affine_weight gate, up, down;
+};
+
+tf_affine_weight affine(char* q, char* s, char* b, int experts, int out, int in) {
+  tf_affine_weight w;
+  w.q = reinterpret_cast<const uint32_t*>(q);
+  w.scales = s;
+  w.biases = b;
+  w.experts = experts;
+  w.out_features = out;
+  w.in_features = in;
+  w.group_size = 64;
+  w.bits = 4;
+  return w;
+}
+
+}  // namespace
+
+struct tf_model {
+  tf_olmoe_config c{};
+  int device = 0;
+  char* arena = nullptr;
+  size_t arena_bytes = 0;
+  std::map<std::string, Role> roles;
+  tf_affine_weight embed{}, lm_head{};
+  const __half* final_norm = nullptr;
+  std::vector<LayerW> layers;
+  bool finalized = false;
+  int sessions = 0;
+};
+
+namespace {
+
+// Event-pair recorder behind tf_session_trace.
+struct SessionTracer : Tracer {
+  struct Pair {
+    int phase;
+    cudaEvent_t a, b;
+  };
+  std::vector<cudaEvent_t> pool;
+  std::vector<Pair> pairs;
+  int open_phase = -1;
+  cudaEvent_t open_ev = nullptr;
+  cudaEvent_t get() {
+    if (!pool.empty()) {
+      cudaEvent_t e = pool.back();
+      pool.pop_back();
+      return e;
+    }
+    cudaEvent_t e = nullptr;
+    cudaEventCreate(&e);
+    return e;
+  }
+  void mark(int phase, bool begin, cudaStream_t s) override {
+    if (begin) {
+      open_phase = phase;
+      open_ev = get();
+      cudaEventRecord(open_ev, s);
+    } else if (open_phase == phase) {
+      cudaEvent_t e = get();
+      cudaEventRecord(e, s);
+      pairs.push_back({phase, open_ev, e});
+      open_phase = -1;
+    }
+  }
+  void recycle() {
+    for (auto& p : pairs) {
+      pool.push_back(p.a);
+      pool.push_back(p.b);
+    }
+    pairs.clear();
+  }
+  ~SessionTracer() override {
+    recycle();
+    for (auto e : pool) cudaEventDestroy(e);
+  }
+};
+
+struct TraceScope {
+  explicit TraceScope(Tracer* t) { g_tracer = t; }
+  ~TraceScope() { g_tracer = nullptr; }
+};
+
+}  // namespace
+
+struct tf_session {
+  tf_model* m = nullptr;
+  int max_batch = 0;
+  int capacity = 0;
+  int max_rows = 0;
+  char* kv = nullptr;
+  std::vector<void*> k, v;
+  std::vector<int32_t> lengths;
+  char* scratch = nullptr;
+  void* h0 = nullptr;
+  void* h1 = nullptr;
+  void* xn = nullptr;
+  void* qkv = nullptr;
+  void* attn = nullptr;
+  int64_t* ids = nullptr;
+  int32_t* pos = nullptr;
+  int32_t* req = nullptr;
+  int32_t* last_rows = nullptr;
+  float* logits = nullptr;  // [max_batch][vocab]
+  void* attn_ws = nullptr;
+  size_t attn_ws_bytes = 0;
+  void* moe_ws = nullptr;
+  size_t moe_ws_bytes = 0;
+  std::atomic<int> cancelled{0};
+  bool tracing = false;
+  SessionTracer tracer;
+};
+
+namespace {
+
+// Scoped device switch.
+struct DeviceGuard {
+  int prev = -1;
+  explicit DeviceGuard(int d) {
+    cudaGetDevice(&prev);
+    if (prev != d) cudaSetDevice(d);
+  }
+  ~DeviceGuard() {
+    if (prev >= 0) cudaSetDevice(prev);
+  }
+};
+
+tf_status validate_config(const tf_olmoe_config* c) {
+  // NativeGraniteMoEPrefill::validate_config (MLXNativeGraniteMoEPrefill.h:306-330).
+  if (!c) return set_error(TF_ERR_INVALID_ARGUMENT, "config is NULL");
+  const int32_t vals[] = {c->layers, c->hidden, c->heads, c->kv_heads, c->head_dim, c->intermediate,
+                          c->vocab, c->experts, c->top_k, c->capacity};
+  for (int32_t v : vals)
+    if (v <= 0) return set_error(TF_ERR_SHAPE, "invalid model geometry");
+  if (c->heads % c->kv_heads || c->head_dim % 2 || (int64_t)c->heads * c->head_dim != c->hidden ||
+      c->top_k > c->experts || c->hidden % 64 || c->intermediate % 64 ||
+      (int64_t)c->capacity * c->top_k > INT32_MAX)
+    return set_error(TF_ERR_SHAPE, "unsupported attention/expert geometry");
+  if (!(c->rms_eps > 0) || !(c->rope_theta > 1))
+    return set_error(TF_ERR_INVALID_ARGUMENT, "invalid normalization/RoPE configuration");
+  if (c->kv_heads != c->heads)
+    return set_error(TF_ERR_UNSUPPORTED, "grouped-query attention is not on this path (kv_heads %d != heads %d)",
+                     c->kv_heads, c->heads);
+  if (c->head_dim != 128) return set_error(TF_ERR_UNSUPPORTED, "head_dim %d (only 128)", c->head_dim);
+  if (c->hidden % 256 || c->hidden > 4096) return set_error(TF_ERR_UNSUPPORTED, "hidden %d", c->hidden);
+  if (c->experts > 64 || c->top_k > 32) return set_error(TF_ERR_UNSUPPORTED, "experts <= 64, top_k <= 32");
+  if (!act_ok(c->act)) return set_error(TF_ERR_INVALID_ARGUMENT, "activation dtype must be f16 or bf16");
+  return TF_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int tf_model_create(const tf_olmoe_config* config, int device, tf_model** model) {
+  if (!model) return set_error(TF_ERR_INVALID_ARGUMENT, "model out-pointer is NULL");
+  *model = nullptr;
+  TF_TRY(validate_config(config));
+  const tf_olmoe_config& c = *config;
+  auto* m = new tf_model();
+  m->c = c;
+  m->device = device;
+  const int H = c.hidden, W = c.heads * c.head_dim, Wkv = c.kv_heads * c.head_dim, E = c.experts,
+            I = c.intermediate, V = c.vocab;
+  // Role table: (name, bytes) in arena order.  q/k/v parts of one layer are
+  // adjacent so that they form one [W + 2 Wkv][H] packed matrix.
+  std::vector<std::pair<std::string, size_t>> order;
+  auto add_affine = [&](const std::string& name, int64_t rows, int64_t in) {
+    order.push_back({name + ".weight", (size_t)rows * in / 2});
+  };
+  auto add_sb = [&](const std::string& name, int64_t rows, int64_t in) {
+    order.push_back({name + ".scales", (size_t)rows * (in / 64) * 2});
+    order.push_back({name + ".biases", (size_t)rows * (in / 64) * 2});
+  };
+  add_affine("model.embed_tokens", V, H);
+  add_sb("model.embed_tokens", V, H);
+  add_affine("lm_head", V, H);
+  add_sb("lm_head", V, H);
+  order.push_back({"model.norm.weight", (size_t)H * 2});
+  for (int l = 0; l < c.layers; ++l) {
+    const std::string p = "model.layers." + std::to_string(l) + ".";
+    order.push_back({p + "input_layernorm.weight", (size_t)H * 2});
+    order.push_back({p + "post_attention_layernorm.weight", (size_t)H * 2});
+    order.push_back({p + "self_attn.q_norm.weight", (size_t)W * 2});
+    order.push_back({p + "self_attn.k_norm.weight", (size_t)Wkv * 2});
+    add_affine(p + "self_attn.q_proj", W, H);
+    add_affine(p + "self_attn.k_proj", Wkv, H);
+    add_affine(p + "self_attn.v_proj", Wkv, H);
+    order.push_back({p + "self_attn.q_proj.scales", (size_t)W * (H / 64) * 2});
+    order.push_back({p + "self_attn.k_proj.scales", (size_t)Wkv * (H / 64) * 2});
+    order.push_back({p + "self_attn.v_proj.scales", (size_t)Wkv * (H / 64) * 2});
+    order.push_back({p + "self_attn.q_proj.biases", (size_t)W * (H / 64) * 2});
+    order.push_back({p + "self_attn.k_proj.biases", (size_t)Wkv * (H / 64) * 2});
+    order.push_back({p + "self_attn.v_proj.biases", (size_t)Wkv * (H / 64) * 2});
+    add_affine(p + "self_attn.o_proj", H, W);
+    add_sb(p + "self_attn.o_proj", H, W);
+    add_affine(p + "mlp.gate", E, H);
+    add_sb(p + "mlp.gate", E, H);
+    for (const char* n : {"gate_proj", "up_proj"}) {
+      add_affine(p + "mlp.switch_mlp." + n, (int64_t)E * I, H);
+      add_sb(p + "mlp.switch_mlp." + n, (int64_t)E * I, H);
+    }
+    add_affine(p + "mlp.switch_mlp.down_proj", (int64_t)E * H, I);
+    add_sb(p + "mlp.switch_mlp.down_proj", (int64_t)E * H, I);
+  }
+  // q|k|v parts must be contiguous: no padding between them.
+  size_t total = 0;
+  std::vector<size_t> offs;
+  for (size_t i = 0; i < order.size(); ++i) {
+    const std::string& n = order[i].first;
+    const bool packed_part = n.find("self_attn.k_proj") != std::string::npos ||
+                             n.find("self_attn.v_proj") != std::string::npos;
+    if (!packed_part) total = align_up(total, 256);
+    offs.push_back(total);
+    total += order[i].second;
+  }
+  total = align_up(total, 256);
+  {
+    DeviceGuard g(device);
+    const cudaError_t e = cudaMalloc(&m->arena, total);
+    if (e != cudaSuccess) {
+      delete m;
+      return set_error(TF_ERR_OUT_OF_MEMORY, "model arena of %zu bytes: %s", total, cudaGetErrorString(e));
+    }
+  }
+  m->arena_bytes = total;
+  for (size_t i = 0; i < order.size(); ++i) m->roles[order[i].first] = Role{m->arena + offs[i], order[i].second, false};
+  auto R = [&](const std::string& n) { return m->roles.at(n).ptr; };
+  m->embed = affine(R("model.embed_tokens.weight"), R("model.embed_tokens.scales"),
+                    R("model.embed_tokens.biases"), 0, V, H);
+  m->lm_head = affine(R("lm_head.weight"), R("lm_head.scales"), R("lm_head.biases"), 0, V, H);
+  m->final_norm = (const __half*)R("model.norm.weight");
+  for (int l = 0; l < c.layers; ++l) {
+    const std::string p = "model.layers." + std::to_string(l) + ".";
+    LayerW L;
+    L.input_norm = (const __half*)R(p + "input_layernorm.weight");
+    L.post_norm = (const __half*)R(p + "post_attention_layernorm.weight");
+    L.q_norm = (const __half*)R(p + "self_attn.q_norm.weight");
+    L.k_norm = (const __half*)R(p + "self_attn.k_norm.weight");
+    L.qkv = affine(R(p + "self_attn.q_proj.weight"), R(p + "self_attn.q_proj.scales"),
+                   R(p + "self_attn.q_proj.biases"), 0, W + 2 * Wkv, H);
+    L.o = affine(R(p + "self_attn.o_proj.weight"), R(p + "self_attn.o_proj.scales"),
+                 R(p + "self_attn.o_proj.biases"), 0, H, W);
+    L.router = affine(R(p + "mlp.gate.weight"), R(p + "mlp.gate.scales"), R(p + "mlp.gate.biases"), 0, E, H);
+    const std::string s = p + "mlp.switch_mlp.";
+    L.gate = affine(R(s + "gate_proj.weight"), R(s + "gate_proj.scales"), R(s + "gate_proj.biases"), E, I, H);
+    L.up = affine(R(s + "up_proj.weight"), R(s + "up_proj.scales"), R(s + "up_proj.biases"), E, I, H);
+    L.down = affine(R(s + "down_proj.weight"), R(s + "down_proj.scales"), R(s + "down_proj.biases"), E, H, I);
+    m->layers.push_back(L);
+  }
+  *model = m;
+  return TF_OK;
+}
+
+int tf_model_bind(tf_model* model, const char* name, const void* data, size_t bytes, int data_on_device) {
+  if (!model || !name || !data) return set_error(TF_ERR_INVALID_ARGUMENT, "bind: NULL argument");
+  if (model->finalized) return set_error(TF_ERR_STATE, "bind: model already finalized");
+  auto it = model->roles.find(name);
+  if (it == model->roles.end())
+    return set_error(TF_ERR_INVALID_ARGUMENT, "unexpected constant/unsupported model structure: %s", name);
+  Role& r = it->second;
+  if (r.bound) return set_error(TF_ERR_STATE, "missing/aliased parameter role: %s bound twice", name);
+  if (bytes != r.bytes)
+    return set_error(TF_ERR_SHAPE, "packed parameter geometry differs: %s has %zu bytes, expected %zu", name,
+                     bytes, r.bytes);
+  DeviceGuard g(model->device);
+  TF_CUDA(cudaMemcpy(r.ptr, data, bytes, data_on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice));
+  r.bound = true;
+  return TF_OK;
+}
+
+int tf_model_finalize(tf_model* model) {
+  if (!model) return set_error(TF_ERR_INVALID_ARGUMENT, "model is NULL");
+  for (const auto& kv : model->roles)
+    if (!kv.second.bound) return set_error(TF_ERR_STATE, "missing parameter role: %s", kv.first.c_str());
+  model->finalized = true;
+  return TF_OK;
+}
+
+int tf_model_destroy(tf_model* model) {
+  if (!model) return TF_OK;
+  if (model->sessions > 0) return set_error(TF_ERR_STATE, "model still has %d sessions", model->sessions);
+  DeviceGuard g(model->device);
+  cudaFree(model->arena);
+  delete model;
+  return TF_OK;
+}
+
+int tf_session_create(tf_model* model, int32_t max_batch, int32_t capacity, int32_t max_prefill_tokens,
+                      tf_session** session) {
+  if (!session) return set_error(TF_ERR_INVALID_ARGUMENT, "session out-pointer is NULL");
+  *session = nullptr;
+  if (!model || !model->finalized) return set_error(TF_ERR_STATE, "model missing or not finalized");
+  if (max_batch <= 0 || capacity <= 0 || max_prefill_tokens < 0)
+    return set_error(TF_ERR_INVALID_ARGUMENT, "session: bad sizes");
+  const tf_olmoe_config& c = model->c;
+  if (capacity > c.capacity)
+    return set_error(TF_ERR_CAPACITY, "Runtime capacity %d must not extend the model's %d", capacity, c.capacity);
+  auto* s = new tf_session();
+  s->m = model;
+  s->max_batch = max_batch;
+  s->capacity = capacity;
+  s->max_rows = max_batch > max_prefill_tokens ? max_batch : max_prefill_tokens;
+  s->lengths.assign(max_batch, 0);
+  const int H = c.hidden, W = c.heads * c.head_dim, Wkv = c.kv_heads * c.head_dim;
+  const int64_t R = s->max_rows;
+  const size_t per_cache = (size_t)max_batch * c.kv_heads * capacity * c.head_dim * 2;
+  tf_moe_args ma{};
+  ma.tokens = R;
+  ma.hidden = H;
+  ma.intermediate = c.intermediate;
+  ma.experts = c.experts;
+  ma.top_k = c.top_k;
+  ma.act = c.act;
+  s->moe_ws_bytes = moe_workspace_bytes(&ma);
+  s->attn_ws_bytes = attention_ws_bytes(R, c.heads, capacity, c.act);
+  Carve cv(nullptr, 0);
+  auto plan = [&](Carve& k) {
+    s->h0 = k.take<char>((size_t)R * H * 2);
+    s->h1 = k.take<char>((size_t)R * H * 2);
+    s->xn = k.take<char>((size_t)R * H * 2);
+    s->qkv = k.take<char>((size_t)R * (W + 2 * Wkv) * 2);
+    s->attn = k.take<char>((size_t)R * W * 2);
+    s->ids = k.take<int64_t>((size_t)R * 8);
+    s->pos = k.take<int32_t>((size_t)R * 4);
+    s->req = k.take<int32_t>((size_t)R * 4);
+    s->last_rows = k.take<int32_t>((size_t)max_batch * 4);
+    s->logits = k.take<float>((size_t)max_batch * c.vocab * 4);
+    s->attn_ws = k.take<char>(s->attn_ws_bytes);
+    s->moe_ws = k.take<char>(s->moe_ws_bytes);
+  };
+  plan(cv);
+  DeviceGuard g(model->device);
+  cudaError_t e = cudaMalloc(&s->kv, per_cache * 2 * c.layers);
+  if (e != cudaSuccess) {
+    delete s;
+    return set_error(TF_ERR_OUT_OF_MEMORY, "KV cache of %zu bytes: %s", per_cache * 2 * c.layers,
+                     cudaGetErrorString(e));
+  }
+  e = cudaMalloc(&s->scratch, cv.used);
+  if (e != cudaSuccess) {
+    cudaFree(s->kv);
+    delete s;
+    return set_error(TF_ERR_OUT_OF_MEMORY, "session scratch of %zu bytes: %s", cv.used, cudaGetErrorString(e));
+  }
+  Carve real(s->scratch, cv.used);
+  plan(real);
+  for (int l = 0; l < c.layers; ++l) {
+    s->k.push_back(s->kv + per_cache * (2 * l));
+    s->v.push_back(s->kv + per_cache * (2 * l + 1));
+  }
+  model->sessions++;
+  *session = s;
+  return TF_OK;
+}
+
+int tf_session_destroy(tf_session* s) {
+  if (!s) return TF_OK;
+  DeviceGuard g(s->m->device);
+  cudaFree(s->kv);
+  cudaFree(s->scratch);
+  s->m->sessions--;
+  delete s;
+  return TF_OK;
+}
+
+int tf_session_kv(tf_session* s, int32_t layer, void** k_cache, void** v_cache) {
+  if (!s || !k_cache || !v_cache) return set_error(TF_ERR_INVALID_ARGUMENT, "NULL argument");
+  if (layer < 0 || layer >= s->m->c.layers) return set_error(TF_ERR_INVALID_ARGUMENT, "layer out of range");
+  *k_cache = s->k[layer];
+  *v_cache = s->v[layer];
+  return TF_OK;
+}
+
+int tf_session_set_lengths(tf_session* s, const int32_t* lengths, int32_t batch) {
+  if (!s || (!lengths && batch)) return set_error(TF_ERR_INVALID_ARGUMENT, "NULL argument");
+  if (batch < 0 || batch > s->max_batch) return set_error(TF_ERR_INVALID_ARGUMENT, "batch out of range");
+  for (int b = 0; b < batch; ++b)
+    if (lengths[b] < 0 || lengths[b] > s->capacity)
+      return set_error(TF_ERR_CAPACITY, "length %d of request %d outside [0, %d]", lengths[b], b, s->capacity);
+  for (int b = 0; b < batch; ++b) s->lengths[b] = lengths[b];
+  return TF_OK;
+}
+
+int tf_session_get_lengths(tf_session* s, int32_t* lengths, int32_t batch) {
+  if (!s || (!lengths && batch)) return set_error(TF_ERR_INVALID_ARGUMENT, "NULL argument");
+  if (batch < 0 || batch > s->max_batch) return set_error(TF_ERR_INVALID_ARGUMENT, "batch out of range");
+  for (int b = 0; b < batch; ++b) lengths[b] = s->lengths[b];
+  return TF_OK;
+}
+
+int tf_session_cancel(tf_session* s) {
+  if (!s) return set_error(TF_ERR_INVALID_ARGUMENT, "session is NULL");
+  s->cancelled.store(1);
+  return TF_OK;
+}
+
+int tf_session_reset(tf_session* s) {
+  if (!s) return set_error(TF_ERR_INVALID_ARGUMENT, "session is NULL");
+  s->cancelled.store(0);
+  for (auto& l : s->lengths) l = 0;
+  return TF_OK;
+}
+
+}  // extern "C"
+
+namespace {
+
+// Forward `rows` token rows through every layer.  Inputs already on device:
+// s->ids [rows], s->pos [rows], s->req [rows] (or identity when req_ident).
+// Leaves the final hidden states in s->h0.
+tf_status forward_rows(tf_session* s, int64_t rows, bool req_ident, int max_len, cudaStream_t st) {
+  const tf_model* m = s->m;
+  const tf_olmoe_config& c = m->c;
+  const int H = c.hidden, W = c.heads * c.head_dim;
+  const int QKV = W + 2 * c.kv_heads * c.head_dim;
+  trace(PH_EMBED, true, st);
+  TF_TRY(launch_embedding(s->ids, rows, m->embed, c.act, s->h0, st));
+  trace(PH_EMBED, false, st);
+  for (int l = 0; l < c.layers; ++l) {
+    if (s->cancelled.load()) return set_error(TF_ERR_CANCELLED, "cancelled before layer %d", l);
+    const LayerW& L = m->layers[l];
+    trace(PH_INPUT_NORM, true, st);
+    TF_TRY(launch_rms_norm(s->h0, rows, H, L.input_norm, c.rms_eps, c.act, s->xn, st));
+    trace(PH_INPUT_NORM, false, st);
+    QmmProblem q;
+    q.mode = QMM_DENSE;
+    q.act = c.act;
+    q.x = s->xn;
+    q.x_stride = H;
+    q.n = rows;
+    q.w0 = L.qkv;
+    q.y = s->qkv;
+    q.y_stride = QKV;
+    trace(PH_QKV, true, st);
+    TF_TRY(launch_qmm(q, st));
+    trace(PH_QKV, false, st);
+    AttnProblem a;
+    a.qkv = s->qkv;
+    a.rows = rows;
+    a.heads = c.heads;
+    a.head_dim = c.head_dim;
+    a.q_norm = L.q_norm;
+    a.k_norm = L.k_norm;
+    a.eps = c.rms_eps;
+    a.theta = c.rope_theta;
+    a.pos = s->pos;
+    a.req = req_ident ? nullptr : s->req;
+    a.max_len = max_len;
+    a.k_cache = s->k[l];
+    a.v_cache = s->v[l];
+    a.capacity = s->capacity;
+    a.scale = (float)(1.0 / sqrt((double)c.head_dim));
+    a.act = c.act;
+    a.out = s->attn;
+    a.ws = s->attn_ws;
+    a.ws_bytes = s->attn_ws_bytes;
+    trace(PH_ATTENTION, true, st);
+    TF_TRY(launch_attention(a, st));
+    trace(PH_ATTENTION, false, st);
+    QmmProblem o;
+    o.mode = QMM_DENSE;
+    o.epilogue = EPI_RESIDUAL;
+    o.act = c.act;
+    o.x = s->attn;
+    o.x_stride = W;
+    o.n = rows;
+    o.w0 = L.o;
+    o.y = s->h1;
+    o.y_stride = H;
+    o.residual = s->h0;
+    o.residual_stride = H;
+    trace(PH_O_PROJ, true, st);
+    TF_TRY(launch_qmm(o, st));
+    trace(PH_O_PROJ, false, st);
+    trace(PH_POST_NORM, true, st);
+    TF_TRY(launch_rms_norm(s->h1, rows, H, L.post_norm, c.rms_eps, c.act, s->xn, st));
+    trace(PH_POST_NORM, false, st);
+    tf_moe_args ma{};
+    ma.x = s->xn;
+    ma.residual = s->h1;
+    ma.out = s->h0;
+    ma.tokens = rows;
+    ma.hidden = H;
+    ma.intermediate = c.intermediate;
+    ma.experts = c.experts;
+    ma.top_k = c.top_k;
+    ma.act = c.act;
+    ma.router.dense = nullptr;
+    ma.router.affine = L.router;
+    ma.gate_proj = L.gate;
+    ma.up_proj = L.up;
+    ma.down_proj = L.down;
+    TF_TRY(moe_run(&ma, s->moe_ws, s->moe_ws_bytes, st));
+  }
+  return TF_OK;
+}
+
+// Final RMSNorm + lm_head of selected rows -> s->logits [n][vocab].
+tf_status head_rows(tf_session* s, int64_t rows, const int32_t* sel, int64_t n, cudaStream_t st) {
+  const tf_olmoe_config& c = s->m->c;
+  trace(PH_FINAL_NORM, true, st);
+  TF_TRY(launch_rms_norm(s->h0, rows, c.hidden, s->m->final_norm, c.rms_eps, c.act, s->xn, st));
+  trace(PH_FINAL_NORM, false, st);
+  QmmProblem h;
+  h.mode = QMM_DENSE;
+  h.epilogue = EPI_F32;
+  h.act = c.act;
+  h.x = s->xn;
+  h.x_stride = c.hidden;
+  h.x_index = sel;
+  h.n = n;
+  h.w0 = s->m->lm_head;
+  h.y = s->logits;
+  h.y_stride = c.vocab;
+  trace(PH_LM_HEAD, true, st);
+  TF_TRY(launch_qmm(h, st));
+  trace(PH_LM_HEAD, false, st);
+  return TF_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int tf_session_decode(tf_session* s, const int64_t* token_ids, const int32_t* positions, int32_t batch,
+                      float* logits, int flags, void* stream) {
+  if (!s || !token_ids) return set_error(TF_ERR_INVALID_ARGUMENT, "decode: NULL argument");
+  if (batch <= 0 || batch > s->max_batch)
+    return set_error(TF_ERR_INVALID_ARGUMENT, "decode: batch %d outside [1, %d]", batch, s->max_batch);
+  if (s->cancelled.load()) return set_error(TF_ERR_CANCELLED, "session cancelled");
+  const tf_olmoe_config& c = s->m->c;
+  std::vector<int32_t> pos(batch);
+  int max_len = 0;
+  for (int b = 0; b < batch; ++b) {
+    pos[b] = positions ? positions[b] : s->lengths[b];
+    if (pos[b] != s->lengths[b])
+      return set_error(TF_ERR_INVALID_ARGUMENT, "invalid absolute position %d for request %d (length %d)", pos[b],
+                       b, s->lengths[b]);
+    if (pos[b] >= s->capacity) return set_error(TF_ERR_CAPACITY, "absolute capacity exceeded (request %d)", b);
+    if (pos[b] + 1 > max_len) max_len = pos[b] + 1;
+  }
+  DeviceGuard g(s->m->device);
+  TraceScope ts(s->tracing ? &s->tracer : nullptr);
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  TF_CUDA(cudaMemcpyAsync(s->ids, token_ids, (size_t)batch * 8,
+                          (flags & TF_HOST_INPUTS) ? cudaMemcpyHostToDevice : cudaMemcpyDeviceToDevice, st));
+  TF_CUDA(cudaMemcpyAsync(s->pos, pos.data(), (size_t)batch * 4, cudaMemcpyHostToDevice, st));
+  TF_TRY(forward_rows(s, batch, true, max_len, st));
+  if (logits) {
+    TF_TRY(head_rows(s, batch, nullptr, batch, st));
+    TF_CUDA(cudaMemcpyAsync(logits, s->logits, (size_t)batch * c.vocab * 4,
+                            (flags & TF_HOST_OUTPUT) ? cudaMemcpyDeviceToHost : cudaMemcpyDeviceToDevice, st));
+    if (flags & TF_HOST_OUTPUT) TF_CUDA(cudaStreamSynchronize(st));
+  }
+  for (int b = 0; b < batch; ++b) s->lengths[b] += 1;
+  return TF_OK;
+}
+
+int tf_session_prefill(tf_session* s, const int32_t* requests, const int32_t* token_counts, int32_t num_requests,
+                       const int64_t* token_ids, float* last_logits, int flags, void* stream) {
+  if (!s || !requests || !token_counts || !token_ids)
+    return set_error(TF_ERR_INVALID_ARGUMENT, "prefill: NULL argument");
+  if (num_requests <= 0 || num_requests > s->max_batch)
+    return set_error(TF_ERR_INVALID_ARGUMENT, "prefill: %d requests outside [1, %d]", num_requests, s->max_batch);
+  if (s->cancelled.load()) return set_error(TF_ERR_CANCELLED, "session cancelled");
+  const tf_olmoe_config& c = s->m->c;
+  std::vector<int32_t> pos, req, last(num_requests);
+  std::vector<char> seen(s->max_batch, 0);
+  int max_len = 0;
+  for (int i = 0; i < num_requests; ++i) {
+    const int r = requests[i], n = token_counts[i];
+    if (r < 0 || r >= s->max_batch || seen[r])
+      return set_error(TF_ERR_INVALID_ARGUMENT, "prefill: request %d invalid or repeated", r);
+    seen[r] = 1;
+    if (n <= 0) return set_error(TF_ERR_INVALID_ARGUMENT, "prefill: request %d has %d tokens", r, n);
+    const int start = s->lengths[r];
+    if ((int64_t)start + n > s->capacity) return set_error(TF_ERR_CAPACITY, "absolute capacity exceeded");
+    for (int t = 0; t < n; ++t) {
+      pos.push_back(start + t);
+      req.push_back(r);
+    }
+    last[i] = (int32_t)pos.size() - 1;
+    if (start + n > max_len) max_len = start + n;
+  }
+  const int64_t rows = (int64_t)pos.size();
+  if (rows > s->max_rows)
+    return set_error(TF_ERR_CAPACITY, "prefill: %lld rows exceed the session's %d", (long long)rows, s->max_rows);
+  DeviceGuard g(s->m->device);
+  TraceScope ts(s->tracing ? &s->tracer : nullptr);
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  TF_CUDA(cudaMemcpyAsync(s->ids, token_ids, (size_t)rows * 8,
+                          (flags & TF_HOST_INPUTS) ? cudaMemcpyHostToDevice : cudaMemcpyDeviceToDevice, st));
+  TF_CUDA(cudaMemcpyAsync(s->pos, pos.data(), (size_t)rows * 4, cudaMemcpyHostToDevice, st));
+  TF_CUDA(cudaMemcpyAsync(s->req, req.data(), (size_t)rows * 4, cudaMemcpyHostToDevice, st));
+  TF_CUDA(cudaMemcpyAsync(s->last_rows, last.data(), (size_t)num_requests * 4, cudaMemcpyHostToDevice, st));
+  TF_TRY(forward_rows(s, rows, false, max_len, st));
+  if (last_logits) {
+    TF_TRY(head_rows(s, rows, s->last_rows, num_requests, st));
+    TF_CUDA(cudaMemcpyAsync(last_logits, s->logits, (size_t)num_requests * c.vocab * 4,
+                            (flags & TF_HOST_OUTPUT) ? cudaMemcpyDeviceToHost : cudaMemcpyDeviceToDevice, st));
+  }
+  // The host vectors above are pageable; make sure the copies finished.
+  TF_CUDA(cudaStreamSynchronize(st));
+  for (int i = 0; i < num_requests; ++i) s->lengths[requests[i]] += token_counts[i];
+  return TF_OK;
+}
+
+int tf_trace_phases(void) { return PH_COUNT; }
+
+const char* tf_trace_phase_name(int phase) {
+  return (phase >= 0 && phase < PH_COUNT) ? kPhaseNames[phase] : "";
+}
+
+int tf_session_trace(tf_session* s, int enable) {
+  if (!s) return set_error(TF_ERR_INVALID_ARGUMENT, "session is NULL");
+  s->tracing = enable != 0;
+  return TF_OK;
+}
+
+int tf_session_trace_read(tf_session* s, float* total_ms, int32_t* counts) {
+  if (!s || !total_ms || !counts) return set_error(TF_ERR_INVALID_ARGUMENT, "NULL argument");
+  for (int p = 0; p < PH_COUNT; ++p) {
+    total_ms[p] = 0.f;
+    counts[p] = 0;
+  }
+  DeviceGuard g(s->m->device);
+  for (auto& pr : s->tracer.pairs) {
+    TF_CUDA(cudaEventSynchronize(pr.b));
+    float ms = 0.f;
+    TF_CUDA(cudaEventElapsedTime(&ms, pr.a, pr.b));
+    total_ms[pr.phase] += ms;
+    counts[pr.phase] += 1;
+  }
+  s->tracer.recycle();
+  return TF_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,267 @@
+// MLX-affine 4-bit QMM / gather_qmm as a memory-bound warp-per-row GEMV.
+//
+// Restates native_affine_gather_qmm / native_affine_qmm
+// (overlays/executorch/backends/mlx/native_affine_ops.py:39-74) and the
+// adapter's gather_qmm / quantized_matmul calls
+// (MLXNativeGraniteMoEPrefill.h:539-550) for few tokens per weight matrix
+// (decode).  y = act(sum_k x_k (code_k s_g + b_g)) with fp32 accumulation,
+// evaluated per 32-element half-group as s_g * sum(x*code) + b_g * sum(x).
+//
+// Work is a list of (segment, block of 32 output rows) items, grid-strided
+// over a fixed grid so the launch never depends on device-side routing:
+//   DENSE     - one segment (expert 0) holding every slot;
+//   PER_ROUTE - slot n is its own segment with expert indices[n];
+//   GROUPED   - active expert a owns slots offsets[e] .. offsets[e+1] (the
+//               output of the route sort), so an expert's weights are read
+//               once for all of its tokens.
+// Each warp owns 4 rows; lane l owns the 16-byte weight chunks l + 32m of a
+// row (32 codes each) and keeps the matching activations in registers.
+//
+// Nibble decode: for code j (bits 4j) of a word w, j <= 4,
+//   float(0x4B000000 | (w & (0xF << 4j))) - 2^23 == code_j * 16^j  (exact),
+// so the activation is stored pre-multiplied by 16^-j (an exact power of two)
+// and one LOP3 + one FADD + one FFMA handle a code.  Codes 5..7 use w >> 20.
+#include "common.cuh"
+#include "internal.h"
+
+namespace tf {
+
+constexpr int kGemvWarps = 8;
+constexpr int kRowsPerWarp = 4;
+constexpr int kGemvRows = kGemvWarps * kRowsPerWarp;
+
+struct GemvArgs {
+  const void* x;
+  int64_t x_stride;
+  const int32_t* x_index;
+  int x_div;
+  int rows_per_x;
+  int64_t n;
+  const int32_t* indices;
+  const int32_t* offsets;
+  const int32_t* active;
+  const int32_t* active_count;
+  const uint32_t* q0;
+  const __half* s0;
+  const __half* b0;
+  const uint32_t* q1;
+  const __half* s1;
+  const __half* b1;
+  int out;
+  int in;
+  int experts;
+  void* y;
+  int64_t y_stride;
+  const void* residual;
+  int64_t residual_stride;
+};
+
+__device__ __forceinline__ float nib(uint32_t masked) {
+  return __int_as_float(0x4B000000u | masked) - 8388608.0f;
+}
+
+// Dot of one 32-code chunk (uint4) with pre-scaled activations xs[32].
+__device__ __forceinline__ float chunk_dot(const uint4& wv, const float* xs) {
+  const uint32_t words[4] = {wv.x, wv.y, wv.z, wv.w};
+  float p = 0.f;
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const uint32_t w = words[k];
+    const uint32_t h = w >> 20;
+    const float* xk = xs + 8 * k;
+    p = fmaf(xk[0], nib(w & 0xFu), p);
+    p = fmaf(xk[1], nib(w & 0xF0u), p);
+    p = fmaf(xk[2], nib(w & 0xF00u), p);
+    p = fmaf(xk[3], nib(w & 0xF000u), p);
+    p = fmaf(xk[4], nib(w & 0xF0000u), p);
+    p = fmaf(xk[5], nib(h & 0xFu), p);
+    p = fmaf(xk[6], nib(h & 0xF0u), p);
+    p = fmaf(xk[7], nib(h & 0xF00u), p);
+  }
+  return p;
+}
+
+__device__ __forceinline__ float silu_f(float g) { return g / (1.0f + expf(-g)); }
+
+template <typename T, int MODE, int EPI, int TB, int M>
+__global__ void __launch_bounds__(kGemvWarps * 32) qmm_gemv_kernel(GemvArgs a) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int nrb = (a.out + kGemvRows - 1) / kGemvRows;
+  const int nchunk = a.in / 32;
+  int64_t nseg;
+  if (MODE == QMM_DENSE) nseg = 1;
+  else if (MODE == QMM_PER_ROUTE) nseg = a.n;
+  else nseg = *a.active_count;
+  const int64_t items = nseg * nrb;
+  constexpr int NW = EPI == EPI_SWIGLU ? 2 : 1;
+  // Pre-scale factors 16^-j for code position j of a word (j = i % 8).
+  const float pre[8] = {1.f, 1.f / 16, 1.f / 256, 1.f / 4096, 1.f / 65536, 1.f, 1.f / 16, 1.f / 256};
+
+  for (int64_t item = blockIdx.x; item < items; item += gridDim.x) {
+    const int64_t seg = item / nrb;
+    const int rb = (int)(item % nrb);
+    int e;
+    int64_t s0, s1;
+    if (MODE == QMM_DENSE) {
+      e = 0; s0 = 0; s1 = a.n;
+    } else if (MODE == QMM_PER_ROUTE) {
+      e = a.indices[seg]; s0 = seg; s1 = seg + 1;
+    } else {
+      e = a.active[seg]; s0 = a.offsets[e]; s1 = a.offsets[e + 1];
+    }
+    const int row0 = rb * kGemvRows + warp * kRowsPerWarp;
+    for (int64_t tb = s0; tb < s1; tb += TB) {
+      // Activations of up to TB slots, pre-scaled, plus per-chunk sums.
+      float xs[TB][M][32];
+      float xsum[TB][M];
+#pragma unroll
+      for (int tt = 0; tt < TB; ++tt) {
+        const int64_t slot = tb + tt;
+#pragma unroll
+        for (int m = 0; m < M; ++m) {
+          xsum[tt][m] = 0.f;
+          const int c = lane + 32 * m;
+          if (slot < s1 && c < nchunk) {
+            const int64_t xr = a.x_index ? a.x_index[slot] / a.x_div : slot / a.rows_per_x;
+            const T* xp = (const T*)a.x + xr * a.x_stride + 32 * c;
+#pragma unroll
+            for (int v = 0; v < 4; ++v) {
+              float f[8];
+              unpack8<T>(ld_v4(xp + 8 * v), f);
+#pragma unroll
+              for (int i = 0; i < 8; ++i) {
+                xsum[tt][m] += f[i];
+                xs[tt][m][8 * v + i] = f[i] * pre[i];
+              }
+            }
+          } else {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) xs[tt][m][i] = 0.f;
+          }
+        }
+      }
+#pragma unroll
+      for (int r = 0; r < kRowsPerWarp; ++r) {
+        const int row = row0 + r;
+        if (row >= a.out) break;
+        float acc[NW][TB];
+#pragma unroll
+        for (int w = 0; w < NW; ++w) {
+          const uint32_t* q = w == 0 ? a.q0 : a.q1;
+          const __half* sc = w == 0 ? a.s0 : a.s1;
+          const __half* bi = w == 0 ? a.b0 : a.b1;
+          const int64_t wrow = (int64_t)e * a.out + row;
+          const uint32_t* qrow = q + wrow * (a.in / 8);
+#pragma unroll
+          for (int tt = 0; tt < TB; ++tt) acc[w][tt] = 0.f;
+          uint4 wv[M];
+#pragma unroll
+          for (int m = 0; m < M; ++m) {
+            const int c = lane + 32 * m;
+            wv[m] = c < nchunk ? ld_stream_v4(qrow + 4 * c) : make_uint4(0, 0, 0, 0);
+          }
+#pragma unroll
+          for (int m = 0; m < M; ++m) {
+            const int c = lane + 32 * m;
+            if (c < nchunk) {
+              const float s = __half2float(sc[wrow * (a.in / 64) + c / 2]);
+              const float b = __half2float(bi[wrow * (a.in / 64) + c / 2]);
+#pragma unroll
+              for (int tt = 0; tt < TB; ++tt)
+                acc[w][tt] = fmaf(s, chunk_dot(wv[m], xs[tt][m]), fmaf(b, xsum[tt][m], acc[w][tt]));
+            }
+          }
+#pragma unroll
+          for (int tt = 0; tt < TB; ++tt) acc[w][tt] = warp_sum_butterfly(acc[w][tt]);
+        }
+#pragma unroll
+        for (int tt = 0; tt < TB; ++tt) {
+          const int64_t slot = tb + tt;
+          if (lane == tt && slot < s1) {
+            T* yp = (T*)a.y + slot * a.y_stride + row;  // unused for EPI_F32
+            if (EPI == EPI_SWIGLU) {
+              const float g = round_act<T>(acc[0][tt]);
+              const float u = round_act<T>(acc[NW - 1][tt]);
+              *yp = from_f<T>(round_act<T>(silu_f(g)) * u);
+            } else if (EPI == EPI_F32) {
+              ((float*)a.y)[slot * a.y_stride + row] = round_act<T>(acc[0][tt]);
+            } else if (EPI == EPI_RESIDUAL) {
+              const float res = to_f(((const T*)a.residual)[slot * a.residual_stride + row]);
+              *yp = from_f<T>(res + round_act<T>(acc[0][tt]));
+            } else {
+              *yp = from_f<T>(acc[0][tt]);
+            }
+          }
+        }
+      }
+    }
+  }
+}
+
+template <typename T, int MODE, int EPI>
+static tf_status qmm_dispatch(const GemvArgs& a, cudaStream_t s) {
+  int sms = 148;
+  int64_t max_seg = MODE == QMM_DENSE ? 1 : MODE == QMM_PER_ROUTE ? a.n : a.experts;
+  const int nrb = (a.out + kGemvRows - 1) / kGemvRows;
+  int64_t items = max_seg * nrb;
+  if (items <= 0) return TF_OK;
+  const unsigned grid = (unsigned)(items < (int64_t)sms * 8 ? items : (int64_t)sms * 8);
+  if (a.in <= 1024)
+    qmm_gemv_kernel<T, MODE, EPI, 2, 1><<<grid, kGemvWarps * 32, 0, s>>>(a);
+  else if (a.in <= 2048)
+    qmm_gemv_kernel<T, MODE, EPI, 1, 2><<<grid, kGemvWarps * 32, 0, s>>>(a);
+  else
+    qmm_gemv_kernel<T, MODE, EPI, 1, 4><<<grid, kGemvWarps * 32, 0, s>>>(a);
+  return check_launch("qmm_gemv");
+}
+
+template <typename T>
+static tf_status qmm_by_mode(const GemvArgs& a, int mode, int epi, cudaStream_t s) {
+#define TF_QMM_EPI(MODE)                                                       \
+  switch (epi) {                                                               \
+    case EPI_PLAIN: return qmm_dispatch<T, MODE, EPI_PLAIN>(a, s);             \
+    case EPI_SWIGLU: return qmm_dispatch<T, MODE, EPI_SWIGLU>(a, s);           \
+    case EPI_F32: return qmm_dispatch<T, MODE, EPI_F32>(a, s);                 \
+    default: return qmm_dispatch<T, MODE, EPI_RESIDUAL>(a, s);                 \
+  }
+  switch (mode) {
+    case QMM_DENSE: TF_QMM_EPI(QMM_DENSE)
+    case QMM_PER_ROUTE: TF_QMM_EPI(QMM_PER_ROUTE)
+    default: TF_QMM_EPI(QMM_GROUPED)
+  }
+#undef TF_QMM_EPI
+}
+
+tf_status launch_qmm(const QmmProblem& p, cudaStream_t s) {
+  if (p.n == 0) return TF_OK;
+  if (p.w0.in_features > 4096)
+    return set_error(TF_ERR_UNSUPPORTED, "qmm: in_features %d > 4096", p.w0.in_features);
+  GemvArgs a;
+  a.x = p.x;
+  a.x_stride = p.x_stride;
+  a.x_index = p.x_index;
+  a.x_div = p.x_div;
+  a.rows_per_x = p.rows_per_x;
+  a.n = p.n;
+  a.indices = p.indices;
+  a.offsets = p.offsets;
+  a.active = p.active;
+  a.active_count = p.active_count;
+  a.q0 = p.w0.q;
+  a.s0 = (const __half*)p.w0.scales;
+  a.b0 = (const __half*)p.w0.biases;
+  a.q1 = p.epilogue == EPI_SWIGLU ? p.w1.q : p.w0.q;
+  a.s1 = (const __half*)(p.epilogue == EPI_SWIGLU ? p.w1.scales : p.w0.scales);
+  a.b1 = (const __half*)(p.epilogue == EPI_SWIGLU ? p.w1.biases : p.w0.biases);
+  a.out = p.w0.out_features;
+  a.in = p.w0.in_features;
+  a.experts = p.w0.experts > 0 ? p.w0.experts : 1;
+  a.y = p.y;
+  a.y_stride = p.y_stride;
+  a.residual = p.residual;
+  a.residual_stride = p.residual_stride;
+  if (p.act == TF_DTYPE_F16) return qmm_by_mode<__half>(a, p.mode, p.epilogue, s);
+  return qmm_by_mode<__nv_bfloat16>(a, p.mode, p.epilogue, s);
+}
+
+}  // namespace tf

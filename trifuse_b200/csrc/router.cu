@@ -1,0 +1,372 @@
+// OLMoE router: GEMV + softmax + stable top-k, and the stable route sort.
+//
+// Restates (file:line relative to the TriFuse root):
+//  - linear(x, layer.router)          MLXNativeGraniteMoEPrefill.h:631
+//  - olmoe_route / Metal router        overlays/executorch/backends/mlx/runtime/
+//                                      MLXOLMoERouter.h:19-120
+//  - native_olmoe_softmax / topk       native_affine_ops.py:128-153
+//  - route sort (argsort + inverse)    MLXNativeGraniteMoEPrefill.h:666-684
+//
+// One warp per token.  Every fp32 step is explicitly rounded so the result is
+// bit-identical to oracle/olmoe.py (router_logits_*, olmoe_softmax,
+// olmoe_topk): the dot product uses the chunk order "lane l owns 8-element
+// chunks l + 32j", the softmax uses exp in double rounded to fp32, and the
+// rank compares the act-rounded probabilities (NaN last, ties to lower id).
+#include <math.h>
+
+#include "common.cuh"
+#include "internal.h"
+
+namespace tf {
+
+constexpr int kRouterWarps = 4;
+
+// Ranks and writes the top-k of one token.  la0/la1: act-rounded logits of
+// experts lane and lane+32 (ignored when >= E).
+template <typename T>
+__device__ __forceinline__ void route_token(int lane, float la0, float la1, int E, int K,
+                                            int64_t t, T* probs, int32_t* idx, T* gates) {
+  const bool v0 = lane < E, v1 = lane + 32 < E;
+  float m = -INFINITY;
+  if (v0) m = fmaxf(m, la0);
+  if (v1) m = fmaxf(m, la1);
+  m = warp_max(m);
+  float e0 = 0.f, e1 = 0.f, part = 0.f;
+  if (v0) {
+    e0 = __double2float_rn(exp((double)__fsub_rn(la0, m)));
+    part = __fadd_rn(part, e0);
+  }
+  if (v1) {
+    e1 = __double2float_rn(exp((double)__fsub_rn(la1, m)));
+    part = __fadd_rn(part, e1);
+  }
+  const float sum = warp_sum_butterfly(part);
+  const float p0 = round_act<T>(__fdiv_rn(e0, sum));
+  const float p1 = round_act<T>(__fdiv_rn(e1, sum));
+  if (probs) {
+    if (v0) probs[t * E + lane] = from_f<T>(p0);
+    if (v1) probs[t * E + lane + 32] = from_f<T>(p1);
+  }
+  if (!idx) return;
+  int r0 = 0, r1 = 0;
+  const bool n0 = isnan(p0), n1 = isnan(p1);
+  for (int j = 0; j < E; ++j) {
+    const float o = __shfl_sync(0xffffffffu, j < 32 ? p0 : p1, j & 31);
+    const bool on = isnan(o);
+    // MLXOLMoERouter.h:67-78: before = other ranks strictly first; equal
+    // values (or both NaN) keep increasing expert id.
+    const bool before0 = !on && (n0 || o > p0);
+    const bool eq0 = (on && n0) || (!on && !n0 && o == p0);
+    r0 += (before0 || (eq0 && j < lane)) ? 1 : 0;
+    const bool before1 = !on && (n1 || o > p1);
+    const bool eq1 = (on && n1) || (!on && !n1 && o == p1);
+    r1 += (before1 || (eq1 && j < lane + 32)) ? 1 : 0;
+  }
+  if (v0 && r0 < K) {
+    idx[t * K + r0] = lane;
+    if (gates) gates[t * K + r0] = from_f<T>(p0);
+  }
+  if (v1 && r1 < K) {
+    idx[t * K + r1] = lane + 32;
+    if (gates) gates[t * K + r1] = from_f<T>(p1);
+  }
+}
+
+// Router GEMV: J = hidden / 256 chunks per lane.
+template <typename T, bool DENSE, int J>
+__global__ void __launch_bounds__(kRouterWarps * 32)
+    router_kernel(const T* __restrict__ x, int64_t tokens, const T* __restrict__ wd,
+                  const uint32_t* __restrict__ wq, const __half* __restrict__ ws,
+                  const __half* __restrict__ wb, int E, int K, T* logits, int32_t* idx, T* gates) {
+  const int lane = threadIdx.x & 31;
+  const int64_t t = (int64_t)blockIdx.x * kRouterWarps + (threadIdx.x >> 5);
+  if (t >= tokens) return;
+  constexpr int H = J * 256;
+  float xf[J][8];
+#pragma unroll
+  for (int j = 0; j < J; ++j) unpack8<T>(ld_v4(x + t * H + 8 * (lane + 32 * j)), xf[j]);
+  float la0 = 0.f, la1 = 0.f;
+  for (int e = 0; e < E; ++e) {
+    float acc = 0.f;
+#pragma unroll
+    for (int j = 0; j < J; ++j) {
+      const int c = lane + 32 * j;
+      float wf[8];
+      if (DENSE) {
+        unpack8<T>(ld_v4(wd + (int64_t)e * H + 8 * c), wf);
+      } else {
+        const uint32_t word = wq[(int64_t)e * (H / 8) + c];
+        const float s = __half2float(ws[(int64_t)e * (H / 64) + c / 8]);
+        const float b = __half2float(wb[(int64_t)e * (H / 64) + c / 8]);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float code = (float)((word >> (4 * i)) & 0xFu);
+          wf[i] = __half2float(__float2half_rn(__fadd_rn(__fmul_rn(code, s), b)));
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < 8; ++i) acc = __fadd_rn(acc, __fmul_rn(xf[j][i], wf[i]));
+    }
+    const float la = round_act<T>(warp_sum_butterfly(acc));
+    if (e == lane) la0 = la;
+    if (e == lane + 32) la1 = la;
+    if (logits && lane == 0) logits[t * E + e] = from_f<T>(la);
+  }
+  if (idx) route_token<T>(lane, la0, la1, E, K, t, (T*)nullptr, idx, gates);
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kRouterWarps * 32)
+    route_kernel(const T* __restrict__ logits, int64_t tokens, int E, int K, T* probs,
+                 int32_t* idx, T* gates) {
+  const int lane = threadIdx.x & 31;
+  const int64_t t = (int64_t)blockIdx.x * kRouterWarps + (threadIdx.x >> 5);
+  if (t >= tokens) return;
+  const float la0 = lane < E ? to_f(logits[t * E + lane]) : 0.f;
+  const float la1 = lane + 32 < E ? to_f(logits[t * E + lane + 32]) : 0.f;
+  route_token<T>(lane, la0, la1, E, K, t, probs, idx, gates);
+}
+
+// Rank only (input already probabilities).
+template <typename T>
+__global__ void __launch_bounds__(kRouterWarps * 32)
+    topk_kernel(const T* __restrict__ probs, int64_t rows, int E, int K, int32_t* idx) {
+  const int lane = threadIdx.x & 31;
+  const int64_t t = (int64_t)blockIdx.x * kRouterWarps + (threadIdx.x >> 5);
+  if (t >= rows) return;
+  const float p0 = lane < E ? to_f(probs[t * E + lane]) : 0.f;
+  const float p1 = lane + 32 < E ? to_f(probs[t * E + lane + 32]) : 0.f;
+  const bool v0 = lane < E, v1 = lane + 32 < E;
+  int r0 = 0, r1 = 0;
+  const bool n0 = isnan(p0), n1 = isnan(p1);
+  for (int j = 0; j < E; ++j) {
+    const float o = __shfl_sync(0xffffffffu, j < 32 ? p0 : p1, j & 31);
+    const bool on = isnan(o);
+    r0 += ((!on && (n0 || o > p0)) || (((on && n0) || (!on && !n0 && o == p0)) && j < lane)) ? 1 : 0;
+    r1 += ((!on && (n1 || o > p1)) || (((on && n1) || (!on && !n1 && o == p1)) && j < lane + 32)) ? 1 : 0;
+  }
+  if (v0 && r0 < K) idx[t * K + r0] = lane;
+  if (v1 && r1 < K) idx[t * K + r1] = lane + 32;
+}
+
+template <typename T>
+__global__ void take_along_kernel(const T* __restrict__ x, int64_t rows, int width,
+                                  const int32_t* __restrict__ idx, int K, T* out) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= rows * K) return;
+  const int64_t r = i / K;
+  out[i] = x[r * width + idx[i]];
+}
+
+template <typename T, bool DENSE>
+static tf_status router_dispatch(const void* x, int64_t tokens, int hidden,
+                                 const tf_router_weight& r, int E, int K, void* logits,
+                                 int32_t* idx, void* gates, cudaStream_t s) {
+  const unsigned blocks = (unsigned)((tokens + kRouterWarps - 1) / kRouterWarps);
+  const T* wd = (const T*)r.dense;
+  const uint32_t* wq = r.affine.q;
+  const __half* wsc = (const __half*)r.affine.scales;
+  const __half* wbi = (const __half*)r.affine.biases;
+#define TF_ROUTER_CASE(JJ)                                                            \
+  case JJ:                                                                            \
+    router_kernel<T, DENSE, JJ><<<blocks, kRouterWarps * 32, 0, s>>>(                 \
+        (const T*)x, tokens, wd, wq, wsc, wbi, E, K, (T*)logits, idx, (T*)gates);     \
+    break;
+  switch (hidden / 256) {
+    TF_ROUTER_CASE(1)
+    TF_ROUTER_CASE(2)
+    TF_ROUTER_CASE(4)
+    TF_ROUTER_CASE(8)
+    TF_ROUTER_CASE(16)
+    default:
+      return set_error(TF_ERR_UNSUPPORTED, "router: hidden %d not in {256,512,1024,2048,4096}",
+                       hidden);
+  }
+#undef TF_ROUTER_CASE
+  return check_launch("router");
+}
+
+tf_status launch_router(const void* x, int64_t tokens, int hidden, const tf_router_weight& r,
+                        int E, int K, int act, void* logits, int32_t* idx, void* gates,
+                        cudaStream_t s) {
+  if (tokens == 0) return TF_OK;
+  const bool dense = r.dense != nullptr;
+  if (act == TF_DTYPE_F16)
+    return dense ? router_dispatch<__half, true>(x, tokens, hidden, r, E, K, logits, idx, gates, s)
+                 : router_dispatch<__half, false>(x, tokens, hidden, r, E, K, logits, idx, gates, s);
+  return dense
+             ? router_dispatch<__nv_bfloat16, true>(x, tokens, hidden, r, E, K, logits, idx, gates, s)
+             : router_dispatch<__nv_bfloat16, false>(x, tokens, hidden, r, E, K, logits, idx, gates, s);
+}
+
+tf_status launch_route(const void* logits, int64_t tokens, int E, int K, int act, void* probs,
+                       int32_t* idx, void* gates, cudaStream_t s) {
+  if (tokens == 0) return TF_OK;
+  const unsigned blocks = (unsigned)((tokens + kRouterWarps - 1) / kRouterWarps);
+  if (act == TF_DTYPE_F16)
+    route_kernel<__half><<<blocks, kRouterWarps * 32, 0, s>>>(
+        (const __half*)logits, tokens, E, K, (__half*)probs, idx, (__half*)gates);
+  else
+    route_kernel<__nv_bfloat16><<<blocks, kRouterWarps * 32, 0, s>>>(
+        (const __nv_bfloat16*)logits, tokens, E, K, (__nv_bfloat16*)probs, idx,
+        (__nv_bfloat16*)gates);
+  return check_launch("route");
+}
+
+tf_status launch_topk(const void* probs, int64_t rows, int E, int K, int act, int32_t* idx,
+                      cudaStream_t s) {
+  if (rows == 0) return TF_OK;
+  const unsigned blocks = (unsigned)((rows + kRouterWarps - 1) / kRouterWarps);
+  if (act == TF_DTYPE_F16)
+    topk_kernel<__half><<<blocks, kRouterWarps * 32, 0, s>>>((const __half*)probs, rows, E, K, idx);
+  else
+    topk_kernel<__nv_bfloat16><<<blocks, kRouterWarps * 32, 0, s>>>((const __nv_bfloat16*)probs,
+                                                                    rows, E, K, idx);
+  return check_launch("topk");
+}
+
+tf_status launch_take_along(const void* x, int64_t rows, int width, const int32_t* idx, int K,
+                            int act, void* out, cudaStream_t s) {
+  const int64_t n = rows * K;
+  if (n == 0) return TF_OK;
+  const unsigned blocks = (unsigned)((n + 255) / 256);
+  if (act == TF_DTYPE_F16)
+    take_along_kernel<__half><<<blocks, 256, 0, s>>>((const __half*)x, rows, width, idx, K,
+                                                     (__half*)out);
+  else
+    take_along_kernel<__nv_bfloat16><<<blocks, 256, 0, s>>>((const __nv_bfloat16*)x, rows, width,
+                                                            idx, K, (__nv_bfloat16*)out);
+  return check_launch("take_along");
+}
+
+// ---------------------------------------------------------------------------
+// Stable counting sort of expert ids.
+//
+// Tiles of kSortTile routes.  Pass 1 counts each tile's routes per expert;
+// pass 2 (one block) turns the counts into global offsets, per-tile bases
+// and the ascending list of active experts; pass 3 places every route at
+// base[tile][e] + (routes of e earlier in the tile), using warp match masks
+// plus a per-warp exclusive scan, so slot order equals flat order within an
+// expert: order == stable argsort(ids).
+
+constexpr int kSortTile = 1024;
+constexpr int kSortMaxExperts = 256;
+
+__global__ void __launch_bounds__(kSortTile)
+    sort_count_kernel(const int32_t* __restrict__ ids, int64_t n, int E, int32_t* tile_counts) {
+  __shared__ int32_t cnt[kSortMaxExperts];
+  for (int e = threadIdx.x; e < E; e += blockDim.x) cnt[e] = 0;
+  __syncthreads();
+  const int64_t i = (int64_t)blockIdx.x * kSortTile + threadIdx.x;
+  if (i < n) atomicAdd(&cnt[ids[i]], 1);
+  __syncthreads();
+  for (int e = threadIdx.x; e < E; e += blockDim.x) tile_counts[(int64_t)blockIdx.x * E + e] = cnt[e];
+}
+
+// One block of kSortMaxExperts threads; thread e owns expert e.
+__global__ void __launch_bounds__(kSortMaxExperts)
+    sort_scan_kernel(int64_t tiles, int E, int32_t* tile_counts, int32_t* offsets, int32_t* active,
+                     int32_t* active_count) {
+  __shared__ int32_t total[kSortMaxExperts];
+  const int e = threadIdx.x;
+  int32_t sum = 0;
+  if (e < E)
+    for (int64_t t = 0; t < tiles; ++t) sum += tile_counts[t * E + e];
+  total[e] = e < E ? sum : 0;
+  __syncthreads();
+  if (e == 0) {
+    int32_t run = 0, na = 0;
+    for (int x = 0; x < E; ++x) {
+      offsets[x] = run;
+      const int32_t c = total[x];
+      total[x] = run;
+      run += c;
+      if (c > 0) active[na++] = x;
+    }
+    offsets[E] = run;
+    *active_count = na;
+  }
+  __syncthreads();
+  if (e < E) {
+    int32_t base = total[e];
+    for (int64_t t = 0; t < tiles; ++t) {
+      const int32_t c = tile_counts[t * E + e];
+      tile_counts[t * E + e] = base;  // becomes the tile's base for expert e
+      base += c;
+    }
+  }
+}
+
+__global__ void __launch_bounds__(kSortTile)
+    sort_place_kernel(const int32_t* __restrict__ ids, int64_t n, int E,
+                      const int32_t* __restrict__ tile_base, int32_t* order, int32_t* inverse) {
+  __shared__ int32_t warp_cnt[kSortTile / 32][kSortMaxExperts];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  for (int i = threadIdx.x; i < (kSortTile / 32) * E; i += blockDim.x)
+    warp_cnt[i / E][i % E] = 0;
+  __syncthreads();
+  const int64_t i = (int64_t)blockIdx.x * kSortTile + threadIdx.x;
+  const bool valid = i < n;
+  const int e = valid ? ids[i] : -1;
+  const unsigned peers = __match_any_sync(0xffffffffu, e);
+  const int rank = __popc(peers & ((1u << lane) - 1u));
+  if (valid && rank == 0) warp_cnt[warp][e] = __popc(peers);
+  __syncthreads();
+  // Exclusive scan over warps per expert, seeded with the tile base.
+  for (int x = threadIdx.x; x < E; x += blockDim.x) {
+    int32_t run = tile_base[(int64_t)blockIdx.x * E + x];
+    for (int w = 0; w < kSortTile / 32; ++w) {
+      const int32_t c = warp_cnt[w][x];
+      warp_cnt[w][x] = run;
+      run += c;
+    }
+  }
+  __syncthreads();
+  if (valid) {
+    const int32_t pos = warp_cnt[warp][e] + rank;
+    order[pos] = (int32_t)i;
+    inverse[i] = pos;
+  }
+}
+
+__global__ void gather_index_kernel(const int32_t* __restrict__ src, const int32_t* __restrict__ perm,
+                                    int64_t n, int div, int32_t* dst) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) dst[i] = src ? src[perm[i]] / div : perm[i] / div;
+}
+
+size_t sort_workspace_bytes(int64_t n, int experts) {
+  const int64_t tiles = (n + kSortTile - 1) / kSortTile;
+  return align_up((size_t)(tiles > 0 ? tiles : 1) * experts * sizeof(int32_t), 256);
+}
+
+tf_status launch_route_sort(const int32_t* ids, int64_t n, int E, int32_t* order, int32_t* inverse,
+                            int32_t* offsets, int32_t* active, int32_t* active_count, void* ws,
+                            size_t ws_bytes, cudaStream_t s) {
+  if (E > kSortMaxExperts)
+    return set_error(TF_ERR_UNSUPPORTED, "route sort supports at most %d experts", kSortMaxExperts);
+  if (ws_bytes < sort_workspace_bytes(n, E))
+    return set_error(TF_ERR_INVALID_ARGUMENT, "route sort workspace too small");
+  const int64_t tiles = (n + kSortTile - 1) / kSortTile;
+  int32_t* tile_counts = (int32_t*)ws;
+  if (tiles > 0) {
+    sort_count_kernel<<<(unsigned)tiles, kSortTile, 0, s>>>(ids, n, E, tile_counts);
+    TF_TRY(check_launch("sort_count"));
+  }
+  sort_scan_kernel<<<1, kSortMaxExperts, 0, s>>>(tiles, E, tile_counts, offsets, active, active_count);
+  TF_TRY(check_launch("sort_scan"));
+  if (tiles > 0) {
+    sort_place_kernel<<<(unsigned)tiles, kSortTile, 0, s>>>(ids, n, E, tile_counts, order, inverse);
+    TF_TRY(check_launch("sort_place"));
+  }
+  return TF_OK;
+}
+
+tf_status launch_gather_index(const int32_t* src, const int32_t* perm, int64_t n, int div,
+                              int32_t* dst, cudaStream_t s) {
+  if (n == 0) return TF_OK;
+  gather_index_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(src, perm, n, div, dst);
+  return check_launch("gather_index");
+}
+
+}  // namespace tf

@@ -1,0 +1,189 @@
+"""Device-resident OLMoE model and per-request sessions over the C ABI.
+
+Mirrors the reference's owner objects: ``Model`` stands for the
+NativeGraniteMoEPrefill adapter bound to a loaded checkpoint
+(MLXNativeGraniteMoEPrefill.h:157-304) and ``Session`` for the resident
+session with its KV cache (TFETResidentSession.h: forward / prefill /
+beginRequest / cancel).  All compute happens in libtrifuse_b200.so.
+"""
+from __future__ import annotations
+
+import ctypes as C
+from dataclasses import dataclass
+
+import torch
+
+from ._lib import DTYPE_BF16, DTYPE_F16, HOST_INPUTS, HOST_OUTPUT, OLMoEConfig, check, lib
+
+
+@dataclass
+class Config:
+    """OLMoE geometry (export_native_olmoe_target.py:27-63); defaults are
+    OLMoE-1B-7B."""
+    layers: int = 16
+    hidden: int = 2048
+    heads: int = 16
+    kv_heads: int = 16
+    head_dim: int = 128
+    intermediate: int = 1024
+    vocab: int = 50304
+    experts: int = 64
+    top_k: int = 8
+    capacity: int = 4096
+    rms_eps: float = 1e-5
+    rope_theta: float = 10000.0
+    act: torch.dtype = torch.float16
+
+    def c_struct(self) -> OLMoEConfig:
+        return OLMoEConfig(self.layers, self.hidden, self.heads, self.kv_heads, self.head_dim,
+                           self.intermediate, self.vocab, self.experts, self.top_k, self.capacity,
+                           self.rms_eps, self.rope_theta,
+                           DTYPE_F16 if self.act == torch.float16 else DTYPE_BF16)
+
+
+class Model:
+    def __init__(self, cfg: Config, weights: dict, device: int = 0):
+        self.cfg = cfg
+        self.device = device
+        h = C.c_void_p()
+        c = cfg.c_struct()
+        check(lib().tf_model_create(C.byref(c), device, C.byref(h)))
+        self.handle = h
+        try:
+            for name, t in weights.items():
+                t = t.contiguous()
+                nbytes = t.numel() * t.element_size()
+                check(lib().tf_model_bind(h, name.encode(), C.c_void_p(t.data_ptr()), nbytes,
+                                          int(t.is_cuda)))
+            check(lib().tf_model_finalize(h))
+        except Exception:
+            lib().tf_model_destroy(h)
+            self.handle = None
+            raise
+
+    def close(self):
+        if self.handle:
+            check(lib().tf_model_destroy(self.handle))
+            self.handle = None
+
+    def __del__(self):  # pragma: no cover
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class Session:
+    def __init__(self, model: Model, max_batch: int, capacity: int, max_prefill_tokens: int = 0):
+        self.model = model
+        self.max_batch = max_batch
+        self.capacity = capacity
+        h = C.c_void_p()
+        check(lib().tf_session_create(model.handle, max_batch, capacity, max_prefill_tokens, C.byref(h)))
+        self.handle = h
+
+    def kv(self, layer: int):
+        """(k, v) device pointers of one layer: f16 [max_batch][kv_heads][capacity][head_dim]."""
+        k, v = C.c_void_p(), C.c_void_p()
+        check(lib().tf_session_kv(self.handle, layer, C.byref(k), C.byref(v)))
+        return k.value, v.value
+
+    def kv_tensors(self, layer: int):
+        """Torch views of one layer's caches (no copy)."""
+        cfg = self.model.cfg
+        shape = (self.max_batch, cfg.kv_heads, self.capacity, cfg.head_dim)
+        out = []
+        for ptr in self.kv(layer):
+            out.append(_device_view(ptr, shape, torch.float16, self.model.device))
+        return out
+
+    def set_lengths(self, lengths):
+        arr = (C.c_int32 * len(lengths))(*lengths)
+        check(lib().tf_session_set_lengths(self.handle, arr, len(lengths)))
+
+    def lengths(self, batch=None):
+        batch = self.max_batch if batch is None else batch
+        arr = (C.c_int32 * batch)()
+        check(lib().tf_session_get_lengths(self.handle, arr, batch))
+        return list(arr)
+
+    def decode(self, token_ids: torch.Tensor, positions=None, logits: torch.Tensor | None = None):
+        """One token per request; token_ids int64 [B] (host or device);
+        returns fp32 logits [B, vocab] on the same side as `logits` or the ids."""
+        B = token_ids.numel()
+        ids = token_ids.to(torch.int64).contiguous()
+        flags = 0 if ids.is_cuda else HOST_INPUTS
+        if logits is None:
+            logits = torch.empty((B, self.model.cfg.vocab), dtype=torch.float32,
+                                 device=ids.device if ids.is_cuda else "cpu",
+                                 pin_memory=not ids.is_cuda)
+        if not logits.is_cuda:
+            flags |= HOST_OUTPUT
+        pos = None
+        if positions is not None:
+            pos = (C.c_int32 * B)(*[int(p) for p in positions])
+        check(lib().tf_session_decode(self.handle, C.c_void_p(ids.data_ptr()), pos, B,
+                                      C.c_void_p(logits.data_ptr()), flags,
+                                      C.c_void_p(torch.cuda.current_stream().cuda_stream)))
+        return logits
+
+    def prefill(self, requests, token_lists, want_logits=True):
+        """Prefill several requests; token_lists: list of int64 tensors/lists."""
+        counts = [len(t) for t in token_lists]
+        ids = torch.cat([torch.as_tensor(t, dtype=torch.int64).cpu() for t in token_lists]).contiguous()
+        n = len(requests)
+        req = (C.c_int32 * n)(*requests)
+        cnt = (C.c_int32 * n)(*counts)
+        logits = None
+        if want_logits:
+            logits = torch.empty((n, self.model.cfg.vocab), dtype=torch.float32)
+        check(lib().tf_session_prefill(self.handle, req, cnt, n, C.c_void_p(ids.data_ptr()),
+                                       C.c_void_p(logits.data_ptr()) if logits is not None else None,
+                                       HOST_INPUTS | HOST_OUTPUT,
+                                       C.c_void_p(torch.cuda.current_stream().cuda_stream)))
+        return logits
+
+    def trace(self, enable: bool):
+        """Turn phase tracing (CUDA events around each forward phase) on/off."""
+        check(lib().tf_session_trace(self.handle, int(enable)))
+
+    def trace_read(self):
+        """{phase: (total_ms, count)} over traced calls since the last read."""
+        n = lib().tf_trace_phases()
+        ms = (C.c_float * n)()
+        cnt = (C.c_int32 * n)()
+        check(lib().tf_session_trace_read(self.handle, ms, cnt))
+        return {lib().tf_trace_phase_name(i).decode(): (ms[i], cnt[i]) for i in range(n)}
+
+    def cancel(self):
+        check(lib().tf_session_cancel(self.handle))
+
+    def reset(self):
+        check(lib().tf_session_reset(self.handle))
+
+    def close(self):
+        if self.handle:
+            check(lib().tf_session_destroy(self.handle))
+            self.handle = None
+
+    def __del__(self):  # pragma: no cover
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def _device_view(ptr: int, shape, dtype, device: int) -> torch.Tensor:
+    """Wrap externally owned device memory as a tensor (lifetime = session)."""
+    numel = 1
+    for d in shape:
+        numel *= d
+    esize = torch.empty((), dtype=dtype).element_size()
+
+    class _Holder:
+        __cuda_array_interface__ = {
+            "shape": (numel * esize,), "typestr": "|u1", "data": (ptr, False), "version": 3,
+        }
+
+    raw = torch.as_tensor(_Holder(), device=f"cuda:{device}")
+    return raw.view(dtype).reshape(shape)
