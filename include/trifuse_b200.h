@@ -94,6 +94,16 @@ int tf_device_check(int device);
  * Diagnostic counter; no reference counterpart beyond the env-gated timing
  * lines of src/apple/TFETResidentSession.mm:48-83. */
 uint64_t tf_launch_count(void);
+/* Kernel path for the 4-bit QMMs: 0 = automatic (tensor cores when a weight
+ * matrix serves enough tokens), 1 = CUDA-core GEMV only, 2 = tensor cores
+ * whenever the shape allows.  Process-wide; for A/B checks and timing.
+ * The reference's analogue is TRIFUSE_SORTED_QMM_BM (patches/mlx.patch:
+ * 186-206) selecting its gather_qmm tile. */
+int tf_set_qmm_path(int path);
+/* First error code recorded by a device-side bounded wait since the last
+ * clear (0 = none): a tensor-core tile whose pipeline stalled past its
+ * limit returns early instead of hanging.  Synchronizes the device. */
+int tf_device_error(int clear);
 
 /* ------------------------------------------------------------------------ */
 /* operators (graph-level surface)                                            */

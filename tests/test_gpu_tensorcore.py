@@ -1,0 +1,86 @@
+"""Parity of the tcgen05/TMEM 4-bit QMM path (batched decode / prefill
+shapes) against the oracle and against the CUDA-core GEMV path."""
+import contextlib
+
+import numpy as np
+import pytest
+
+import oracle
+from tests.gpu_util import bits_equal, dev, experts_dev, experts_np, host
+from tests.parity import assert_close
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def ops():
+    from trifuse_b200 import ops as _ops
+    return _ops
+
+
+@contextlib.contextmanager
+def path(ops, p):
+    ops.set_qmm_path(p)
+    try:
+        yield
+    finally:
+        ops.set_qmm_path(0)
+
+
+@pytest.mark.parametrize("act,T,out,inn", [("f16", 8, 2048, 2048), ("bf16", 16, 6144, 2048),
+                                           ("f16", 64, 2048, 1024), ("bf16", 300, 1024, 2048),
+                                           ("f16", 77, 50304 // 8, 2048)])
+def test_dense_tensor_core_qmm(ops, act, T, out, inn):
+    rng = np.random.default_rng(11)
+    x = oracle.to_act(rng.standard_normal((T, inn)).astype(np.float32), act)
+    q, s, b = oracle.affine_quantize(oracle.round_bf16(rng.standard_normal((out, inn)).astype(np.float32) * 0.02))
+    args = (dev(x, act), dev(q), dev(s), dev(b), 64, 4)
+    with path(ops, 2):
+        tc = host(ops.native_affine_qmm(*args))
+    with path(ops, 1):
+        gemv = host(ops.native_affine_qmm(*args))
+    assert ops.device_error() == 0
+    ref = oracle.affine_qmm(x, q, s, b, act)
+    assert_close(tc, ref)
+    assert_close(tc, gemv)
+
+
+@pytest.mark.parametrize("act,T,skew", [("f16", 64, False), ("bf16", 256, False), ("f16", 600, True),
+                                        ("bf16", 2048, True)])
+def test_moe_tensor_core_against_oracle(ops, act, T, skew):
+    rng = np.random.default_rng(12)
+    H, I, E, K = 2048, 1024, 64, 8
+    x = oracle.to_act(rng.standard_normal((T, H)).astype(np.float32), act)
+    res = oracle.to_act(rng.standard_normal((T, H)).astype(np.float32), act)
+    ex = experts_np(rng, E, H, I)
+    wr = rng.standard_normal((E, H)).astype(np.float32) * 0.02
+    if skew:  # uneven expert loads: router rows with larger norms win more tokens
+        wr *= (1 + np.abs(rng.standard_normal((E, 1)).astype(np.float32)) * 3)
+    w = oracle.to_act(wr, act)
+    d = experts_dev(ex)
+    with path(ops, 2):
+        out, aux = ops.moe(dev(x, act), dev(res, act), dev(w, act), d["gate"], d["up"], d["down"], K,
+                           return_aux=True)
+    assert ops.device_error() == 0
+    ref, raux = oracle.moe_block(x, res, ("dense", w), ex, K, act)
+    assert np.array_equal(host(aux["indices"]), raux["indices"])
+    assert_close(host(out), ref)
+
+
+def test_expert_hook_tensor_core(ops):
+    rng = np.random.default_rng(13)
+    act, T, H, I, E, N = "bf16", 200, 2048, 1024, 8, 900
+    x = oracle.to_act(rng.standard_normal((T, H)).astype(np.float32), act)
+    ex = experts_np(rng, E, H, I)
+    tok = rng.integers(0, T, size=N).astype(np.int32)
+    eid = rng.integers(0, E, size=N).astype(np.int32)
+    d = experts_dev(ex)
+    with path(ops, 2):
+        out, inverse = ops.expert_gpu(dev(x, act), dev(tok), dev(eid), False, d["gate"], d["up"], d["down"])
+    assert ops.device_error() == 0
+    order = np.argsort(eid, kind="stable")
+    rows = x[tok[order]]
+    sel = eid[order]
+    h = oracle.swiglu(oracle.gather_qmm(rows, *ex["gate"], sel, act),
+                      oracle.gather_qmm(rows, *ex["up"], sel, act), act)
+    assert_close(host(out), oracle.gather_qmm(h, *ex["down"], sel, act))

@@ -89,6 +89,8 @@ SIGNATURES = {
     "tf_session_prefill": [P, P, P, I32, P, P, C.c_int, P],
     "tf_session_cancel": [P],
     "tf_launch_count": [],
+    "tf_set_qmm_path": [C.c_int],
+    "tf_device_error": [C.c_int],
     "tf_trace_phases": [],
     "tf_trace_phase_name": [C.c_int],
     "tf_session_trace": [P, C.c_int],

@@ -86,6 +86,17 @@ int tf_abi_version(void) { return TF_ABI_VERSION; }
 
 uint64_t tf_launch_count(void) { return g_launches.load(); }
 
+int tf_set_qmm_path(int path) {
+  if (path < 0 || path > 2) return set_error(TF_ERR_INVALID_ARGUMENT, "qmm path must be 0, 1 or 2");
+  g_qmm_path = path;
+  return TF_OK;
+}
+
+int tf_device_error(int clear) {
+  TF_CUDA(cudaDeviceSynchronize());
+  return read_tc_error(clear != 0);
+}
+
 const char* tf_last_error(void) { return g_error.c_str(); }
 
 const char* tf_status_name(int status) {

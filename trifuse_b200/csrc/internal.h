@@ -129,7 +129,14 @@ struct QmmProblem {
   const void* residual = nullptr;  // EPI_RESIDUAL, indexed like y
   int64_t residual_stride = 0;
 };
+// Dispatches to the tensor-core kernel (launch_qmm_tc) when the problem has
+// enough tokens per weight matrix, else to the CUDA-core GEMV.
 tf_status launch_qmm(const QmmProblem& p, cudaStream_t s);
+tf_status launch_qmm_gemv(const QmmProblem& p, cudaStream_t s);
+tf_status launch_qmm_tc(const QmmProblem& p, cudaStream_t s);
+// 0 = automatic, 1 = CUDA-core GEMV only, 2 = tensor cores whenever eligible.
+extern int g_qmm_path;
+int read_tc_error(bool clear);
 
 // ---------------------------------------------------------------- combine
 tf_status launch_combine(const void* y_sorted, const int32_t* inverse, const void* gates,

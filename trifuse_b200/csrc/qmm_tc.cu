@@ -1,0 +1,580 @@
+// MLX-affine 4-bit grouped QMM on the 5th-generation tensor cores
+// (tcgen05 + TMEM), for many tokens per weight matrix (batched decode and
+// prefill).
+//
+// Restates native_affine_gather_qmm / quantized_matmul
+// (overlays/executorch/backends/mlx/native_affine_ops.py:39-74,
+// MLXNativeGraniteMoEPrefill.h:539-550, 685-687) as D = W_e . X^T per expert:
+// the weight rows are the MMA's M side (128 rows per tile) and the expert's
+// tokens the N side (up to NMAX per tile), so a tile of few tokens still
+// fills the 128-row MMA.  Weights are dequantized once per tile and k-step
+// as fp16(code*s + b) / bf16(code*s + b) (fp32 FMA, one rounding; the
+// reference rounds the dequantized weight to its float16 scale dtype,
+// native_affine_ops.py:36) and accumulated in fp32 in TMEM.
+//
+// Block roles (160 threads):
+//   warps 0-3  producers: thread r owns A row r.  Per k-step (64 inputs =
+//              one quantization group) it cp.async-stages its row's 32
+//              packed bytes and a share of the tokens' 128-byte activation
+//              rows (the B tile, gathered by route order), then dequantizes
+//              its row into the 128B-swizzled K-major A tile;
+//              afterwards the same warps are the epilogue (tcgen05.ld).
+//   warp 4     allocates TMEM; lane 0 issues tcgen05.mma (4 x K=16 per
+//              k-step) and tcgen05.commit to release stages.
+// Stages are guarded by mbarriers; every wait is bounded (about one second
+// of SM clock) and on expiry records an error code instead of hanging.
+#include <stdio.h>
+
+#include "common.cuh"
+#include "internal.h"
+
+namespace tf {
+
+__device__ int g_tc_error = 0;  // first error code recorded by a bounded wait
+
+namespace tc {
+
+constexpr int kProducerWarps = 4;
+constexpr int kThreads = (kProducerWarps + 1) * 32;
+constexpr int kM = 128;            // A rows per tile (MMA M)
+constexpr int kKStep = 64;         // inputs per k-step (one group, 128 B of 16-bit)
+constexpr long long kWaitCycles = 2000000000LL;
+
+__device__ __forceinline__ uint32_t smem_addr(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count));
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_addr(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait: false (and an error code recorded) when the phase does not
+// complete within kWaitCycles.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int code) {
+  if (mbar_try(bar, parity)) return true;
+  const long long t0 = clock64();
+  while (!mbar_try(bar, parity)) {
+    if (clock64() - t0 > kWaitCycles) {
+      atomicCAS(&g_tc_error, 0, code);
+      return false;
+    }
+  }
+  return true;
+}
+
+__device__ __forceinline__ void cp_async16(void* dst, const void* src, uint32_t src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_addr(dst)), "l"(src),
+               "r"(src_bytes)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+__device__ __forceinline__ void fence_proxy_async() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+// K-major, 128-byte swizzled operand descriptor (rows of 128 B, 8-row groups
+// 1024 B apart; start address advanced by 32 B per K=16 slice).
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3FFFu);         // start address
+  d |= (uint64_t)1 << 16;                          // leading byte offset (unused for SW128 K-major)
+  d |= (uint64_t)(1024u >> 4) << 32;               // stride byte offset
+  d |= (uint64_t)1 << 46;                          // descriptor version (sm100)
+  d |= (uint64_t)2 << 61;                          // SWIZZLE_128B
+  return d;
+}
+
+// Instruction descriptor, kind::f16 with fp32 accumulate, K-major A and B.
+__device__ __forceinline__ uint32_t idesc_f16(bool bf16, int m, int n) {
+  uint32_t d = 0;
+  d |= 1u << 4;                                    // D format F32
+  d |= (bf16 ? 1u : 0u) << 7;                      // A format
+  d |= (bf16 ? 1u : 0u) << 10;                     // B format
+  d |= (uint32_t)(n >> 3) << 17;
+  d |= (uint32_t)(m >> 4) << 24;
+  return d;
+}
+
+__device__ __forceinline__ void mma_f16(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc,
+                                       uint32_t accumulate) {
+  uint32_t mask0 = 0, mask1 = 0, mask2 = 0, mask3 = 0;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}"
+      ::"r"(tmem_d), "l"(a), "l"(b), "r"(idesc), "r"(accumulate), "r"(mask0), "r"(mask1), "r"(mask2),
+      "r"(mask3)
+      : "memory");
+}
+
+__device__ __forceinline__ void mma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   smem_addr(bar))
+               : "memory");
+}
+
+// 16 consecutive fp32 columns of this thread's TMEM lane.
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// Two fp32 -> packed 16-bit pair (round to nearest even).
+template <typename T>
+__device__ __forceinline__ uint32_t pack2(float lo, float hi);
+template <>
+__device__ __forceinline__ uint32_t pack2<__half>(float lo, float hi) {
+  __half2 h = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+template <>
+__device__ __forceinline__ uint32_t pack2<__nv_bfloat16>(float lo, float hi) {
+  __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+__device__ __forceinline__ float code_f(uint32_t w, int j) {
+  return __int_as_float(0x4B000000u | ((w >> (4 * j)) & 0xFu)) - 8388608.0f;
+}
+
+struct Args {
+  const void* x;
+  int64_t x_stride;
+  const int32_t* x_index;
+  int x_div;
+  int64_t n;  // slots
+  const int32_t* offsets;
+  const int32_t* active;
+  const int32_t* active_count;
+  int grouped;
+  const uint32_t* q0;
+  const __half* s0;
+  const __half* b0;
+  const uint32_t* q1;
+  const __half* s1;
+  const __half* b1;
+  int out;     // weight rows per expert (per matrix)
+  int in;
+  int nt;      // token tile (<= NMAX)
+  int row_blocks;
+  void* y;
+  int64_t y_stride;
+  const void* residual;
+  int64_t residual_stride;
+};
+
+template <int NMAX, int STAGES>
+struct Smem {
+  static constexpr int kA = kM * 128;         // 16 KB, bf16/f16 tile
+  static constexpr int kB = NMAX * 128;       // token tile
+  static constexpr int kP = kM * 32;          // packed codes of the tile
+  static constexpr int kStage = kA + kB + kP;
+  static size_t bytes(int in) {
+    // [barriers 1 KB][rows NMAX*4][scales+biases kM*(in/64)*4][pad to 1024][stages]
+    size_t head = 1024 + NMAX * 4 + (size_t)kM * (in / 64) * 4;
+    head = (head + 1023) / 1024 * 1024;
+    return head + (size_t)STAGES * kStage + 1024;  // +1024 for base alignment
+  }
+};
+
+template <typename T, int EPI, int NMAX, int STAGES>
+__global__ void __launch_bounds__(kThreads, 1) qmm_tc_kernel(Args a) {
+  extern __shared__ uint8_t smem_raw[];
+  using S = Smem<NMAX, STAGES>;
+  // 1024-byte aligned base (swizzle atoms must be 1024-aligned).
+  uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(base);
+  uint64_t* empty = full + STAGES;
+  uint64_t* done = empty + STAGES;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+  int* tile_info = reinterpret_cast<int*>(tmem_slot + 1);  // [expert, s0, count]
+  int32_t* rows = reinterpret_cast<int32_t*>(base + 1024);
+  __half* sb = reinterpret_cast<__half*>(rows + NMAX);    // [kM][groups] scales then biases
+  const int groups = a.in / 64;
+  size_t head = 1024 + NMAX * 4 + (size_t)kM * groups * 4;
+  head = (head + 1023) / 1024 * 1024;
+  uint8_t* stages = base + head;
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+
+  // ---- which tile: (expert, token block, row block)
+  const int rb = blockIdx.x % a.row_blocks;
+  int64_t tblock = blockIdx.x / a.row_blocks;
+  if (tid == 0) {
+    int e = -1, s0 = 0, cnt = 0;
+    if (!a.grouped) {
+      const int64_t nblk = (a.n + a.nt - 1) / a.nt;
+      if (tblock < nblk) {
+        e = 0;
+        s0 = (int)(tblock * a.nt);
+        cnt = (int)((a.n - s0) < (int64_t)a.nt ? (a.n - s0) : (int64_t)a.nt);
+      }
+    } else {
+      const int na = *a.active_count;
+      for (int i = 0; i < na; ++i) {
+        const int ex = a.active[i];
+        const int c0 = a.offsets[ex], c1 = a.offsets[ex + 1];
+        const int nb = (c1 - c0 + a.nt - 1) / a.nt;
+        if (tblock < nb) {
+          e = ex;
+          s0 = c0 + (int)tblock * a.nt;
+          cnt = min(a.nt, c1 - s0);
+          break;
+        }
+        tblock -= nb;
+      }
+    }
+    tile_info[0] = e;
+    tile_info[1] = s0;
+    tile_info[2] = cnt;
+  }
+  __syncthreads();
+  const int e = tile_info[0];
+  if (e < 0) return;  // past the last tile of this launch
+  const int s0 = tile_info[1], cnt = tile_info[2];
+  const int n_mma = (cnt + 15) / 16 * 16;  // MMA N: multiple of 16 for M = 128
+  const int nk = a.in / kKStep;
+
+  // ---- setup: barriers, TMEM, token rows
+  if (tid == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], kProducerWarps * 32);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(done, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == kProducerWarps) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(tmem_slot)),
+                 "r"((uint32_t)NMAX));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  for (int i = tid; i < NMAX; i += kThreads) {
+    int32_t r = -1;
+    if (i < cnt) {
+      const int64_t slot = s0 + i;
+      r = a.x_index ? a.x_index[slot] / a.x_div : (int32_t)slot;
+    }
+    rows[i] = r;
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  // A row r of this tile: matrix 0 rows for EPI != SWIGLU; for SWIGLU rows
+  // 0..63 are gate rows f0.. and 64..127 the matching up rows.
+  if (warp < kProducerWarps) {
+    const int r = tid;
+    int wrow;
+    const uint32_t* q;
+    const __half* sc;
+    const __half* bi;
+    if (EPI == EPI_SWIGLU) {
+      const int f = rb * (kM / 2) + (r & 63);
+      wrow = f < a.out ? f : a.out - 1;
+      q = r < 64 ? a.q0 : a.q1;
+      sc = r < 64 ? a.s0 : a.s1;
+      bi = r < 64 ? a.b0 : a.b1;
+    } else {
+      const int f = rb * kM + r;
+      wrow = f < a.out ? f : a.out - 1;
+      q = a.q0;
+      sc = a.s0;
+      bi = a.b0;
+    }
+    const int64_t grow = (int64_t)e * a.out + wrow;
+    const uint32_t* qrow = q + grow * (a.in / 8);
+    // Row scales / biases for the whole K extent (first commit group).
+    __half* my_s = sb + (size_t)r * groups;
+    __half* my_b = sb + (size_t)kM * groups + (size_t)r * groups;
+    for (int g = 0; g < groups; g += 8) {
+      cp_async16(my_s + g, sc + grow * groups + g, 16);
+      cp_async16(my_b + g, bi + grow * groups + g, 16);
+    }
+    const T* xb = static_cast<const T*>(a.x);
+    auto issue = [&](int k) {
+      uint8_t* st = stages + (size_t)(k % STAGES) * S::kStage;
+      uint8_t* P = st + S::kA + S::kB;
+      cp_async16(P + r * 32, qrow + k * 8, 16);
+      cp_async16(P + r * 32 + 16, qrow + k * 8 + 4, 16);
+      uint8_t* Bt = st + S::kA;
+      for (int c = r; c < n_mma * 8; c += kProducerWarps * 32) {
+        const int tok = c >> 3, ch = c & 7;
+        const int32_t xr = rows[tok];
+        const void* src = xb + (xr >= 0 ? (int64_t)xr * a.x_stride : 0) + k * kKStep + ch * 8;
+        cp_async16(Bt + tok * 128 + ((ch ^ (tok & 7)) << 4), src, xr >= 0 ? 16u : 0u);
+      }
+    };
+    bool ok = true;
+    for (int k = 0; k < STAGES - 1; ++k) {
+      if (k < nk) issue(k);
+      cp_async_commit();
+    }
+    for (int k = 0; k < nk && ok; ++k) {
+      const int kn = k + STAGES - 1;
+      if (kn < nk) {
+        if (kn >= STAGES) ok = mbar_wait(&empty[kn % STAGES], ((kn / STAGES) - 1) & 1, 1);
+        if (ok) issue(kn);
+      }
+      cp_async_commit();
+      cp_async_wait<STAGES - 1>();
+      // Dequantize this thread's row of k-step k into the swizzled A tile.
+      uint8_t* st = stages + (size_t)(k % STAGES) * S::kStage;
+      const uint4* P = reinterpret_cast<const uint4*>(st + S::kA + S::kB + r * 32);
+      const uint4 p0 = P[0], p1 = P[1];
+      const float s = __half2float(my_s[k]);
+      const float b = __half2float(my_b[k]);
+      const uint32_t words[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
+      uint8_t* Arow = st + r * 128;
+#pragma unroll
+      for (int ch = 0; ch < 8; ++ch) {
+        const uint32_t w = words[ch];
+        uint4 v;
+        v.x = pack2<T>(fmaf(code_f(w, 0), s, b), fmaf(code_f(w, 1), s, b));
+        v.y = pack2<T>(fmaf(code_f(w, 2), s, b), fmaf(code_f(w, 3), s, b));
+        v.z = pack2<T>(fmaf(code_f(w, 4), s, b), fmaf(code_f(w, 5), s, b));
+        v.w = pack2<T>(fmaf(code_f(w, 6), s, b), fmaf(code_f(w, 7), s, b));
+        *reinterpret_cast<uint4*>(Arow + ((ch ^ (r & 7)) << 4)) = v;
+      }
+      fence_proxy_async();
+      mbar_arrive(&full[k % STAGES]);
+    }
+    cp_async_wait<0>();
+    // ---- epilogue: wait for the accumulator, read this warp's 32 lanes.
+    const uint32_t mine = (ok && mbar_wait(done, 0, 3)) ? 1u : 0u;
+    uint32_t all_ok;
+    // Every producer thread reaches this barrier (all waits are bounded);
+    // the AND makes the epilogue decision uniform across the four warps.
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 p, %1, 0;\n\t"
+        "bar.red.and.pred q, 1, %2, p;\n\tselp.u32 %0, 1, 0, q;\n\t}"
+        : "=r"(all_ok)
+        : "r"(mine), "n"(kProducerWarps * 32)
+        : "memory");
+    tc_fence_after();
+    if (all_ok) {
+      const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+      float* xch = reinterpret_cast<float*>(stages);  // [64][NMAX] up values for SWIGLU
+      __syncwarp();
+      if (EPI == EPI_SWIGLU) {
+        // warps 2,3 hold up rows; publish them, then warps 0,1 combine.
+        if (warp >= 2) {
+          for (int c0 = 0; c0 < n_mma; c0 += 16) {
+            float v[16];
+            tmem_ld16(tmem + lane_base + c0, v);
+#pragma unroll
+            for (int i = 0; i < 16; ++i) xch[(size_t)(r - 64) * NMAX + c0 + i] = v[i];
+          }
+        }
+        asm volatile("bar.sync 2, %0;" ::"n"(kProducerWarps * 32) : "memory");
+        if (warp < 2) {
+          const int f = rb * (kM / 2) + r;
+          for (int c0 = 0; c0 < n_mma; c0 += 16) {
+            float v[16];
+            tmem_ld16(tmem + lane_base + c0, v);
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              const int tok = c0 + i;
+              if (tok < cnt && f < a.out) {
+                const float g = round_act<T>(v[i]);
+                const float u = round_act<T>(xch[(size_t)r * NMAX + tok]);
+                const float sl = round_act<T>(g / (1.0f + expf(-g)));
+                T* yp = static_cast<T*>(a.y) + (int64_t)(s0 + tok) * a.y_stride + f;
+                *yp = from_f<T>(sl * u);
+              }
+            }
+          }
+        }
+      } else {
+        const int f = rb * kM + r;
+        for (int c0 = 0; c0 < n_mma; c0 += 16) {
+          float v[16];
+          tmem_ld16(tmem + lane_base + c0, v);
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const int tok = c0 + i;
+            if (tok < cnt && f < a.out) {
+              const int64_t slot = s0 + tok;
+              if (EPI == EPI_F32) {
+                static_cast<float*>(a.y)[slot * a.y_stride + f] = round_act<T>(v[i]);
+              } else if (EPI == EPI_RESIDUAL) {
+                const float res = to_f(static_cast<const T*>(a.residual)[slot * a.residual_stride + f]);
+                static_cast<T*>(a.y)[slot * a.y_stride + f] = from_f<T>(res + round_act<T>(v[i]));
+              } else {
+                static_cast<T*>(a.y)[slot * a.y_stride + f] = from_f<T>(v[i]);
+              }
+            }
+          }
+        }
+      }
+    }
+  } else if (lane == 0) {
+    // ---- MMA issuer
+    const uint32_t idesc = idesc_f16(Act<T>::kDtype == TF_DTYPE_BF16, kM, n_mma);
+    bool ok = true;
+    int issued = 0;
+    for (int k = 0; k < nk; ++k) {
+      if (!mbar_wait(&full[k % STAGES], (k / STAGES) & 1, 2)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      uint8_t* st = stages + (size_t)(k % STAGES) * S::kStage;
+      const uint32_t a_addr = smem_addr(st), b_addr = smem_addr(st + S::kA);
+#pragma unroll
+      for (int j = 0; j < kKStep / 16; ++j)
+        mma_f16(tmem, sw128_desc(a_addr + 32 * j), sw128_desc(b_addr + 32 * j), idesc,
+                (k > 0 || j > 0) ? 1u : 0u);
+      mma_commit(&empty[k % STAGES]);
+      ++issued;
+    }
+    // Signal (or, on error, drain) completion of every MMA issued.
+    mma_commit(done);
+    if (!ok) mbar_wait(done, 0, 4);
+    (void)issued;
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == kProducerWarps)
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"((uint32_t)NMAX));
+}
+
+}  // namespace tc
+
+namespace {
+
+template <typename T, int EPI, int NMAX, int STAGES>
+tf_status launch_tc_cfg(const tc::Args& a, int64_t token_tiles, cudaStream_t s) {
+  using S = tc::Smem<NMAX, STAGES>;
+  const size_t smem = S::bytes(a.in);
+  static bool attr_set = false;
+  if (!attr_set) {
+    TF_CUDA(cudaFuncSetAttribute(tc::qmm_tc_kernel<T, EPI, NMAX, STAGES>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    attr_set = true;
+  }
+  const int64_t grid = token_tiles * a.row_blocks;
+  if (grid <= 0) return TF_OK;
+  if (grid > 0x7fffffff) return set_error(TF_ERR_UNSUPPORTED, "qmm_tc: grid too large");
+  tc::qmm_tc_kernel<T, EPI, NMAX, STAGES><<<(unsigned)grid, tc::kThreads, smem, s>>>(a);
+  return check_launch("qmm_tc");
+}
+
+template <typename T, int EPI>
+tf_status launch_tc_epi(const tc::Args& a0, int64_t max_count_hint, int64_t tiles_bound_64,
+                        int64_t tiles_bound_256, cudaStream_t s) {
+  tc::Args a = a0;
+  if (max_count_hint <= 64) {
+    a.nt = 64;
+    return launch_tc_cfg<T, EPI, 64, 3>(a, tiles_bound_64, s);
+  }
+  a.nt = 256;
+  return launch_tc_cfg<T, EPI, 256, 3>(a, tiles_bound_256, s);
+}
+
+}  // namespace
+
+// Tensor-core QMM for the same problem description as launch_qmm.
+// avg_tokens: host estimate of tokens per weight matrix (chooses the tile).
+tf_status launch_qmm_tc(const QmmProblem& p, cudaStream_t s) {
+  if (p.n == 0) return TF_OK;
+  if (p.mode == QMM_PER_ROUTE) return set_error(TF_ERR_UNSUPPORTED, "qmm_tc: per-route mode");
+  const int in = p.w0.in_features;
+  if (in % 64 || in > 8192) return set_error(TF_ERR_UNSUPPORTED, "qmm_tc: in_features %d", in);
+  tc::Args a;
+  a.x = p.x;
+  a.x_stride = p.x_stride;
+  a.x_index = p.x_index;
+  a.x_div = p.x_div;
+  a.n = p.n;
+  a.offsets = p.offsets;
+  a.active = p.active;
+  a.active_count = p.active_count;
+  a.grouped = p.mode == QMM_GROUPED;
+  a.q0 = p.w0.q;
+  a.s0 = (const __half*)p.w0.scales;
+  a.b0 = (const __half*)p.w0.biases;
+  const bool sw = p.epilogue == EPI_SWIGLU;
+  a.q1 = sw ? p.w1.q : p.w0.q;
+  a.s1 = (const __half*)(sw ? p.w1.scales : p.w0.scales);
+  a.b1 = (const __half*)(sw ? p.w1.biases : p.w0.biases);
+  a.out = p.w0.out_features;
+  a.in = in;
+  a.row_blocks = sw ? (a.out + 63) / 64 : (a.out + 127) / 128;
+  a.y = p.y;
+  a.y_stride = p.y_stride;
+  a.residual = p.residual;
+  a.residual_stride = p.residual_stride;
+  // Token tiles: dense = ceil(n / nt); grouped <= experts + n / nt.
+  const int experts = p.w0.experts > 0 ? p.w0.experts : 1;
+  int64_t t64, t256, hint;
+  if (a.grouped) {
+    t64 = experts + p.n / 64 + 1;
+    t256 = experts + p.n / 256 + 1;
+    hint = (p.n + experts - 1) / experts;  // mean tokens per expert
+  } else {
+    t64 = (p.n + 63) / 64;
+    t256 = (p.n + 255) / 256;
+    hint = p.n;
+  }
+  // The 64-token tile re-reads weights once per 64 tokens; beyond that the
+  // 256-token tile's extra MMA width is cheaper.
+  const int64_t max_hint = a.grouped ? (hint <= 32 ? 64 : 65) : hint;
+#define TF_TC_EPI(E)                                                                              \
+  return p.act == TF_DTYPE_F16 ? launch_tc_epi<__half, E>(a, max_hint, t64, t256, s)              \
+                               : launch_tc_epi<__nv_bfloat16, E>(a, max_hint, t64, t256, s);
+  switch (p.epilogue) {
+    case EPI_PLAIN: TF_TC_EPI(EPI_PLAIN)
+    case EPI_SWIGLU: TF_TC_EPI(EPI_SWIGLU)
+    case EPI_RESIDUAL: TF_TC_EPI(EPI_RESIDUAL)
+    default: TF_TC_EPI(EPI_F32)
+  }
+#undef TF_TC_EPI
+}
+
+int read_tc_error(bool clear) {
+  int v = 0;
+  cudaMemcpyFromSymbol(&v, g_tc_error, sizeof(int));
+  if (clear) {
+    const int z = 0;
+    cudaMemcpyToSymbol(g_tc_error, &z, sizeof(int));
+  }
+  return v;
+}
+
+}  // namespace tf

@@ -337,3 +337,13 @@ def attention_decode(qkv: Tensor, q_norm: Tensor, k_norm: Tensor, positions: Ten
                                     rope_theta, _ptr(pos), max_length, _ptr(k_cache), _ptr(v_cache), cap,
                                     scale, _act(qkv), _ptr(out), _ptr(ws), nb.value, _stream()))
     return out
+
+
+def set_qmm_path(path: int):
+    """0 = automatic, 1 = CUDA-core GEMV only, 2 = tensor cores when eligible."""
+    check(lib().tf_set_qmm_path(int(path)))
+
+
+def device_error(clear: bool = True) -> int:
+    """First error code recorded by a device-side bounded wait (0 = none)."""
+    return lib().tf_device_error(int(clear))
