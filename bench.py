@@ -120,12 +120,12 @@ class ClockSampler:
                 "samples": len(sm)}
 
 
-def build_model(B, L, cap, device):
+def build_model(B, L, cap, device, layers=16):
     import torch
 
     from trifuse_b200.model import Config, Model, Session
     from trifuse_b200.quant import synthetic_olmoe
-    cfg = Config(capacity=cap)
+    cfg = Config(capacity=cap, layers=layers)
     w = synthetic_olmoe(cfg, seed=20260102, device=f"cuda:{device}")
     model = Model(cfg, w, device=device)
     del w
@@ -245,6 +245,9 @@ def main():
     ap.add_argument("--batch", type=int, default=64)
     ap.add_argument("--kv-len", type=int, default=4096)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--layers", type=int, default=16, help="model depth (profiling small cases)")
+    ap.add_argument("--ncu", action="store_true",
+                    help="profiling run: warm up, then one decode step between cudaProfilerStart/Stop")
     args = ap.parse_args()
     rank, local_rank, world = env_rank()
     if args.impl == "reference":
@@ -268,13 +271,28 @@ def main():
 
     B, L = args.batch, args.kv_len
     cap = L + 2 * (args.warmup + args.steps) + 8
-    cfg, model, sess = build_model(B, L, cap, local_rank)
+    cfg, model, sess = build_model(B, L, cap, local_rank, args.layers)
     stream = torch.cuda.current_stream()
     g = torch.Generator(device="cuda")
     g.manual_seed(20260104 + rank)
     n_ids = args.warmup + args.steps
     ids = torch.randint(0, cfg.vocab, (n_ids, B), device="cuda", generator=g, dtype=torch.int64)
     logits = torch.empty((B, cfg.vocab), dtype=torch.float32, device="cuda")
+
+    if args.ncu:
+        sess.set_lengths([L] * B)
+        for i in range(args.warmup):
+            sess.decode(ids[i], logits=logits)
+        torch.cuda.synchronize()
+        torch.cuda.profiler.start()
+        sess.decode(ids[args.warmup], logits=logits)
+        torch.cuda.synchronize()
+        torch.cuda.profiler.stop()
+        if rank == 0:
+            print(json.dumps({"ncu_step": True, "batch": B, "kv_len": L, "layers": args.layers}))
+        sess.close()
+        model.close()
+        return
 
     uuid = None
     try:
