@@ -213,7 +213,8 @@ int tf_moe_forward(const tf_moe_args* args, void* workspace, size_t workspace_by
  * promise that expert_ids never decrease.  n == 0 is allowed.
  * Replaces NativeMoEExpertHook::GPUCallable (overlays/executorch/backends/mlx/
  * runtime/MLXMoEExpertHook.h:25-32; body MLXNativeGraniteMoEPrefill.h:635-658). */
-int tf_moe_expert_workspace_size(int64_t n, int32_t intermediate, int32_t experts, size_t* bytes);
+int tf_moe_expert_workspace_size(int64_t n, int64_t x_rows, int32_t hidden, int32_t intermediate,
+                                 int32_t experts, int act, size_t* bytes);
 int tf_moe_expert_gpu(const void* x, int64_t x_rows, int32_t hidden, const int32_t* token_indices,
                       const int32_t* expert_ids, int64_t n, int experts_sorted,
                       int32_t intermediate, int32_t experts, const tf_affine_weight* gate_proj,

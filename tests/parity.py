@@ -2,7 +2,14 @@
 
 The bar for floating-point outputs is max-abs 2e-2 and mean relative 5e-3,
 with fp32 accumulation; the relative error is averaged over elements whose
-reference magnitude is at least 1e-2 (smaller ones are covered by max-abs)."""
+reference magnitude is at least 1e-2 (smaller ones are covered by max-abs).
+
+Layer outputs that include the residual stream (out = act(residual + moe))
+use ``ulp_act``: there max-abs may also reach one unit in the last place of
+the activation dtype at the reference value's magnitude.  Both sides round
+the same fp32 sum to bf16/f16, and at |out| >= 4 one bf16 ulp is 3.1e-2, so
+any accumulation-order difference flips a final rounding by exactly one ulp.
+The MoE contribution itself (residual = 0) always meets the plain bar."""
 import numpy as np
 
 MAX_ABS = 2e-2
@@ -19,11 +26,24 @@ def errors(got, ref):
     return float(diff.max()) if diff.size else 0.0, rel
 
 
-def assert_close(got, ref, act=None, max_abs=MAX_ABS, mean_rel=MEAN_REL):
+def act_ulp(ref, act):
+    """One unit in the last place of `act` (f16 / bf16) at |ref|."""
+    mant = {"f16": 10, "bf16": 7}[act]
+    mag = np.maximum(np.abs(np.asarray(ref, np.float64)), 2.0 ** -14)
+    return np.exp2(np.floor(np.log2(mag)) - mant)
+
+
+def assert_close(got, ref, act=None, max_abs=MAX_ABS, mean_rel=MEAN_REL, ulp_act=None):
     got = np.asarray(got, np.float64)
     ref = np.asarray(ref, np.float64)
     assert np.array_equal(np.isnan(got), np.isnan(ref)), "NaN pattern differs"
     m = ~np.isnan(ref)
     mx, rel = errors(got[m], ref[m])
+    if ulp_act is not None:
+        bound = np.maximum(max_abs, act_ulp(ref[m], ulp_act))
+        over = np.abs(got[m] - ref[m]) > bound
+        assert not over.any() and rel <= mean_rel, (
+            f"max_abs={mx:.3e} ({int(over.sum())} above max(2e-2, 1 ulp)) mean_rel={rel:.3e}")
+        return mx, rel
     assert mx <= max_abs and rel <= mean_rel, f"max_abs={mx:.3e} mean_rel={rel:.3e}"
     return mx, rel

@@ -100,18 +100,20 @@ def test_session_admission_rules(tiny):
     assert torch.isfinite(out).all()
 
 
-def test_full_geometry_layer_tensor_core_path():
+@pytest.mark.parametrize("act", ["f16", "bf16"])
+def test_full_geometry_layer_tensor_core_path(act):
     """One layer at OLMoE-1B-7B geometry (H=2048, 16 heads, E=64, K=8,
     I=1024; vocab cut to 4096): prefill rows and a 40-request decode batch
     run the tensor-core QMMs; logits match the oracle."""
     from trifuse_b200.model import Config, Model, Session
     from trifuse_b200.quant import synthetic_olmoe
-    cfg = Config(layers=1, vocab=4096, capacity=64)
+    tdt = torch.float16 if act == "f16" else torch.bfloat16
+    cfg = Config(layers=1, vocab=4096, capacity=64, act=tdt)
     w = synthetic_olmoe(cfg, seed=11, device="cuda")
     model = Model(cfg, w)
     sess = Session(model, max_batch=40, capacity=64, max_prefill_tokens=64)
     ow = oracle_weights(w, cfg)
-    ocfg = oracle.OLMoEConfig(layers=1, vocab=4096, capacity=64, act="f16")
+    ocfg = oracle.OLMoEConfig(layers=1, vocab=4096, capacity=64, act=act)
     rng = np.random.default_rng(3)
     B = 40
     prompts = [rng.integers(0, cfg.vocab, size=n) for n in (20, 12)]
@@ -119,15 +121,15 @@ def test_full_geometry_layer_tensor_core_path():
     lg = host(sess.prefill([0, 1], prompts))
     for r in range(2):
         ref = oracle.model_forward(prompts[r], ow, ocfg, caches[r][0], caches[r][1], 0)
-        assert_close(lg[r], ref)
+        assert_close(lg[r], ref, ulp_act=act)
     lengths = [20, 12] + [0] * (B - 2)
     toks = rng.integers(0, cfg.vocab, size=B)
     lg = host(sess.decode(torch.tensor(toks, dtype=torch.int64, device="cuda")))
-    h = oracle.affine_embedding(toks, *ow["embed"], "f16")
+    h = oracle.affine_embedding(toks, *ow["embed"], act)
     out = oracle.decode_layer_batched(h, ow["layers"][0], ocfg, [c[0][0] for c in caches],
                                       [c[1][0] for c in caches], lengths)
-    ref = oracle.affine_qmm(oracle.rms_norm(out, ow["final_norm"], ocfg.rms_eps, "f16"), *ow["lm_head"], "f16")
-    assert_close(lg, ref)
+    ref = oracle.affine_qmm(oracle.rms_norm(out, ow["final_norm"], ocfg.rms_eps, act), *ow["lm_head"], act)
+    assert_close(lg, ref, ulp_act=act)
     from trifuse_b200 import ops
     assert ops.device_error() == 0
     sess.close()

@@ -58,13 +58,17 @@ def test_moe_tensor_core_against_oracle(ops, act, T, skew):
         wr *= (1 + np.abs(rng.standard_normal((E, 1)).astype(np.float32)) * 3)
     w = oracle.to_act(wr, act)
     d = experts_dev(ex)
+    zero = np.zeros_like(res)
     with path(ops, 2):
         out, aux = ops.moe(dev(x, act), dev(res, act), dev(w, act), d["gate"], d["up"], d["down"], K,
                            return_aux=True)
+        moe_only = ops.moe(dev(x, act), dev(zero, act), dev(w, act), d["gate"], d["up"], d["down"], K)
     assert ops.device_error() == 0
     ref, raux = oracle.moe_block(x, res, ("dense", w), ex, K, act)
+    ref0, _ = oracle.moe_block(x, zero, ("dense", w), ex, K, act)
     assert np.array_equal(host(aux["indices"]), raux["indices"])
-    assert_close(host(out), ref)
+    assert_close(host(moe_only), ref0)            # the gather_qmm path's own output
+    assert_close(host(out), ref, ulp_act=act)     # with the residual stream
 
 
 def test_expert_hook_tensor_core(ops):

@@ -315,6 +315,8 @@ struct MoePlan {
   size_t sort_ws_bytes;
   void* h;
   void* y;
+  void* x16;  // f16 operand copies for the tensor-core path with bf16 activations
+  void* h16;
   size_t used;
 };
 
@@ -335,6 +337,9 @@ static MoePlan plan_moe(const tf_moe_args* a, void* ws, size_t ws_bytes) {
   p.sort_ws = c.take<char>(p.sort_ws_bytes);
   p.h = c.take<char>((size_t)N * a->intermediate * ab);
   p.y = c.take<char>((size_t)N * a->hidden * ab);
+  const bool bf = a->act == TF_DTYPE_BF16;
+  p.x16 = bf ? c.take<char>((size_t)T * a->hidden * 2) : nullptr;
+  p.h16 = bf ? c.take<char>((size_t)N * a->intermediate * 2) : nullptr;
   p.used = c.used;
   return p;
 }
@@ -389,9 +394,6 @@ static tf_status run_moe(const tf_moe_args* a, const MoePlan& p, cudaStream_t s)
   up.w1 = a->up_proj;
   up.y = p.h;
   up.y_stride = a->intermediate;
-  trace(PH_GATE_UP, true, s);
-  TF_TRY(launch_qmm(up, s));
-  trace(PH_GATE_UP, false, s);
   QmmProblem dn = up;
   dn.epilogue = EPI_PLAIN;
   dn.x = p.h;
@@ -402,6 +404,22 @@ static tf_status run_moe(const tf_moe_args* a, const MoePlan& p, cudaStream_t s)
   dn.w0 = a->down_proj;
   dn.y = p.y;
   dn.y_stride = a->hidden;
+  const bool tc_up = qmm_uses_tc(up), tc_dn = qmm_uses_tc(dn);
+  if (a->act == TF_DTYPE_BF16 && tc_up) {
+    TF_TRY(launch_bf16_to_f16(a->x, a->tokens * a->hidden, p.x16, s));
+    up.x16 = p.x16;
+    if (tc_dn) {  // h goes straight to the next tensor-core QMM in f16 storage
+      up.y_f16 = 1;
+      dn.x16 = p.h;
+    }
+  }
+  trace(PH_GATE_UP, true, s);
+  TF_TRY(launch_qmm(up, s));
+  trace(PH_GATE_UP, false, s);
+  if (a->act == TF_DTYPE_BF16 && tc_dn && !up.y_f16) {
+    TF_TRY(launch_bf16_to_f16(p.h, N * a->intermediate, p.h16, s));
+    dn.x16 = p.h16;
+  }
   trace(PH_DOWN, true, s);
   TF_TRY(launch_qmm(dn, s));
   trace(PH_DOWN, false, s);
@@ -446,22 +464,37 @@ int tf_moe_forward(const tf_moe_args* args, void* workspace, size_t workspace_by
 
 // ---------------------------------------------------------------- expert hook
 
-static size_t expert_ws(int64_t n, int32_t intermediate, int32_t experts, int ab) {
-  Carve c(nullptr, 0);
-  c.take<int32_t>((size_t)n * 4);  // order
-  c.take<int32_t>((size_t)n * 4);  // x rows
-  c.take<int32_t>((size_t)(experts + 1) * 4);
-  c.take<int32_t>((size_t)experts * 4);
-  c.take<int32_t>(4);
-  c.take<char>(sort_workspace_bytes(n, experts));
-  c.take<char>((size_t)n * intermediate * ab);
-  return c.used;
+struct ExpertPlan {
+  int32_t *order, *xrow, *offsets, *active, *active_count;
+  void *sws, *h, *x16, *h16;
+  size_t sws_bytes, used;
+};
+
+static ExpertPlan plan_expert(void* ws, size_t ws_bytes, int64_t n, int64_t x_rows, int32_t hidden,
+                              int32_t intermediate, int32_t experts, int act) {
+  Carve c(ws, ws_bytes);
+  ExpertPlan p;
+  p.order = c.take<int32_t>((size_t)n * 4);
+  p.xrow = c.take<int32_t>((size_t)n * 4);
+  p.offsets = c.take<int32_t>((size_t)(experts + 1) * 4);
+  p.active = c.take<int32_t>((size_t)experts * 4);
+  p.active_count = c.take<int32_t>(4);
+  p.sws_bytes = sort_workspace_bytes(n, experts);
+  p.sws = c.take<char>(p.sws_bytes);
+  p.h = c.take<char>((size_t)n * intermediate * act_bytes(act));
+  const bool bf = act == TF_DTYPE_BF16;
+  p.x16 = bf ? c.take<char>((size_t)x_rows * hidden * 2) : nullptr;
+  p.h16 = bf ? c.take<char>((size_t)n * intermediate * 2) : nullptr;
+  p.used = c.used;
+  return p;
 }
 
-int tf_moe_expert_workspace_size(int64_t n, int32_t intermediate, int32_t experts, size_t* bytes) {
-  if (!bytes || n < 0 || intermediate <= 0 || experts <= 0)
+int tf_moe_expert_workspace_size(int64_t n, int64_t x_rows, int32_t hidden, int32_t intermediate,
+                                 int32_t experts, int act, size_t* bytes) {
+  if (!bytes || n < 0 || x_rows < 0 || hidden <= 0 || intermediate <= 0 || experts <= 0)
     return set_error(TF_ERR_INVALID_ARGUMENT, "bad arguments");
-  *bytes = expert_ws(n, intermediate, experts, 2);
+  TF_TRY(check_act(act));
+  *bytes = plan_expert(nullptr, 0, n, x_rows, hidden, intermediate, experts, act).used;
   return TF_OK;
 }
 
@@ -482,23 +515,21 @@ int tf_moe_expert_gpu(const void* x, int64_t x_rows, int32_t hidden, const int32
       down->in_features != intermediate || gate->experts != experts || up->experts != experts ||
       down->experts != experts)
     return set_error(TF_ERR_SHAPE, "expert hook: packed parameter geometry differs");
-  if (workspace_bytes < expert_ws(n, intermediate, experts, act_bytes(act)))
+  if (workspace_bytes < plan_expert(nullptr, 0, n, x_rows, hidden, intermediate, experts, act).used)
     return set_error(TF_ERR_INVALID_ARGUMENT, "expert hook: workspace too small");
   if (n == 0) return TF_OK;
   if (!x || !token_indices || !expert_ids || !out_sorted || !inverse || !aligned16(x))
     return set_error(TF_ERR_INVALID_ARGUMENT, "expert hook: NULL or unaligned pointer");
   cudaStream_t s = st(stream);
-  Carve c(workspace, workspace_bytes);
-  int32_t* order = c.take<int32_t>((size_t)n * 4);
-  int32_t* xrow = c.take<int32_t>((size_t)n * 4);
-  int32_t* offsets = c.take<int32_t>((size_t)(experts + 1) * 4);
-  int32_t* active = c.take<int32_t>((size_t)experts * 4);
-  int32_t* active_count = c.take<int32_t>(4);
-  const size_t sb = sort_workspace_bytes(n, experts);
-  void* sws = c.take<char>(sb);
-  void* h = c.take<char>((size_t)n * intermediate * act_bytes(act));
-  TF_TRY(launch_route_sort(expert_ids, n, experts, order, inverse, offsets, active, active_count, sws,
-                           sb, s));
+  const ExpertPlan w = plan_expert(workspace, workspace_bytes, n, x_rows, hidden, intermediate, experts, act);
+  int32_t* order = w.order;
+  int32_t* xrow = w.xrow;
+  int32_t* offsets = w.offsets;
+  int32_t* active = w.active;
+  int32_t* active_count = w.active_count;
+  void* h = w.h;
+  TF_TRY(launch_route_sort(expert_ids, n, experts, order, inverse, offsets, active, active_count, w.sws,
+                           w.sws_bytes, s));
   TF_TRY(launch_gather_index(token_indices, order, n, 1, xrow, s));
   QmmProblem p;
   p.mode = QMM_GROUPED;
@@ -515,7 +546,6 @@ int tf_moe_expert_gpu(const void* x, int64_t x_rows, int32_t hidden, const int32
   p.w1 = *up;
   p.y = h;
   p.y_stride = intermediate;
-  TF_TRY(launch_qmm(p, s));
   QmmProblem d = p;
   d.epilogue = EPI_PLAIN;
   d.x = h;
@@ -524,6 +554,20 @@ int tf_moe_expert_gpu(const void* x, int64_t x_rows, int32_t hidden, const int32
   d.w0 = *down;
   d.y = out_sorted;
   d.y_stride = hidden;
+  const bool tc_up = qmm_uses_tc(p), tc_dn = qmm_uses_tc(d);
+  if (act == TF_DTYPE_BF16 && tc_up) {
+    TF_TRY(launch_bf16_to_f16(x, x_rows * hidden, w.x16, s));
+    p.x16 = w.x16;
+    if (tc_dn) {
+      p.y_f16 = 1;
+      d.x16 = h;
+    }
+  }
+  TF_TRY(launch_qmm(p, s));
+  if (act == TF_DTYPE_BF16 && tc_dn && !p.y_f16) {
+    TF_TRY(launch_bf16_to_f16(h, n * intermediate, w.h16, s));
+    d.x16 = w.h16;
+  }
   return launch_qmm(d, s);
 }
 

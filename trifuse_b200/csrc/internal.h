@@ -128,7 +128,14 @@ struct QmmProblem {
   int64_t y_stride = 0;
   const void* residual = nullptr;  // EPI_RESIDUAL, indexed like y
   int64_t residual_stride = 0;
+  // Tensor-core path with bf16 activations: f16 copy of x (same rows and
+  // stride), and for EPI_SWIGLU whether y is written in f16 storage.
+  const void* x16 = nullptr;
+  int y_f16 = 0;
 };
+// Path launch_qmm would take for this problem (true = tensor cores).
+bool qmm_uses_tc(const QmmProblem& p);
+tf_status launch_bf16_to_f16(const void* x, int64_t n, void* y, cudaStream_t s);
 // Dispatches to the tensor-core kernel (launch_qmm_tc) when the problem has
 // enough tokens per weight matrix, else to the CUDA-core GEMV.
 tf_status launch_qmm(const QmmProblem& p, cudaStream_t s);

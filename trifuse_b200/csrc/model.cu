@@ -138,6 +138,7 @@ struct tf_session {
   void* xn = nullptr;
   void* qkv = nullptr;
   void* attn = nullptr;
+  void* x16 = nullptr;  // f16 operand copy (bf16 models, tensor-core projections)
   int64_t* ids = nullptr;
   int32_t* pos = nullptr;
   int32_t* req = nullptr;
@@ -362,6 +363,7 @@ int tf_session_create(tf_model* model, int32_t max_batch, int32_t capacity, int3
     s->xn = k.take<char>((size_t)R * H * 2);
     s->qkv = k.take<char>((size_t)R * (W + 2 * Wkv) * 2);
     s->attn = k.take<char>((size_t)R * W * 2);
+    s->x16 = k.take<char>((size_t)R * (H > W ? H : W) * 2);
     s->ids = k.take<int64_t>((size_t)R * 8);
     s->pos = k.take<int32_t>((size_t)R * 4);
     s->req = k.take<int32_t>((size_t)R * 4);
@@ -447,6 +449,16 @@ int tf_session_reset(tf_session* s) {
 
 namespace {
 
+// Dense projection; with bf16 activations on the tensor-core path the input
+// rows are first copied to f16 (the MMA operand dtype).
+tf_status dense_qmm(tf_session* s, QmmProblem& q, int64_t x_rows, cudaStream_t st) {
+  if (q.act == TF_DTYPE_BF16 && qmm_uses_tc(q)) {
+    TF_TRY(launch_bf16_to_f16(q.x, x_rows * q.x_stride, s->x16, st));
+    q.x16 = s->x16;
+  }
+  return launch_qmm(q, st);
+}
+
 // Forward `rows` token rows through every layer.  Inputs already on device:
 // s->ids [rows], s->pos [rows], s->req [rows] (or identity when req_ident).
 // Leaves the final hidden states in s->h0.
@@ -474,7 +486,7 @@ tf_status forward_rows(tf_session* s, int64_t rows, bool req_ident, int max_len,
     q.y = s->qkv;
     q.y_stride = QKV;
     trace(PH_QKV, true, st);
-    TF_TRY(launch_qmm(q, st));
+    TF_TRY(dense_qmm(s, q, rows, st));
     trace(PH_QKV, false, st);
     AttnProblem a;
     a.qkv = s->qkv;
@@ -512,7 +524,7 @@ tf_status forward_rows(tf_session* s, int64_t rows, bool req_ident, int max_len,
     o.residual = s->h0;
     o.residual_stride = H;
     trace(PH_O_PROJ, true, st);
-    TF_TRY(launch_qmm(o, st));
+    TF_TRY(dense_qmm(s, o, rows, st));
     trace(PH_O_PROJ, false, st);
     trace(PH_POST_NORM, true, st);
     TF_TRY(launch_rms_norm(s->h1, rows, H, L.post_norm, c.rms_eps, c.act, s->xn, st));
@@ -555,7 +567,7 @@ tf_status head_rows(tf_session* s, int64_t rows, const int32_t* sel, int64_t n, 
   h.y = s->logits;
   h.y_stride = c.vocab;
   trace(PH_LM_HEAD, true, st);
-  TF_TRY(launch_qmm(h, st));
+  TF_TRY(dense_qmm(s, h, rows, st));
   trace(PH_LM_HEAD, false, st);
   return TF_OK;
 }

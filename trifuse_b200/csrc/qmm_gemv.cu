@@ -234,22 +234,20 @@ static tf_status qmm_by_mode(const GemvArgs& a, int mode, int epi, cudaStream_t 
 
 int g_qmm_path = 0;
 
-tf_status launch_qmm(const QmmProblem& p, cudaStream_t s) {
-  if (p.n == 0) return TF_OK;
+bool qmm_uses_tc(const QmmProblem& p) {
   const int in = p.w0.in_features;
   const bool tc_ok = p.mode != QMM_PER_ROUTE && in % 512 == 0 && in <= 8192;
-  if (tc_ok && g_qmm_path != 1) {
-    bool use_tc = g_qmm_path == 2;
-    if (!use_tc) {
-      if (p.mode == QMM_DENSE) {
-        use_tc = p.n >= 8;
-      } else {
-        const int experts = p.w0.experts > 0 ? p.w0.experts : 1;
-        use_tc = p.n >= 4 * (int64_t)experts;  // >= 4 tokens per expert on average
-      }
-    }
-    if (use_tc) return launch_qmm_tc(p, s);
-  }
+  if (!tc_ok || g_qmm_path == 1) return false;
+  if (g_qmm_path == 2) return true;
+  if (p.mode == QMM_DENSE) return p.n >= 8;
+  const int experts = p.w0.experts > 0 ? p.w0.experts : 1;
+  return p.n >= 4 * (int64_t)experts;  // >= 4 tokens per expert on average
+}
+
+tf_status launch_qmm(const QmmProblem& p, cudaStream_t s) {
+  if (p.n == 0) return TF_OK;
+  // bf16 activations reach the tensor cores only with their f16 copy.
+  if (qmm_uses_tc(p) && (p.act != TF_DTYPE_BF16 || p.x16)) return launch_qmm_tc(p, s);
   return launch_qmm_gemv(p, s);
 }
 

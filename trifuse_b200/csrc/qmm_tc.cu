@@ -7,10 +7,11 @@
 // MLXNativeGraniteMoEPrefill.h:539-550, 685-687) as D = W_e . X^T per expert:
 // the weight rows are the MMA's M side (128 rows per tile) and the expert's
 // tokens the N side (up to NMAX per tile), so a tile of few tokens still
-// fills the 128-row MMA.  Weights are dequantized once per tile and k-step
-// as fp16(code*s + b) / bf16(code*s + b) (fp32 FMA, one rounding; the
-// reference rounds the dequantized weight to its float16 scale dtype,
-// native_affine_ops.py:36) and accumulated in fp32 in TMEM.
+// fills the 128-row MMA.  The MMA always runs f16 x f16 -> f32: weights are
+// dequantized per tile and k-step to fp16(code*s + b) (fp32 FMA, one
+// rounding), the dtype the reference rounds its dequantized weight to (its
+// float16 scale dtype, native_affine_ops.py:36); bf16 activations arrive as
+// an f16 copy (exact for |x| in the f16 normal range, see convert kernel).
 //
 // Block roles (160 threads):
 //   warps 0-3  producers: thread r owns A row r.  Per k-step (64 inputs =
@@ -192,6 +193,7 @@ struct Args {
   int row_blocks;
   void* y;
   int64_t y_stride;
+  int y_f16;  // SWIGLU: store h in f16 (feeds the next tensor-core QMM)
   const void* residual;
   int64_t residual_stride;
 };
@@ -325,7 +327,7 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_tc_kernel(Args a) {
       cp_async16(my_s + g, sc + grow * groups + g, 16);
       cp_async16(my_b + g, bi + grow * groups + g, 16);
     }
-    const T* xb = static_cast<const T*>(a.x);
+    const __half* xb = static_cast<const __half*>(a.x);  // f16 operand copy of the activations
     auto issue = [&](int k) {
       uint8_t* st = stages + (size_t)(k % STAGES) * S::kStage;
       uint8_t* P = st + S::kA + S::kB;
@@ -364,10 +366,10 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_tc_kernel(Args a) {
       for (int ch = 0; ch < 8; ++ch) {
         const uint32_t w = words[ch];
         uint4 v;
-        v.x = pack2<T>(fmaf(code_f(w, 0), s, b), fmaf(code_f(w, 1), s, b));
-        v.y = pack2<T>(fmaf(code_f(w, 2), s, b), fmaf(code_f(w, 3), s, b));
-        v.z = pack2<T>(fmaf(code_f(w, 4), s, b), fmaf(code_f(w, 5), s, b));
-        v.w = pack2<T>(fmaf(code_f(w, 6), s, b), fmaf(code_f(w, 7), s, b));
+        v.x = pack2<__half>(fmaf(code_f(w, 0), s, b), fmaf(code_f(w, 1), s, b));
+        v.y = pack2<__half>(fmaf(code_f(w, 2), s, b), fmaf(code_f(w, 3), s, b));
+        v.z = pack2<__half>(fmaf(code_f(w, 4), s, b), fmaf(code_f(w, 5), s, b));
+        v.w = pack2<__half>(fmaf(code_f(w, 6), s, b), fmaf(code_f(w, 7), s, b));
         *reinterpret_cast<uint4*>(Arow + ((ch ^ (r & 7)) << 4)) = v;
       }
       fence_proxy_async();
@@ -413,8 +415,12 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_tc_kernel(Args a) {
                 const float g = round_act<T>(v[i]);
                 const float u = round_act<T>(xch[(size_t)r * NMAX + tok]);
                 const float sl = round_act<T>(g / (1.0f + expf(-g)));
-                T* yp = static_cast<T*>(a.y) + (int64_t)(s0 + tok) * a.y_stride + f;
-                *yp = from_f<T>(sl * u);
+                const int64_t at = (int64_t)(s0 + tok) * a.y_stride + f;
+                const float h = round_act<T>(sl * u);
+                if (a.y_f16)
+                  static_cast<__half*>(a.y)[at] = __float2half_rn(h);  // act value in f16 storage
+                else
+                  static_cast<T*>(a.y)[at] = from_f<T>(h);
               }
             }
           }
@@ -444,7 +450,7 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_tc_kernel(Args a) {
     }
   } else if (lane == 0) {
     // ---- MMA issuer
-    const uint32_t idesc = idesc_f16(Act<T>::kDtype == TF_DTYPE_BF16, kM, n_mma);
+    const uint32_t idesc = idesc_f16(false, kM, n_mma);  // f16 x f16 -> f32
     bool ok = true;
     int issued = 0;
     for (int k = 0; k < nk; ++k) {
@@ -482,11 +488,13 @@ template <typename T, int EPI, int NMAX, int STAGES>
 tf_status launch_tc_cfg(const tc::Args& a, int64_t token_tiles, cudaStream_t s) {
   using S = tc::Smem<NMAX, STAGES>;
   const size_t smem = S::bytes(a.in);
-  static bool attr_set = false;
-  if (!attr_set) {
+  // The opt-in size grows with the K extent (row scales live in smem); raise
+  // it whenever a launch needs more than any earlier one.
+  static size_t attr_bytes = 0;
+  if (smem > attr_bytes) {
     TF_CUDA(cudaFuncSetAttribute(tc::qmm_tc_kernel<T, EPI, NMAX, STAGES>,
                                  cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    attr_set = true;
+    attr_bytes = smem;
   }
   const int64_t grid = token_tiles * a.row_blocks;
   if (grid <= 0) return TF_OK;
@@ -516,8 +524,11 @@ tf_status launch_qmm_tc(const QmmProblem& p, cudaStream_t s) {
   if (p.mode == QMM_PER_ROUTE) return set_error(TF_ERR_UNSUPPORTED, "qmm_tc: per-route mode");
   const int in = p.w0.in_features;
   if (in % 64 || in > 8192) return set_error(TF_ERR_UNSUPPORTED, "qmm_tc: in_features %d", in);
+  if (p.act == TF_DTYPE_BF16 && !p.x16)
+    return set_error(TF_ERR_STATE, "qmm_tc: bf16 activations need their f16 operand copy");
   tc::Args a;
-  a.x = p.x;
+  a.x = p.act == TF_DTYPE_BF16 ? p.x16 : p.x;
+  a.y_f16 = p.y_f16;
   a.x_stride = p.x_stride;
   a.x_index = p.x_index;
   a.x_div = p.x_div;
@@ -565,6 +576,29 @@ tf_status launch_qmm_tc(const QmmProblem& p, cudaStream_t s) {
     default: TF_TC_EPI(EPI_F32)
   }
 #undef TF_TC_EPI
+}
+
+// bf16 -> f16 operand copy for the tensor-core QMM.  Exact for |x| in
+// [2^-14, 65504] (bf16's 8-bit significand fits f16's 11 bits); values
+// beyond the f16 range would become inf, so they record error code 5.
+__global__ void bf16_to_f16_kernel(const __nv_bfloat16* __restrict__ x, int64_t n8, __half* __restrict__ y) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n8) return;
+  float f[8];
+  unpack8<__nv_bfloat16>(ld_v4(x + 8 * i), f);
+  bool bad = false;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) bad |= fabsf(f[j]) > 65504.f;
+  if (bad) atomicCAS(&g_tc_error, 0, 5);
+  *reinterpret_cast<uint4*>(y + 8 * i) = pack8<__half>(f);
+}
+
+tf_status launch_bf16_to_f16(const void* x, int64_t n, void* y, cudaStream_t s) {
+  if (n == 0) return TF_OK;
+  if (n % 8) return set_error(TF_ERR_SHAPE, "bf16_to_f16: count %lld not a multiple of 8", (long long)n);
+  const int64_t n8 = n / 8;
+  bf16_to_f16_kernel<<<(unsigned)((n8 + 255) / 256), 256, 0, s>>>((const __nv_bfloat16*)x, n8, (__half*)y);
+  return check_launch("bf16_to_f16");
 }
 
 int read_tc_error(bool clear) {

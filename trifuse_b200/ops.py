@@ -294,7 +294,8 @@ def expert_gpu(x: Tensor, token_indices: Tensor, expert_ids: Tensor, experts_sor
     out = torch.empty((n, H), dtype=x.dtype, device=x.device)
     inverse = torch.empty(n, dtype=torch.int32, device=x.device)
     nb = C.c_size_t()
-    check(lib().tf_moe_expert_workspace_size(n, g.out_features, g.experts, C.byref(nb)))
+    check(lib().tf_moe_expert_workspace_size(n, xc.shape[0], H, g.out_features, g.experts, _act(x),
+                                             C.byref(nb)))
     ws = _ws(nb.value, x.device)
     check(lib().tf_moe_expert_gpu(_ptr(xc), xc.shape[0], H, _ptr(token_indices), _ptr(expert_ids), n,
                                   int(experts_sorted), g.out_features, g.experts, C.byref(g), C.byref(u),
