@@ -206,6 +206,22 @@ int tf_moe_workspace_size(const tf_moe_args* args, size_t* bytes);
 int tf_moe_forward(const tf_moe_args* args, void* workspace, size_t workspace_bytes,
                    void* stream);
 
+/* The MoE block for callers that cannot allocate device memory while it runs
+ * (a host framework's execute callback with a pre-planned memory arena, or a
+ * serving loop where cudaMalloc/cudaFree would synchronize the device):
+ * same computation and arguments as tf_moe_forward, but no workspace
+ * argument and no allocation of any kind.  Its scratch is one fixed
+ * TF_MOE_NOALLOC_SCRATCH_BYTES buffer built into this library, held on every
+ * GPU that loads it.  Calls with more than TF_MOE_NOALLOC_MAX_TOKENS tokens,
+ * or whose scratch would exceed the buffer (it fits 64 tokens at
+ * OLMoE-1B-7B geometry), return TF_ERR_CAPACITY.  The first call on a device looks up the
+ * buffer's device address, so make it before any stream capture.  All calls
+ * share the buffer: calls that overlap on the GPU race and must be
+ * serialized.  No counterpart in the reference. */
+#define TF_MOE_NOALLOC_SCRATCH_BYTES ((size_t)6 << 20)
+#define TF_MOE_NOALLOC_MAX_TOKENS 64
+int tf_moe_forward_noalloc(const tf_moe_args* args, void* stream);
+
 /* The expert hook's GPU callable (workspace): for parallel route vectors
  * (token_indices[n], expert_ids[n]) return out_sorted [n][hidden], the expert
  * outputs in expert-sorted order, and inverse [n] so that

@@ -70,6 +70,7 @@ SIGNATURES = {
     "tf_moe_route_sort": [P, I64, I32, I32, P, P, P, P, SZ, P],
     "tf_moe_workspace_size": [C.POINTER(MoeArgs), PSZ],
     "tf_moe_forward": [C.POINTER(MoeArgs), P, SZ, P],
+    "tf_moe_forward_noalloc": [C.POINTER(MoeArgs), P],
     "tf_moe_expert_workspace_size": [I64, I64, I32, I32, I32, C.c_int, PSZ],
     "tf_moe_expert_gpu": [P, I64, I32, P, P, I64, C.c_int, I32, I32, C.POINTER(AffineWeight),
                           C.POINTER(AffineWeight), C.POINTER(AffineWeight), C.c_int, P, P, P, SZ, P],
