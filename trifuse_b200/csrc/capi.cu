@@ -260,7 +260,7 @@ int tf_olmoe_router(const void* x, int64_t tokens, int32_t hidden, const tf_rout
   TF_TRY(check_act(act));
   TF_TRY(check_route(tokens, experts, k));
   TF_TRY(check_router(router, hidden, experts));
-  if (hidden % 256 || hidden > 4096) return set_error(TF_ERR_SHAPE, "router: hidden must be a multiple of 256 <= 4096");
+  if (hidden % 256 || hidden > 2048) return set_error(TF_ERR_SHAPE, "router: hidden must be a multiple of 256 <= 2048");
   if (tokens && (!x || !aligned16(x) || !indices || !gates))
     return set_error(TF_ERR_INVALID_ARGUMENT, "router: NULL or unaligned pointer");
   return launch_router(x, tokens, hidden, *router, experts, k, act, logits, indices, gates, st(stream));
@@ -348,7 +348,7 @@ static tf_status check_moe(const tf_moe_args* a) {
   if (!a) return set_error(TF_ERR_INVALID_ARGUMENT, "moe: args is NULL");
   TF_TRY(check_act(a->act));
   TF_TRY(check_route(a->tokens, a->experts, a->top_k));
-  if (a->hidden % 256 || a->hidden > 4096 || a->intermediate % 64 || a->intermediate <= 0)
+  if (a->hidden % 256 || a->hidden > 2048 || a->intermediate % 64 || a->intermediate <= 0)
     return set_error(TF_ERR_SHAPE, "moe: unsupported hidden/intermediate geometry");
   TF_TRY(check_router(&a->router, a->hidden, a->experts));
   TF_TRY(check_affine(&a->gate_proj, "gate_proj", true));

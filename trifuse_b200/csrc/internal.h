@@ -132,7 +132,13 @@ struct QmmProblem {
   // stride), and for EPI_SWIGLU whether y is written in f16 storage.
   const void* x16 = nullptr;
   int y_f16 = 0;
+  // Optional split-K workspace for dense tensor-core problems with few tiles
+  // (fp32 partials, then 1024 int counters at its end that must be zero
+  // before first use; each launch leaves them zero again).
+  void* splitk_ws = nullptr;
+  size_t splitk_bytes = 0;
 };
+constexpr size_t kSplitKWorkspaceBytes = (size_t)16 << 20;
 // Path launch_qmm would take for this problem (true = tensor cores).
 bool qmm_uses_tc(const QmmProblem& p);
 tf_status launch_bf16_to_f16(const void* x, int64_t n, void* y, cudaStream_t s);

@@ -139,6 +139,7 @@ struct tf_session {
   void* qkv = nullptr;
   void* attn = nullptr;
   void* x16 = nullptr;  // f16 operand copy (bf16 models, tensor-core projections)
+  void* splitk = nullptr;  // split-K partials + counters for the dense projections
   int64_t* ids = nullptr;
   int32_t* pos = nullptr;
   int32_t* req = nullptr;
@@ -184,7 +185,7 @@ tf_status validate_config(const tf_olmoe_config* c) {
     return set_error(TF_ERR_UNSUPPORTED, "grouped-query attention is not on this path (kv_heads %d != heads %d)",
                      c->kv_heads, c->heads);
   if (c->head_dim != 128) return set_error(TF_ERR_UNSUPPORTED, "head_dim %d (only 128)", c->head_dim);
-  if (c->hidden % 256 || c->hidden > 4096) return set_error(TF_ERR_UNSUPPORTED, "hidden %d", c->hidden);
+  if (c->hidden % 256 || c->hidden > 2048) return set_error(TF_ERR_UNSUPPORTED, "hidden %d (router supports <= 2048)", c->hidden);
   if (c->experts > 64 || c->top_k > 32) return set_error(TF_ERR_UNSUPPORTED, "experts <= 64, top_k <= 32");
   if (!act_ok(c->act)) return set_error(TF_ERR_INVALID_ARGUMENT, "activation dtype must be f16 or bf16");
   return TF_OK;
@@ -364,6 +365,7 @@ int tf_session_create(tf_model* model, int32_t max_batch, int32_t capacity, int3
     s->qkv = k.take<char>((size_t)R * (W + 2 * Wkv) * 2);
     s->attn = k.take<char>((size_t)R * W * 2);
     s->x16 = k.take<char>((size_t)R * (H > W ? H : W) * 2);
+    s->splitk = k.take<char>(kSplitKWorkspaceBytes);
     s->ids = k.take<int64_t>((size_t)R * 8);
     s->pos = k.take<int32_t>((size_t)R * 4);
     s->req = k.take<int32_t>((size_t)R * 4);
@@ -388,6 +390,14 @@ int tf_session_create(tf_model* model, int32_t max_batch, int32_t capacity, int3
   }
   Carve real(s->scratch, cv.used);
   plan(real);
+  // Split-K tile counters start at zero; every launch leaves them zero.
+  e = cudaMemset(s->splitk, 0, kSplitKWorkspaceBytes);
+  if (e != cudaSuccess) {
+    cudaFree(s->kv);
+    cudaFree(s->scratch);
+    delete s;
+    return set_error(TF_ERR_CUDA, "session scratch init: %s", cudaGetErrorString(e));
+  }
   for (int l = 0; l < c.layers; ++l) {
     s->k.push_back(s->kv + per_cache * (2 * l));
     s->v.push_back(s->kv + per_cache * (2 * l + 1));
@@ -452,6 +462,8 @@ namespace {
 // Dense projection; with bf16 activations on the tensor-core path the input
 // rows are first copied to f16 (the MMA operand dtype).
 tf_status dense_qmm(tf_session* s, QmmProblem& q, int64_t x_rows, cudaStream_t st) {
+  q.splitk_ws = s->splitk;
+  q.splitk_bytes = kSplitKWorkspaceBytes;
   if (q.act == TF_DTYPE_BF16 && qmm_uses_tc(q)) {
     TF_TRY(launch_bf16_to_f16(q.x, x_rows * q.x_stride, s->x16, st));
     q.x16 = s->x16;

@@ -20,8 +20,10 @@
 //              rows (the B tile, gathered by route order), then dequantizes
 //              its row into the 128B-swizzled K-major A tile;
 //              afterwards the same warps are the epilogue (tcgen05.ld).
+//              Packed codes are prefetched PK-1 k-steps ahead and activation
+//              tiles SB-2 ahead, so HBM and L2 latency overlap the dequant.
 //   warp 4     allocates TMEM; lane 0 issues tcgen05.mma (4 x K=16 per
-//              k-step) and tcgen05.commit to release stages.
+//              k-step) and tcgen05.commit to release the A and B slots.
 // Stages are guarded by mbarriers; every wait is bounded (about one second
 // of SM clock) and on expiry records an error code instead of hanging.
 #include <stdio.h>
@@ -194,48 +196,59 @@ struct Args {
   void* y;
   int64_t y_stride;
   int y_f16;  // SWIGLU: store h in f16 (feeds the next tensor-core QMM)
+  int ksplit;       // K splits per tile (1 = none)
+  float* partials;  // split-K: [tiles][ksplit][nt][128] fp32
+  int* counters;    // split-K: [tiles], zero between launches
   const void* residual;
   int64_t residual_stride;
 };
 
-template <int NMAX, int STAGES>
+// Three rings: SA dequantized A tiles (the MMA's A operand), SB activation
+// tiles (its B operand, filled by cp.async), PK packed-code tiles (cp.async,
+// read back by the thread that loaded them).  Layout after a 1 KB barrier
+// block: token rows, row scales/biases, then the rings (1024-aligned).
+template <int NMAX, int SA, int SB, int PK>
 struct Smem {
-  static constexpr int kA = kM * 128;         // 16 KB, bf16/f16 tile
-  static constexpr int kB = NMAX * 128;       // token tile
-  static constexpr int kP = kM * 32;          // packed codes of the tile
-  static constexpr int kStage = kA + kB + kP;
-  static size_t bytes(int in) {
-    // [barriers 1 KB][rows NMAX*4][scales+biases kM*(in/64)*4][pad to 1024][stages]
-    size_t head = 1024 + NMAX * 4 + (size_t)kM * (in / 64) * 4;
-    head = (head + 1023) / 1024 * 1024;
-    return head + (size_t)STAGES * kStage + 1024;  // +1024 for base alignment
+  static constexpr int kA = kM * 128;    // 16 KB f16 A tile
+  static constexpr int kB = NMAX * 128;  // token tile
+  static constexpr int kP = kM * 32;     // packed codes of one k-step
+  __host__ __device__ static size_t head(int in) {
+    const size_t h = 1024 + NMAX * 4 + (size_t)kM * (in / 64) * 4;
+    return (h + 1023) / 1024 * 1024;
   }
+  static size_t bytes(int in) { return head(in) + (size_t)SA * kA + (size_t)SB * kB + (size_t)PK * kP + 1024; }
 };
 
-template <typename T, int EPI, int NMAX, int STAGES>
+template <typename T, int EPI, int NMAX, int SA, int SB, int PK>
 __global__ void __launch_bounds__(kThreads, 1) qmm_tc_kernel(Args a) {
+  static_assert(SB >= 3 && PK >= SB - 1 && SA >= 2, "ring depths");
   extern __shared__ uint8_t smem_raw[];
-  using S = Smem<NMAX, STAGES>;
+  using S = Smem<NMAX, SA, SB, PK>;
   // 1024-byte aligned base (swizzle atoms must be 1024-aligned).
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(base);
-  uint64_t* empty = full + STAGES;
-  uint64_t* done = empty + STAGES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(base);  // [SA] A(k) and B(k) ready
+  uint64_t* empty_a = full + SA;                         // [SA] MMA(k) done with A slot
+  uint64_t* empty_b = empty_a + SA;                      // [SB] MMA(k) done with B slot
+  uint64_t* done = empty_b + SB;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
   int* tile_info = reinterpret_cast<int*>(tmem_slot + 1);  // [expert, s0, count]
   int32_t* rows = reinterpret_cast<int32_t*>(base + 1024);
   __half* sb = reinterpret_cast<__half*>(rows + NMAX);    // [kM][groups] scales then biases
   const int groups = a.in / 64;
-  size_t head = 1024 + NMAX * 4 + (size_t)kM * groups * 4;
-  head = (head + 1023) / 1024 * 1024;
-  uint8_t* stages = base + head;
+  uint8_t* ring_a = base + S::head(a.in);
+  uint8_t* ring_b = ring_a + (size_t)SA * S::kA;
+  uint8_t* ring_p = ring_b + (size_t)SB * S::kB;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
 
-  // ---- which tile: (expert, token block, row block)
-  const int rb = blockIdx.x % a.row_blocks;
-  int64_t tblock = blockIdx.x / a.row_blocks;
-  if (tid == 0) {
+  // ---- which tile: (expert, token block, row block, K split)
+  int64_t bidx = blockIdx.x;
+  const int split = (int)(bidx % a.ksplit);
+  bidx /= a.ksplit;
+  const int rb = (int)(bidx % a.row_blocks);
+  const int64_t tblock = bidx / a.row_blocks;
+  const int64_t tile_id = bidx;
+  if (warp == 0) {
     int e = -1, s0 = 0, cnt = 0;
     if (!a.grouped) {
       const int64_t nblk = (a.n + a.nt - 1) / a.nt;
@@ -245,37 +258,64 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_tc_kernel(Args a) {
         cnt = (int)((a.n - s0) < (int64_t)a.nt ? (a.n - s0) : (int64_t)a.nt);
       }
     } else {
+      // Warp-parallel lookup over the active experts, 32 per round: each
+      // lane loads one expert's slot range, an inclusive scan of the token
+      // block counts finds the expert owning token block `tblock`.
       const int na = *a.active_count;
-      for (int i = 0; i < na; ++i) {
-        const int ex = a.active[i];
-        const int c0 = a.offsets[ex], c1 = a.offsets[ex + 1];
-        const int nb = (c1 - c0 + a.nt - 1) / a.nt;
-        if (tblock < nb) {
-          e = ex;
-          s0 = c0 + (int)tblock * a.nt;
-          cnt = min(a.nt, c1 - s0);
-          break;
+      int64_t base = 0;
+      for (int c0 = 0; c0 < na && e < 0; c0 += 32) {
+        const int i = c0 + lane;
+        int ex = -1, lo = 0, hi = 0;
+        if (i < na) {
+          ex = a.active[i];
+          lo = a.offsets[ex];
+          hi = a.offsets[ex + 1];
         }
-        tblock -= nb;
+        const int nb = ex >= 0 ? (hi - lo + a.nt - 1) / a.nt : 0;
+        int incl = nb;
+#pragma unroll
+        for (int off = 1; off < 32; off <<= 1) {
+          const int v = __shfl_up_sync(0xffffffffu, incl, off);
+          if (lane >= off) incl += v;
+        }
+        const unsigned hit = __ballot_sync(0xffffffffu, ex >= 0 && base + incl > tblock);
+        if (hit) {
+          const int src = __ffs(hit) - 1;
+          const int ex_s = __shfl_sync(0xffffffffu, ex, src);
+          const int lo_s = __shfl_sync(0xffffffffu, lo, src);
+          const int hi_s = __shfl_sync(0xffffffffu, hi, src);
+          const int first = (int)(base + __shfl_sync(0xffffffffu, incl - nb, src));
+          e = ex_s;
+          s0 = lo_s + (int)(tblock - first) * a.nt;
+          cnt = min(a.nt, hi_s - s0);
+        }
+        base += __shfl_sync(0xffffffffu, incl, 31);
       }
     }
-    tile_info[0] = e;
-    tile_info[1] = s0;
-    tile_info[2] = cnt;
+    if (lane == 0) {
+      tile_info[0] = e;
+      tile_info[1] = s0;
+      tile_info[2] = cnt;
+    }
   }
   __syncthreads();
   const int e = tile_info[0];
   if (e < 0) return;  // past the last tile of this launch
   const int s0 = tile_info[1], cnt = tile_info[2];
   const int n_mma = (cnt + 15) / 16 * 16;  // MMA N: multiple of 16 for M = 128
-  const int nk = a.in / kKStep;
+  // This block's k-steps [k_lo, k_lo + nk) of the tile's in / 64.
+  const int nk_all = a.in / kKStep;
+  const int nk_per = (nk_all + a.ksplit - 1) / a.ksplit;
+  const int k_lo = split * nk_per;
+  const int nk = max(0, min(nk_all, k_lo + nk_per) - k_lo);
 
   // ---- setup: barriers, TMEM, token rows
   if (tid == 0) {
-    for (int s = 0; s < STAGES; ++s) {
+    for (int s = 0; s < SA; ++s) {
       mbar_init(&full[s], kProducerWarps * 32);
-      mbar_init(&empty[s], 1);
+      mbar_init(&empty_a[s], 1);
     }
+    for (int s = 0; s < SB; ++s) mbar_init(&empty_b[s], 1);
     mbar_init(done, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -328,40 +368,50 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_tc_kernel(Args a) {
       cp_async16(my_b + g, bi + grow * groups + g, 16);
     }
     const __half* xb = static_cast<const __half*>(a.x);  // f16 operand copy of the activations
-    auto issue = [&](int k) {
-      uint8_t* st = stages + (size_t)(k % STAGES) * S::kStage;
-      uint8_t* P = st + S::kA + S::kB;
-      cp_async16(P + r * 32, qrow + k * 8, 16);
-      cp_async16(P + r * 32 + 16, qrow + k * 8 + 4, 16);
-      uint8_t* Bt = st + S::kA;
+    // k below is relative to k_lo (ring slots and barrier phases); weight,
+    // scale and activation addresses use the absolute k-step k_lo + k.
+    auto issue_packed = [&](int k) {
+      uint8_t* P = ring_p + (size_t)(k % PK) * S::kP + r * 32;
+      cp_async16(P, qrow + (k_lo + k) * 8, 16);
+      cp_async16(P + 16, qrow + (k_lo + k) * 8 + 4, 16);
+    };
+    auto issue_b = [&](int k) {
+      uint8_t* Bt = ring_b + (size_t)(k % SB) * S::kB;
       for (int c = r; c < n_mma * 8; c += kProducerWarps * 32) {
         const int tok = c >> 3, ch = c & 7;
         const int32_t xr = rows[tok];
-        const void* src = xb + (xr >= 0 ? (int64_t)xr * a.x_stride : 0) + k * kKStep + ch * 8;
+        const void* src = xb + (xr >= 0 ? (int64_t)xr * a.x_stride : 0) + (k_lo + k) * kKStep + ch * 8;
         cp_async16(Bt + tok * 128 + ((ch ^ (tok & 7)) << 4), src, xr >= 0 ? 16u : 0u);
       }
     };
+    // Iteration `it` issues packed(it + PK - 1) and B(it + SB - 2), commits
+    // one cp.async group, and (it >= 0) dequantizes k-step it.  A B slot is
+    // refilled only after the MMA two k-steps back released it, so the
+    // producer never waits on the MMA it just enabled.  Group accounting:
+    // B(k) is in group k + PK - SB + 1, packed(k) in group k, so after the
+    // commit of iteration k waiting down to SB - 2 pending groups covers both.
     bool ok = true;
-    for (int k = 0; k < STAGES - 1; ++k) {
-      if (k < nk) issue(k);
-      cp_async_commit();
-    }
-    for (int k = 0; k < nk && ok; ++k) {
-      const int kn = k + STAGES - 1;
-      if (kn < nk) {
-        if (kn >= STAGES) ok = mbar_wait(&empty[kn % STAGES], ((kn / STAGES) - 1) & 1, 1);
-        if (ok) issue(kn);
+    for (int it = -(PK - 1); it < nk && ok; ++it) {
+      const int kp = it + PK - 1;
+      if (kp < nk) issue_packed(kp);
+      const int kb = it + SB - 2;
+      if (kb >= 0 && kb < nk) {
+        if (kb >= SB) ok = mbar_wait(&empty_b[kb % SB], ((kb / SB) - 1) & 1, 1);
+        if (ok) issue_b(kb);
       }
       cp_async_commit();
-      cp_async_wait<STAGES - 1>();
+      if (it < 0 || !ok) continue;
+      const int k = it;
+      if (k >= SA) ok = mbar_wait(&empty_a[k % SA], ((k / SA) - 1) & 1, 6);
+      if (!ok) continue;
+      cp_async_wait<SB - 2>();
       // Dequantize this thread's row of k-step k into the swizzled A tile.
-      uint8_t* st = stages + (size_t)(k % STAGES) * S::kStage;
-      const uint4* P = reinterpret_cast<const uint4*>(st + S::kA + S::kB + r * 32);
+      const uint4* P = reinterpret_cast<const uint4*>(ring_p + (size_t)(k % PK) * S::kP + r * 32);
       const uint4 p0 = P[0], p1 = P[1];
-      const float s = __half2float(my_s[k]);
-      const float b = __half2float(my_b[k]);
+      const float s = __half2float(my_s[k_lo + k]);
+      const float b = __half2float(my_b[k_lo + k]);
       const uint32_t words[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
-      uint8_t* Arow = st + r * 128;
+      uint8_t* Arow = ring_a + (size_t)(k % SA) * S::kA + r * 128;
 #pragma unroll
       for (int ch = 0; ch < 8; ++ch) {
         const uint32_t w = words[ch];
@@ -373,7 +423,7 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_tc_kernel(Args a) {
         *reinterpret_cast<uint4*>(Arow + ((ch ^ (r & 7)) << 4)) = v;
       }
       fence_proxy_async();
-      mbar_arrive(&full[k % STAGES]);
+      mbar_arrive(&full[k % SA]);
     }
     cp_async_wait<0>();
     // ---- epilogue: wait for the accumulator, read this warp's 32 lanes.
@@ -390,10 +440,66 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_tc_kernel(Args a) {
     tc_fence_after();
     if (all_ok) {
       const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
-      float* xch = reinterpret_cast<float*>(stages);  // [64][NMAX] up values for SWIGLU
-      __syncwarp();
-      if (EPI == EPI_SWIGLU) {
-        // warps 2,3 hold up rows; publish them, then warps 0,1 combine.
+      auto store_plain = [&](int tok, int f, float v) {
+        const int64_t slot = s0 + tok;
+        if (EPI == EPI_F32) {
+          static_cast<float*>(a.y)[slot * a.y_stride + f] = round_act<T>(v);
+        } else if (EPI == EPI_RESIDUAL) {
+          const float res = to_f(static_cast<const T*>(a.residual)[slot * a.residual_stride + f]);
+          static_cast<T*>(a.y)[slot * a.y_stride + f] = from_f<T>(res + round_act<T>(v));
+        } else {
+          static_cast<T*>(a.y)[slot * a.y_stride + f] = from_f<T>(v);
+        }
+      };
+      auto store_swiglu = [&](int tok, int f, float gacc, float uacc) {
+        const float g = round_act<T>(gacc);
+        const float u = round_act<T>(uacc);
+        const float sl = round_act<T>(g / (1.0f + expf(-g)));
+        const int64_t at = (int64_t)(s0 + tok) * a.y_stride + f;
+        const float h = round_act<T>(sl * u);
+        if (a.y_f16)
+          static_cast<__half*>(a.y)[at] = __float2half_rn(h);  // act value in f16 storage
+        else
+          static_cast<T*>(a.y)[at] = from_f<T>(h);
+      };
+      if (a.ksplit > 1) {
+        // Split-K: publish this block's fp32 partial [token][row]; the last
+        // block of the tile to arrive sums the partials in split order (a
+        // fixed order, whichever block is last) and runs the epilogue.
+        float* part = a.partials + ((size_t)tile_id * a.ksplit + split) * (size_t)a.nt * kM;
+        for (int c0 = 0; c0 < n_mma; c0 += 16) {
+          float v[16];
+          tmem_ld16(tmem + lane_base + c0, v);
+#pragma unroll
+          for (int i = 0; i < 16; ++i)
+            if (c0 + i < cnt) __stcg(part + (size_t)(c0 + i) * kM + r, v[i]);
+        }
+        __threadfence();
+        asm volatile("bar.sync 3, %0;" ::"n"(kProducerWarps * 32) : "memory");
+        if (r == 0) tile_info[3] = atomicAdd(&a.counters[tile_id], 1) == a.ksplit - 1 ? 1 : 0;
+        asm volatile("bar.sync 3, %0;" ::"n"(kProducerWarps * 32) : "memory");
+        if (tile_info[3]) {
+          __threadfence();
+          const float* pb = a.partials + (size_t)tile_id * a.ksplit * a.nt * kM;
+          auto total = [&](int tok, int row) {
+            float acc = 0.f;
+            for (int q = 0; q < a.ksplit; ++q) acc += __ldcg(pb + ((size_t)q * a.nt + tok) * kM + row);
+            return acc;
+          };
+          if (EPI == EPI_SWIGLU) {
+            const int f = rb * (kM / 2) + r;
+            if (r < 64 && f < a.out)
+              for (int tok = 0; tok < cnt; ++tok) store_swiglu(tok, f, total(tok, r), total(tok, r + 64));
+          } else {
+            const int f = rb * kM + r;
+            if (f < a.out)
+              for (int tok = 0; tok < cnt; ++tok) store_plain(tok, f, total(tok, r));
+          }
+          if (r == 0) a.counters[tile_id] = 0;  // ready for the next launch
+        }
+      } else if (EPI == EPI_SWIGLU) {
+        // warps 2,3 hold the up rows; publish them, then warps 0,1 combine.
+        float* xch = reinterpret_cast<float*>(ring_b);  // [64][NMAX], rings idle now
         if (warp >= 2) {
           for (int c0 = 0; c0 < n_mma; c0 += 16) {
             float v[16];
@@ -411,17 +517,7 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_tc_kernel(Args a) {
 #pragma unroll
             for (int i = 0; i < 16; ++i) {
               const int tok = c0 + i;
-              if (tok < cnt && f < a.out) {
-                const float g = round_act<T>(v[i]);
-                const float u = round_act<T>(xch[(size_t)r * NMAX + tok]);
-                const float sl = round_act<T>(g / (1.0f + expf(-g)));
-                const int64_t at = (int64_t)(s0 + tok) * a.y_stride + f;
-                const float h = round_act<T>(sl * u);
-                if (a.y_f16)
-                  static_cast<__half*>(a.y)[at] = __float2half_rn(h);  // act value in f16 storage
-                else
-                  static_cast<T*>(a.y)[at] = from_f<T>(h);
-              }
+              if (tok < cnt && f < a.out) store_swiglu(tok, f, v[i], xch[(size_t)r * NMAX + tok]);
             }
           }
         }
@@ -433,17 +529,7 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_tc_kernel(Args a) {
 #pragma unroll
           for (int i = 0; i < 16; ++i) {
             const int tok = c0 + i;
-            if (tok < cnt && f < a.out) {
-              const int64_t slot = s0 + tok;
-              if (EPI == EPI_F32) {
-                static_cast<float*>(a.y)[slot * a.y_stride + f] = round_act<T>(v[i]);
-              } else if (EPI == EPI_RESIDUAL) {
-                const float res = to_f(static_cast<const T*>(a.residual)[slot * a.residual_stride + f]);
-                static_cast<T*>(a.y)[slot * a.y_stride + f] = from_f<T>(res + round_act<T>(v[i]));
-              } else {
-                static_cast<T*>(a.y)[slot * a.y_stride + f] = from_f<T>(v[i]);
-              }
-            }
+            if (tok < cnt && f < a.out) store_plain(tok, f, v[i]);
           }
         }
       }
@@ -454,18 +540,19 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_tc_kernel(Args a) {
     bool ok = true;
     int issued = 0;
     for (int k = 0; k < nk; ++k) {
-      if (!mbar_wait(&full[k % STAGES], (k / STAGES) & 1, 2)) {
+      if (!mbar_wait(&full[k % SA], (k / SA) & 1, 2)) {
         ok = false;
         break;
       }
       tc_fence_after();
-      uint8_t* st = stages + (size_t)(k % STAGES) * S::kStage;
-      const uint32_t a_addr = smem_addr(st), b_addr = smem_addr(st + S::kA);
+      const uint32_t a_addr = smem_addr(ring_a + (size_t)(k % SA) * S::kA);
+      const uint32_t b_addr = smem_addr(ring_b + (size_t)(k % SB) * S::kB);
 #pragma unroll
       for (int j = 0; j < kKStep / 16; ++j)
         mma_f16(tmem, sw128_desc(a_addr + 32 * j), sw128_desc(b_addr + 32 * j), idesc,
                 (k > 0 || j > 0) ? 1u : 0u);
-      mma_commit(&empty[k % STAGES]);
+      mma_commit(&empty_a[k % SA]);
+      mma_commit(&empty_b[k % SB]);
       ++issued;
     }
     // Signal (or, on error, drain) completion of every MMA issued.
@@ -484,35 +571,50 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_tc_kernel(Args a) {
 
 namespace {
 
-template <typename T, int EPI, int NMAX, int STAGES>
+// Split-K counters live at the end of the caller's split-K workspace.
+constexpr int64_t kSplitKMaxTiles = 1024;
+
+template <typename T, int EPI, int NMAX, int SA, int SB, int PK>
 tf_status launch_tc_cfg(const tc::Args& a, int64_t token_tiles, cudaStream_t s) {
-  using S = tc::Smem<NMAX, STAGES>;
+  using S = tc::Smem<NMAX, SA, SB, PK>;
   const size_t smem = S::bytes(a.in);
   // The opt-in size grows with the K extent (row scales live in smem); raise
   // it whenever a launch needs more than any earlier one.
   static size_t attr_bytes = 0;
   if (smem > attr_bytes) {
-    TF_CUDA(cudaFuncSetAttribute(tc::qmm_tc_kernel<T, EPI, NMAX, STAGES>,
+    TF_CUDA(cudaFuncSetAttribute(tc::qmm_tc_kernel<T, EPI, NMAX, SA, SB, PK>,
                                  cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     attr_bytes = smem;
   }
-  const int64_t grid = token_tiles * a.row_blocks;
+  const int64_t grid = token_tiles * a.row_blocks * a.ksplit;
   if (grid <= 0) return TF_OK;
   if (grid > 0x7fffffff) return set_error(TF_ERR_UNSUPPORTED, "qmm_tc: grid too large");
-  tc::qmm_tc_kernel<T, EPI, NMAX, STAGES><<<(unsigned)grid, tc::kThreads, smem, s>>>(a);
+  tc::qmm_tc_kernel<T, EPI, NMAX, SA, SB, PK><<<(unsigned)grid, tc::kThreads, smem, s>>>(a);
   return check_launch("qmm_tc");
 }
 
 template <typename T, int EPI>
 tf_status launch_tc_epi(const tc::Args& a0, int64_t max_count_hint, int64_t tiles_bound_64,
-                        int64_t tiles_bound_256, cudaStream_t s) {
+                        int64_t tiles_bound_256, size_t splitk_bytes, cudaStream_t s) {
   tc::Args a = a0;
   if (max_count_hint <= 64) {
     a.nt = 64;
-    return launch_tc_cfg<T, EPI, 64, 3>(a, tiles_bound_64, s);
+    // Dense problems with few tiles (decode projections) split K so that
+    // about two blocks per SM stream the weights; each split keeps >= 4
+    // k-steps and the partials must fit the caller's split-K workspace.
+    if (!a.grouped && a.partials && a.counters) {
+      const int64_t tiles = tiles_bound_64 * a.row_blocks;
+      const int nk_all = a.in / 64;
+      int ks = 1;
+      while (ks < 8 && tiles * ks * 2 <= 296 && nk_all % (ks * 2) == 0 && nk_all / (ks * 2) >= 4 &&
+             (size_t)tiles * ks * 2 * 64 * 128 * 4 <= splitk_bytes && tiles <= kSplitKMaxTiles)
+        ks *= 2;
+      a.ksplit = ks;
+    }
+    return launch_tc_cfg<T, EPI, 64, 2, 4, 6>(a, tiles_bound_64, s);
   }
   a.nt = 256;
-  return launch_tc_cfg<T, EPI, 256, 3>(a, tiles_bound_256, s);
+  return launch_tc_cfg<T, EPI, 256, 2, 4, 4>(a, tiles_bound_256, s);
 }
 
 }  // namespace
@@ -529,6 +631,11 @@ tf_status launch_qmm_tc(const QmmProblem& p, cudaStream_t s) {
   tc::Args a;
   a.x = p.act == TF_DTYPE_BF16 ? p.x16 : p.x;
   a.y_f16 = p.y_f16;
+  a.ksplit = 1;
+  a.partials = static_cast<float*>(p.splitk_ws);
+  a.counters = p.splitk_ws ? reinterpret_cast<int*>(static_cast<char*>(p.splitk_ws) + p.splitk_bytes -
+                                                    kSplitKMaxTiles * sizeof(int))
+                           : nullptr;
   a.x_stride = p.x_stride;
   a.x_index = p.x_index;
   a.x_div = p.x_div;
@@ -566,9 +673,10 @@ tf_status launch_qmm_tc(const QmmProblem& p, cudaStream_t s) {
   // The 64-token tile re-reads weights once per 64 tokens; beyond that the
   // 256-token tile's extra MMA width is cheaper.
   const int64_t max_hint = a.grouped ? (hint <= 32 ? 64 : 65) : hint;
-#define TF_TC_EPI(E)                                                                              \
-  return p.act == TF_DTYPE_F16 ? launch_tc_epi<__half, E>(a, max_hint, t64, t256, s)              \
-                               : launch_tc_epi<__nv_bfloat16, E>(a, max_hint, t64, t256, s);
+  const size_t part_bytes = p.splitk_ws ? p.splitk_bytes - kSplitKMaxTiles * sizeof(int) : 0;
+#define TF_TC_EPI(E)                                                                                \
+  return p.act == TF_DTYPE_F16 ? launch_tc_epi<__half, E>(a, max_hint, t64, t256, part_bytes, s)    \
+                               : launch_tc_epi<__nv_bfloat16, E>(a, max_hint, t64, t256, part_bytes, s);
   switch (p.epilogue) {
     case EPI_PLAIN: TF_TC_EPI(EPI_PLAIN)
     case EPI_SWIGLU: TF_TC_EPI(EPI_SWIGLU)

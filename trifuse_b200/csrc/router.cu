@@ -7,7 +7,7 @@
 //  - native_olmoe_softmax / topk       native_affine_ops.py:128-153
 //  - route sort (argsort + inverse)    MLXNativeGraniteMoEPrefill.h:666-684
 //
-// One warp per token.  Every fp32 step is explicitly rounded so the result is
+// Every fp32 step is explicitly rounded so the result is
 // bit-identical to oracle/olmoe.py (router_logits_*, olmoe_softmax,
 // olmoe_topk): the dot product uses the chunk order "lane l owns 8-element
 // chunks l + 32j", the softmax uses exp in double rounded to fp32, and the
@@ -72,22 +72,42 @@ __device__ __forceinline__ void route_token(int lane, float la0, float la1, int 
   }
 }
 
-// Router GEMV: J = hidden / 256 chunks per lane.
-template <typename T, bool DENSE, int J>
-__global__ void __launch_bounds__(kRouterWarps * 32)
+// Router GEMV.  A block of 8 warps owns TPC tokens; warp w computes experts
+// w, w + 8, ... for all of them, so each weight chunk is decoded once per
+// block and reused across its tokens.  Per (token, expert) the arithmetic is
+// the fixed order above: lane l accumulates chunks l + 32j (j outer, the 8
+// elements of a chunk inner) with separate fp32 multiply and add, then the
+// xor butterfly.  The logits go through shared memory to one warp per token
+// for the softmax / rank.  J = hidden / 256.
+constexpr int kRouterBlockWarps = 8;
+
+template <typename T, bool DENSE, int J, int TPC>
+__global__ void __launch_bounds__(kRouterBlockWarps * 32)
     router_kernel(const T* __restrict__ x, int64_t tokens, const T* __restrict__ wd,
                   const uint32_t* __restrict__ wq, const __half* __restrict__ ws,
                   const __half* __restrict__ wb, int E, int K, T* logits, int32_t* idx, T* gates) {
-  const int lane = threadIdx.x & 31;
-  const int64_t t = (int64_t)blockIdx.x * kRouterWarps + (threadIdx.x >> 5);
-  if (t >= tokens) return;
   constexpr int H = J * 256;
-  float xf[J][8];
+  __shared__ float xs[TPC][H];
+  __shared__ float ls[TPC][64];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int64_t t0 = (int64_t)blockIdx.x * TPC;
+  for (int i = threadIdx.x; i < TPC * H / 8; i += blockDim.x) {
+    const int t = i / (H / 8), c = i % (H / 8);
+    float f[8];
+    if (t0 + t < tokens) {
+      unpack8<T>(ld_v4(x + (t0 + t) * H + 8 * c), f);
+    } else {
 #pragma unroll
-  for (int j = 0; j < J; ++j) unpack8<T>(ld_v4(x + t * H + 8 * (lane + 32 * j)), xf[j]);
-  float la0 = 0.f, la1 = 0.f;
-  for (int e = 0; e < E; ++e) {
-    float acc = 0.f;
+      for (int k = 0; k < 8; ++k) f[k] = 0.f;
+    }
+#pragma unroll
+    for (int k = 0; k < 8; ++k) xs[t][8 * c + k] = f[k];
+  }
+  __syncthreads();
+  for (int e = warp; e < E; e += kRouterBlockWarps) {
+    float acc[TPC];
+#pragma unroll
+    for (int t = 0; t < TPC; ++t) acc[t] = 0.f;
 #pragma unroll
     for (int j = 0; j < J; ++j) {
       const int c = lane + 32 * j;
@@ -96,23 +116,36 @@ __global__ void __launch_bounds__(kRouterWarps * 32)
         unpack8<T>(ld_v4(wd + (int64_t)e * H + 8 * c), wf);
       } else {
         const uint32_t word = wq[(int64_t)e * (H / 8) + c];
-        const float s = __half2float(ws[(int64_t)e * (H / 64) + c / 8]);
-        const float b = __half2float(wb[(int64_t)e * (H / 64) + c / 8]);
+        const float sc = __half2float(ws[(int64_t)e * (H / 64) + c / 8]);
+        const float bi = __half2float(wb[(int64_t)e * (H / 64) + c / 8]);
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
           const float code = (float)((word >> (4 * i)) & 0xFu);
-          wf[i] = __half2float(__float2half_rn(__fadd_rn(__fmul_rn(code, s), b)));
+          wf[i] = __half2float(__float2half_rn(__fadd_rn(__fmul_rn(code, sc), bi)));
         }
       }
 #pragma unroll
-      for (int i = 0; i < 8; ++i) acc = __fadd_rn(acc, __fmul_rn(xf[j][i], wf[i]));
+      for (int t = 0; t < TPC; ++t) {
+        const float* xt = &xs[t][8 * c];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) acc[t] = __fadd_rn(acc[t], __fmul_rn(xt[i], wf[i]));
+      }
     }
-    const float la = round_act<T>(warp_sum_butterfly(acc));
-    if (e == lane) la0 = la;
-    if (e == lane + 32) la1 = la;
-    if (logits && lane == 0) logits[t * E + e] = from_f<T>(la);
+#pragma unroll
+    for (int t = 0; t < TPC; ++t) {
+      const float la = round_act<T>(warp_sum_butterfly(acc[t]));
+      if (lane == 0) {
+        ls[t][e] = la;
+        if (logits && t0 + t < tokens) logits[(t0 + t) * E + e] = from_f<T>(la);
+      }
+    }
   }
-  if (idx) route_token<T>(lane, la0, la1, E, K, t, (T*)nullptr, idx, gates);
+  __syncthreads();
+  if (idx && warp < TPC && t0 + warp < tokens) {
+    const float la0 = lane < E ? ls[warp][lane] : 0.f;
+    const float la1 = lane + 32 < E ? ls[warp][lane + 32] : 0.f;
+    route_token<T>(lane, la0, la1, E, K, t0 + warp, (T*)nullptr, idx, gates);
+  }
 }
 
 template <typename T>
@@ -158,32 +191,41 @@ __global__ void take_along_kernel(const T* __restrict__ x, int64_t rows, int wid
   out[i] = x[r * width + idx[i]];
 }
 
-template <typename T, bool DENSE>
-static tf_status router_dispatch(const void* x, int64_t tokens, int hidden,
-                                 const tf_router_weight& r, int E, int K, void* logits,
-                                 int32_t* idx, void* gates, cudaStream_t s) {
-  const unsigned blocks = (unsigned)((tokens + kRouterWarps - 1) / kRouterWarps);
+template <typename T, bool DENSE, int TPC>
+static tf_status router_dispatch_tpc(const void* x, int64_t tokens, int hidden,
+                                     const tf_router_weight& r, int E, int K, void* logits,
+                                     int32_t* idx, void* gates, cudaStream_t s) {
+  const unsigned blocks = (unsigned)((tokens + TPC - 1) / TPC);
   const T* wd = (const T*)r.dense;
   const uint32_t* wq = r.affine.q;
   const __half* wsc = (const __half*)r.affine.scales;
   const __half* wbi = (const __half*)r.affine.biases;
-#define TF_ROUTER_CASE(JJ)                                                            \
-  case JJ:                                                                            \
-    router_kernel<T, DENSE, JJ><<<blocks, kRouterWarps * 32, 0, s>>>(                 \
-        (const T*)x, tokens, wd, wq, wsc, wbi, E, K, (T*)logits, idx, (T*)gates);     \
+#define TF_ROUTER_CASE(JJ)                                                                  \
+  case JJ:                                                                                  \
+    router_kernel<T, DENSE, JJ, TPC><<<blocks, kRouterBlockWarps * 32, 0, s>>>(             \
+        (const T*)x, tokens, wd, wq, wsc, wbi, E, K, (T*)logits, idx, (T*)gates);           \
     break;
   switch (hidden / 256) {
     TF_ROUTER_CASE(1)
     TF_ROUTER_CASE(2)
     TF_ROUTER_CASE(4)
     TF_ROUTER_CASE(8)
-    TF_ROUTER_CASE(16)
     default:
-      return set_error(TF_ERR_UNSUPPORTED, "router: hidden %d not in {256,512,1024,2048,4096}",
-                       hidden);
+      return set_error(TF_ERR_UNSUPPORTED, "router: hidden %d not in {256,512,1024,2048}", hidden);
   }
 #undef TF_ROUTER_CASE
   return check_launch("router");
+}
+
+// One token per block while that still fills the GPU; four (weights decoded
+// once per four tokens) for long prefill batches.
+template <typename T, bool DENSE>
+static tf_status router_dispatch(const void* x, int64_t tokens, int hidden,
+                                 const tf_router_weight& r, int E, int K, void* logits,
+                                 int32_t* idx, void* gates, cudaStream_t s) {
+  if (tokens <= 2048)
+    return router_dispatch_tpc<T, DENSE, 1>(x, tokens, hidden, r, E, K, logits, idx, gates, s);
+  return router_dispatch_tpc<T, DENSE, 4>(x, tokens, hidden, r, E, K, logits, idx, gates, s);
 }
 
 tf_status launch_router(const void* x, int64_t tokens, int hidden, const tf_router_weight& r,
