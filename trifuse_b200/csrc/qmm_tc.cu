@@ -169,8 +169,26 @@ __device__ __forceinline__ uint32_t pack2<__nv_bfloat16>(float lo, float hi) {
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
-__device__ __forceinline__ float code_f(uint32_t w, int j) {
-  return __int_as_float(0x4B000000u | ((w >> (4 * j)) & 0xFu)) - 8388608.0f;
+// Eight codes of one packed word -> eight f16 weights fp16(code*s + b) in k
+// order.  (w >> 4i) & 0x000F000F | 0x6400 6400 is the f16 pair (1024 + c_i,
+// 1024 + c_{i+4}); byte_perm regroups the pairs as (c0,c1) (c2,c3) (c4,c5)
+// (c6,c7); subtracting 1024 is exact and one HFMA2 rounds c*s + b once.
+__device__ __forceinline__ uint4 dequant8(uint32_t w, __half2 s2, __half2 b2) {
+  const uint32_t t0 = (w & 0x000F000Fu) | 0x64006400u;
+  const uint32_t t1 = ((w >> 4) & 0x000F000Fu) | 0x64006400u;
+  const uint32_t t2 = ((w >> 8) & 0x000F000Fu) | 0x64006400u;
+  const uint32_t t3 = ((w >> 12) & 0x000F000Fu) | 0x64006400u;
+  const uint32_t q[4] = {__byte_perm(t0, t1, 0x5410), __byte_perm(t2, t3, 0x5410),
+                         __byte_perm(t0, t1, 0x7632), __byte_perm(t2, t3, 0x7632)};
+  const __half2 k1024 = __half2half2(__ushort_as_half(0x6400));
+  uint32_t o[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const __half2 n = __hsub2(*reinterpret_cast<const __half2*>(&q[i]), k1024);
+    const __half2 h = __hfma2(n, s2, b2);
+    o[i] = *reinterpret_cast<const uint32_t*>(&h);
+  }
+  return make_uint4(o[0], o[1], o[2], o[3]);
 }
 
 struct Args {
@@ -408,18 +426,13 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_tc_kernel(Args a) {
       // Dequantize this thread's row of k-step k into the swizzled A tile.
       const uint4* P = reinterpret_cast<const uint4*>(ring_p + (size_t)(k % PK) * S::kP + r * 32);
       const uint4 p0 = P[0], p1 = P[1];
-      const float s = __half2float(my_s[k_lo + k]);
-      const float b = __half2float(my_b[k_lo + k]);
+      const __half2 s2 = __half2half2(my_s[k_lo + k]);
+      const __half2 b2 = __half2half2(my_b[k_lo + k]);
       const uint32_t words[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
       uint8_t* Arow = ring_a + (size_t)(k % SA) * S::kA + r * 128;
 #pragma unroll
       for (int ch = 0; ch < 8; ++ch) {
-        const uint32_t w = words[ch];
-        uint4 v;
-        v.x = pack2<__half>(fmaf(code_f(w, 0), s, b), fmaf(code_f(w, 1), s, b));
-        v.y = pack2<__half>(fmaf(code_f(w, 2), s, b), fmaf(code_f(w, 3), s, b));
-        v.z = pack2<__half>(fmaf(code_f(w, 4), s, b), fmaf(code_f(w, 5), s, b));
-        v.w = pack2<__half>(fmaf(code_f(w, 6), s, b), fmaf(code_f(w, 7), s, b));
+        const uint4 v = dequant8(words[ch], s2, b2);
         *reinterpret_cast<uint4*>(Arow + ((ch ^ (r & 7)) << 4)) = v;
       }
       fence_proxy_async();
