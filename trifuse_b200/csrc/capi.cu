@@ -315,8 +315,8 @@ struct MoePlan {
   size_t sort_ws_bytes;
   void* h;
   void* y;
-  void* x16;  // f16 operand copies for the tensor-core path with bf16 activations
-  void* h16;
+  void* xs;   // tensor-core operand: x rows in slot order, f16
+  void* h16;  // f16 copy of h when only the down projection uses tensor cores
   size_t used;
 };
 
@@ -337,9 +337,8 @@ static MoePlan plan_moe(const tf_moe_args* a, void* ws, size_t ws_bytes) {
   p.sort_ws = c.take<char>(p.sort_ws_bytes);
   p.h = c.take<char>((size_t)N * a->intermediate * ab);
   p.y = c.take<char>((size_t)N * a->hidden * ab);
-  const bool bf = a->act == TF_DTYPE_BF16;
-  p.x16 = bf ? c.take<char>((size_t)T * a->hidden * 2) : nullptr;
-  p.h16 = bf ? c.take<char>((size_t)N * a->intermediate * 2) : nullptr;
+  p.xs = c.take<char>((size_t)N * a->hidden * 2);
+  p.h16 = c.take<char>((size_t)N * a->intermediate * 2);
   p.used = c.used;
   return p;
 }
@@ -405,19 +404,20 @@ static tf_status run_moe(const tf_moe_args* a, const MoePlan& p, cudaStream_t s)
   dn.y = p.y;
   dn.y_stride = a->hidden;
   const bool tc_up = qmm_uses_tc(up), tc_dn = qmm_uses_tc(dn);
-  if (a->act == TF_DTYPE_BF16 && tc_up) {
-    TF_TRY(launch_bf16_to_f16(a->x, a->tokens * a->hidden, p.x16, s));
-    up.x16 = p.x16;
+  trace(PH_GATE_UP, true, s);
+  if (tc_up) {
+    // The tensor cores read the expert inputs as contiguous f16 rows in slot order.
+    TF_TRY(launch_gather_f16(a->x, a->hidden, a->act, p.order, a->top_k, N, a->hidden, p.xs, s));
+    up.x16 = p.xs;
     if (tc_dn) {  // h goes straight to the next tensor-core QMM in f16 storage
       up.y_f16 = 1;
       dn.x16 = p.h;
     }
   }
-  trace(PH_GATE_UP, true, s);
   TF_TRY(launch_qmm(up, s));
   trace(PH_GATE_UP, false, s);
-  if (a->act == TF_DTYPE_BF16 && tc_dn && !up.y_f16) {
-    TF_TRY(launch_bf16_to_f16(p.h, N * a->intermediate, p.h16, s));
+  if (tc_dn && !up.y_f16) {
+    TF_TRY(launch_gather_f16(p.h, a->intermediate, a->act, nullptr, 1, N, a->intermediate, p.h16, s));
     dn.x16 = p.h16;
   }
   trace(PH_DOWN, true, s);
@@ -482,9 +482,8 @@ static ExpertPlan plan_expert(void* ws, size_t ws_bytes, int64_t n, int64_t x_ro
   p.sws_bytes = sort_workspace_bytes(n, experts);
   p.sws = c.take<char>(p.sws_bytes);
   p.h = c.take<char>((size_t)n * intermediate * act_bytes(act));
-  const bool bf = act == TF_DTYPE_BF16;
-  p.x16 = bf ? c.take<char>((size_t)x_rows * hidden * 2) : nullptr;
-  p.h16 = bf ? c.take<char>((size_t)n * intermediate * 2) : nullptr;
+  p.x16 = c.take<char>((size_t)n * hidden * 2);  // slot-ordered f16 operand
+  p.h16 = c.take<char>((size_t)n * intermediate * 2);
   p.used = c.used;
   return p;
 }
@@ -555,8 +554,8 @@ int tf_moe_expert_gpu(const void* x, int64_t x_rows, int32_t hidden, const int32
   d.y = out_sorted;
   d.y_stride = hidden;
   const bool tc_up = qmm_uses_tc(p), tc_dn = qmm_uses_tc(d);
-  if (act == TF_DTYPE_BF16 && tc_up) {
-    TF_TRY(launch_bf16_to_f16(x, x_rows * hidden, w.x16, s));
+  if (tc_up) {
+    TF_TRY(launch_gather_f16(x, hidden, act, xrow, 1, n, hidden, w.x16, s));
     p.x16 = w.x16;
     if (tc_dn) {
       p.y_f16 = 1;
@@ -564,8 +563,8 @@ int tf_moe_expert_gpu(const void* x, int64_t x_rows, int32_t hidden, const int32
     }
   }
   TF_TRY(launch_qmm(p, s));
-  if (act == TF_DTYPE_BF16 && tc_dn && !p.y_f16) {
-    TF_TRY(launch_bf16_to_f16(h, n * intermediate, w.h16, s));
+  if (tc_dn && !p.y_f16) {
+    TF_TRY(launch_gather_f16(h, intermediate, act, nullptr, 1, n, intermediate, w.h16, s));
     d.x16 = w.h16;
   }
   return launch_qmm(d, s);

@@ -128,8 +128,9 @@ struct QmmProblem {
   int64_t y_stride = 0;
   const void* residual = nullptr;  // EPI_RESIDUAL, indexed like y
   int64_t residual_stride = 0;
-  // Tensor-core path with bf16 activations: f16 copy of x (same rows and
-  // stride), and for EPI_SWIGLU whether y is written in f16 storage.
+  // Tensor-core operand: an f16 copy of the activations with contiguous rows
+  // (dense bf16: x converted, same stride; grouped: slot-ordered rows of
+  // width in_features), and for EPI_SWIGLU whether y is written in f16.
   const void* x16 = nullptr;
   int y_f16 = 0;
   // Optional split-K workspace for dense tensor-core problems with few tiles
@@ -142,6 +143,9 @@ constexpr size_t kSplitKWorkspaceBytes = (size_t)16 << 20;
 // Path launch_qmm would take for this problem (true = tensor cores).
 bool qmm_uses_tc(const QmmProblem& p);
 tf_status launch_bf16_to_f16(const void* x, int64_t n, void* y, cudaStream_t s);
+// y[i][:] = f16(x[perm ? perm[i] / div : i][:]) for i < rows (tensor-core operand).
+tf_status launch_gather_f16(const void* x, int64_t x_stride, int act, const int32_t* perm, int div, int64_t rows,
+                            int width, void* y, cudaStream_t s);
 // Dispatches to the tensor-core kernel (launch_qmm_tc) when the problem has
 // enough tokens per weight matrix, else to the CUDA-core GEMV.
 tf_status launch_qmm(const QmmProblem& p, cudaStream_t s);

@@ -236,7 +236,8 @@ int g_qmm_path = 0;
 
 bool qmm_uses_tc(const QmmProblem& p) {
   const int in = p.w0.in_features;
-  const bool tc_ok = p.mode != QMM_PER_ROUTE && in % 512 == 0 && in <= 8192;
+  const bool tc_ok = p.mode != QMM_PER_ROUTE && in % 512 == 0 && in <= 8192 &&
+                     !(p.mode == QMM_DENSE && p.x_index);
   if (!tc_ok || g_qmm_path == 1) return false;
   if (g_qmm_path == 2) return true;
   if (p.mode == QMM_DENSE) return p.n >= 8;
@@ -246,8 +247,10 @@ bool qmm_uses_tc(const QmmProblem& p) {
 
 tf_status launch_qmm(const QmmProblem& p, cudaStream_t s) {
   if (p.n == 0) return TF_OK;
-  // bf16 activations reach the tensor cores only with their f16 copy.
-  if (qmm_uses_tc(p) && (p.act != TF_DTYPE_BF16 || p.x16)) return launch_qmm_tc(p, s);
+  // The tensor cores read an f16 operand with contiguous rows: x itself for
+  // dense f16, else the caller-provided copy.
+  const bool operand = p.x16 || (p.mode == QMM_DENSE && p.act == TF_DTYPE_F16);
+  if (qmm_uses_tc(p) && operand) return launch_qmm_tc(p, s);
   return launch_qmm_gemv(p, s);
 }
 
