@@ -16,8 +16,9 @@ __global__ void __launch_bounds__(256)
     combine_kernel(const T* __restrict__ y, const int32_t* __restrict__ inverse,
                    const T* __restrict__ gates, const T* __restrict__ residual, int K, int H,
                    T* __restrict__ out) {
-  const int64_t t = blockIdx.y;
-  const int c = blockIdx.x * blockDim.x + threadIdx.x;  // 8-element chunk
+  const int cpr = (H / 8 + blockDim.x - 1) / blockDim.x;  // blocks per token row
+  const int64_t t = blockIdx.x / cpr;
+  const int c = (int)(blockIdx.x % cpr) * blockDim.x + threadIdx.x;  // 8-element chunk
   if (8 * c >= H) return;
   float acc[8];
   for (int k = 0; k < K; ++k) {
@@ -42,7 +43,7 @@ tf_status launch_combine(const void* y_sorted, const int32_t* inverse, const voi
                          const void* residual, int64_t tokens, int k, int hidden, int act,
                          void* out, cudaStream_t s) {
   if (tokens == 0) return TF_OK;
-  dim3 grid((hidden / 8 + 255) / 256, (unsigned)tokens);
+  const unsigned grid = (unsigned)(tokens * ((hidden / 8 + 255) / 256));
   if (act == TF_DTYPE_F16)
     combine_kernel<__half><<<grid, 256, 0, s>>>((const __half*)y_sorted, inverse,
                                                 (const __half*)gates, (const __half*)residual, k,

@@ -60,8 +60,9 @@ template <typename T>
 __global__ void embedding_kernel(const int64_t* __restrict__ ids, const uint32_t* __restrict__ q,
                                  const __half* __restrict__ sc, const __half* __restrict__ bi,
                                  int width, T* __restrict__ y) {
-  const int64_t n = blockIdx.y;
-  const int word = blockIdx.x * blockDim.x + threadIdx.x;
+  const int bpr = (width / 8 + blockDim.x - 1) / blockDim.x;  // blocks per row
+  const int64_t n = blockIdx.x / bpr;
+  const int word = (int)(blockIdx.x % bpr) * blockDim.x + threadIdx.x;
   if (word >= width / 8) return;
   const int64_t row = ids[n];
   const uint32_t wv = q[row * (width / 8) + word];
@@ -81,7 +82,7 @@ tf_status launch_embedding(const int64_t* ids, int64_t n, const tf_affine_weight
                            void* y, cudaStream_t s) {
   if (n == 0) return TF_OK;
   const int width = t.in_features;
-  dim3 grid((width / 8 + 255) / 256, (unsigned)n);
+  const unsigned grid = (unsigned)(n * ((width / 8 + 255) / 256));
   if (out == TF_DTYPE_F16)
     embedding_kernel<__half><<<grid, 256, 0, s>>>(ids, t.q, (const __half*)t.scales,
                                                    (const __half*)t.biases, width, (__half*)y);

@@ -337,7 +337,10 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_tc_kernel(const __grid_consta
   constexpr int kTileRows = kSw ? kM / 2 : kM;  // rows of each weight matrix per tile
 
   if (warp == kLoadWarp) {
-    // ---- loader: one thread issues every TMA
+    // ---- loader: lane 0 streams packed codes (PK ahead of the dequant warps)
+    // and each tile's scales; lane 1 streams activation tiles (SB ahead of
+    // the MMA).  Separate issuers keep the weight stream from waiting on the
+    // MMA, so up to PK k-steps of codes are in flight.
     if (lane == 0) {
       int64_t g = 0;
       bool ok = true;
@@ -363,11 +366,19 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_tc_kernel(const __grid_consta
           mbar_expect_tx(&p_full[ps], (uint32_t)L::kP);
           tma_2d(pdst, &p.tm_q0, k * 8, row0, &p_full[ps]);
           if (kSw) tma_2d(pdst + 64 * 32, &p.tm_q1, k * 8, row0, &p_full[ps]);
+        }
+      }
+    } else if (lane == 1) {
+      int64_t g = 0;
+      bool ok = true;
+      for (int li = 0; li < ntiles && ok; ++li) {
+        const int s0 = table[li].s0;
+        for (int k = 0; k < nk && ok; ++k, ++g) {
           const int bs = (int)(g % SB);
           if (g >= SB) ok = mbar_wait(&b_empty[bs], (uint32_t)(((g / SB) - 1) & 1), abort_flag, 13);
           if (!ok) break;
           mbar_expect_tx(&b_full[bs], (uint32_t)L::kB);
-          tma_2d(ring_b + (size_t)bs * L::kB, &p.tm_x, k * kKStep, ti.s0, &b_full[bs]);
+          tma_2d(ring_b + (size_t)bs * L::kB, &p.tm_x, k * kKStep, s0, &b_full[bs]);
         }
       }
     }
@@ -582,8 +593,8 @@ tf_status launch_nt(tc::Params& p, const QmmProblem& q, int nt, int64_t tiles_bo
                   CU_TENSOR_MAP_SWIZZLE_128B));
   p.tiles_bound = tiles_bound;
   switch (nt) {
-    case 32: return launch_cfg<T, EPI, 32, 12, 2, 6>(p, s);
-    case 64: return launch_cfg<T, EPI, 64, 12, 2, 4>(p, s);
+    case 32: return launch_cfg<T, EPI, 32, 12, 2, 10>(p, s);
+    case 64: return launch_cfg<T, EPI, 64, 12, 2, 6>(p, s);
     default: return launch_cfg<T, EPI, 256, 6, 2, 3>(p, s);
   }
 }
@@ -661,8 +672,9 @@ tf_status launch_qmm_tc(const QmmProblem& q, cudaStream_t s) {
 template <typename Tin>
 __global__ void gather_f16_kernel(const Tin* __restrict__ x, int64_t x_stride, const int32_t* __restrict__ perm,
                                   int div, int64_t rows, int width, __half* __restrict__ y) {
-  const int64_t row = blockIdx.y;
-  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  const int cpr = (width / 8 + blockDim.x - 1) / blockDim.x;  // blocks per row
+  const int64_t row = blockIdx.x / cpr;
+  const int c = (int)(blockIdx.x % cpr) * blockDim.x + threadIdx.x;
   if (row >= rows || 8 * c >= width) return;
   const int64_t src = perm ? perm[row] / div : row;
   float f[8];
@@ -678,8 +690,9 @@ tf_status launch_gather_f16(const void* x, int64_t x_stride, int act, const int3
                             int width, void* y, cudaStream_t s) {
   if (rows == 0) return TF_OK;
   if (width % 8) return set_error(TF_ERR_SHAPE, "gather_f16: width %d", width);
-  if (rows > 2147483647) return set_error(TF_ERR_UNSUPPORTED, "gather_f16: too many rows");
-  dim3 grid((width / 8 + 127) / 128, (unsigned)rows);
+  const int64_t cpr = (width / 8 + 127) / 128;
+  if (rows * cpr > 2147483647) return set_error(TF_ERR_UNSUPPORTED, "gather_f16: too many rows");
+  const unsigned grid = (unsigned)(rows * cpr);
   if (act == TF_DTYPE_F16)
     gather_f16_kernel<__half><<<grid, 128, 0, s>>>((const __half*)x, x_stride, perm, div, rows, width, (__half*)y);
   else
