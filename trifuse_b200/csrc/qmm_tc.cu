@@ -593,9 +593,9 @@ tf_status launch_nt(tc::Params& p, const QmmProblem& q, int nt, int64_t tiles_bo
                   CU_TENSOR_MAP_SWIZZLE_128B));
   p.tiles_bound = tiles_bound;
   switch (nt) {
-    case 32: return launch_cfg<T, EPI, 32, 12, 2, 10>(p, s);
-    case 64: return launch_cfg<T, EPI, 64, 12, 2, 6>(p, s);
-    default: return launch_cfg<T, EPI, 256, 6, 2, 3>(p, s);
+    case 32: return launch_cfg<T, EPI, 32, 8, 4, 8>(p, s);
+    case 64: return launch_cfg<T, EPI, 64, 8, 4, 6>(p, s);
+    default: return launch_cfg<T, EPI, 256, 4, 3, 3>(p, s);
   }
 }
 
