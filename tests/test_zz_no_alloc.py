@@ -70,3 +70,20 @@ def test_noalloc_rejects_batches_beyond_its_buffer():
     a.down_proj = AffineWeight(0x1000, 0x2000, 0x3000, 64, 2048, 1024, 64, 4)
     assert lib().tf_moe_forward_noalloc(C.byref(a), None) == 10  # TF_ERR_CAPACITY
     assert b"fixed buffer" in lib().tf_last_error()
+
+
+def test_noalloc_buffer_holds_its_largest_batch():
+    """The workspace a 64-token OLMoE block needs fits the fixed buffer, for
+    both activation dtypes (runs without a GPU)."""
+    from trifuse_b200._lib import AffineWeight, MoeArgs, lib
+    for act in (1, 2):
+        a = MoeArgs()
+        a.x = a.residual = a.out = 0x1000
+        a.tokens, a.hidden, a.intermediate, a.experts, a.top_k, a.act = 64, 2048, 1024, 64, 8, act
+        a.router.affine = AffineWeight(0x1000, 0x2000, 0x3000, 0, 64, 2048, 64, 4)
+        a.gate_proj = AffineWeight(0x1000, 0x2000, 0x3000, 64, 1024, 2048, 64, 4)
+        a.up_proj = AffineWeight(0x1000, 0x2000, 0x3000, 64, 1024, 2048, 64, 4)
+        a.down_proj = AffineWeight(0x1000, 0x2000, 0x3000, 64, 2048, 1024, 64, 4)
+        nb = C.c_size_t()
+        assert lib().tf_moe_workspace_size(C.byref(a), C.byref(nb)) == 0
+        assert 0 < nb.value <= 6 << 20

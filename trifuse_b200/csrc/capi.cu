@@ -315,8 +315,9 @@ struct MoePlan {
   size_t sort_ws_bytes;
   void* h;
   void* y;
-  void* xs;   // tensor-core operand: x rows in slot order, f16
-  void* h16;  // f16 copy of h when only the down projection uses tensor cores
+  // f16 tensor-core operand: x rows in slot order when gate/up runs on tensor cores, else the
+  // f16 copy of h when only the down projection does (never both in one call).
+  void* op16;
   size_t used;
 };
 
@@ -337,8 +338,7 @@ static MoePlan plan_moe(const tf_moe_args* a, void* ws, size_t ws_bytes) {
   p.sort_ws = c.take<char>(p.sort_ws_bytes);
   p.h = c.take<char>((size_t)N * a->intermediate * ab);
   p.y = c.take<char>((size_t)N * a->hidden * ab);
-  p.xs = c.take<char>((size_t)N * a->hidden * 2);
-  p.h16 = c.take<char>((size_t)N * a->intermediate * 2);
+  p.op16 = c.take<char>((size_t)N * (a->hidden > a->intermediate ? a->hidden : a->intermediate) * 2);
   p.used = c.used;
   return p;
 }
@@ -407,8 +407,8 @@ static tf_status run_moe(const tf_moe_args* a, const MoePlan& p, cudaStream_t s)
   trace(PH_GATE_UP, true, s);
   if (tc_up) {
     // The tensor cores read the expert inputs as contiguous f16 rows in slot order.
-    TF_TRY(launch_gather_f16(a->x, a->hidden, a->act, p.order, a->top_k, N, a->hidden, p.xs, s));
-    up.x16 = p.xs;
+    TF_TRY(launch_gather_f16(a->x, a->hidden, a->act, p.order, a->top_k, N, a->hidden, p.op16, s));
+    up.x16 = p.op16;
     if (tc_dn) {  // h goes straight to the next tensor-core QMM in f16 storage
       up.y_f16 = 1;
       dn.x16 = p.h;
@@ -417,8 +417,8 @@ static tf_status run_moe(const tf_moe_args* a, const MoePlan& p, cudaStream_t s)
   TF_TRY(launch_qmm(up, s));
   trace(PH_GATE_UP, false, s);
   if (tc_dn && !up.y_f16) {
-    TF_TRY(launch_gather_f16(p.h, a->intermediate, a->act, nullptr, 1, N, a->intermediate, p.h16, s));
-    dn.x16 = p.h16;
+    TF_TRY(launch_gather_f16(p.h, a->intermediate, a->act, nullptr, 1, N, a->intermediate, p.op16, s));
+    dn.x16 = p.op16;
   }
   trace(PH_DOWN, true, s);
   TF_TRY(launch_qmm(dn, s));

@@ -29,7 +29,7 @@ namespace {
 
 // Covers one decode step of up to 64 tokens at OLMoE-1B-7B geometry
 // (hidden 2048, intermediate 1024, 64 experts, top-8, f16 or bf16):
-// about 4.3 MiB of route buffers, expert intermediates and f16 operand copies.
+// about 5 MiB of route buffers, expert intermediates and f16 operand copies.
 constexpr size_t kScratchBytes = TF_MOE_NOALLOC_SCRATCH_BYTES;
 
 static __device__ __align__(256) unsigned char g_moe_scratch[kScratchBytes];
