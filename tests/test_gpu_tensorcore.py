@@ -88,3 +88,36 @@ def test_expert_hook_tensor_core(ops):
     h = oracle.swiglu(oracle.gather_qmm(rows, *ex["gate"], sel, act),
                       oracle.gather_qmm(rows, *ex["up"], sel, act), act)
     assert_close(host(out), oracle.gather_qmm(h, *ex["down"], sel, act))
+
+
+def _dequant_torch(q, s, b):
+    """fp16(code * s + b) for packed [out, in/8] uint32 words (torch, fp32 result)."""
+    import torch
+    out, inw = q.shape[0], q.shape[1] * 8
+    qi = q.view(torch.int32).long() & 0xFFFFFFFF
+    codes = torch.stack([(qi >> (4 * i)) & 0xF for i in range(8)], -1).reshape(out, inw).float()
+    w = codes.view(out, -1, 64) * s.float()[..., None] + b.float()[..., None]
+    return w.reshape(out, inw).half().float()
+
+
+def test_tensor_core_many_tiles_per_block_is_deterministic(ops):
+    """Many 256-token tiles per persistent block keep every ring slot busy;
+    repeated launches must agree bit for bit and match an fp32 reference
+    (a slot released before its shared loads completed once let the next
+    TMA fill overtake them)."""
+    import torch
+    from trifuse_b200.quant import random_affine
+    g = torch.Generator(device="cuda")
+    g.manual_seed(21)
+    w = random_affine((32768, 2048), g, "cuda")
+    x = torch.randn(1024, 2048, device="cuda", dtype=torch.float16, generator=g)
+    ref = x.float() @ _dequant_torch(*w).t()
+    with path(ops, 2):
+        ys = [ops.native_affine_qmm(x, *w, 64, 4) for _ in range(3)]
+    torch.cuda.synchronize()
+    assert ops.device_error() == 0
+    for y in ys[1:]:
+        assert torch.equal(y, ys[0])
+    err = (ys[0].float() - ref).abs()
+    assert err.max().item() <= 2e-2 + 4e-3 * ref.abs().max().item()
+    assert (err / (ref.abs() + 1)).mean().item() < 1e-3

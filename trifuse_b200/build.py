@@ -49,6 +49,8 @@ def _compile(src: Path, force: bool, extra: list[str]) -> Path:
     r = subprocess.run(cmd, capture_output=True, text=True)
     if r.returncode != 0:
         raise RuntimeError(f"nvcc failed for {src.name}:\n{r.stdout}\n{r.stderr}")
+    if "-v" in extra:
+        print(f"== {src.name}\n{r.stderr}", end="")
     return obj
 
 

@@ -407,18 +407,21 @@ static tf_status run_moe(const tf_moe_args* a, const MoePlan& p, cudaStream_t s)
   trace(PH_GATE_UP, true, s);
   if (tc_up) {
     // The tensor cores read the expert inputs as contiguous f16 rows in slot order.
-    TF_TRY(launch_gather_f16(a->x, a->hidden, a->act, p.order, a->top_k, N, a->hidden, p.op16, s));
+    TF_TRY(launch_gather_f16(a->x, a->hidden, a->act, p.order, a->top_k, N, a->hidden, p.op16, 1, s));
     up.x16 = p.op16;
+    up.x16_perm = 1;
     if (tc_dn) {  // h goes straight to the next tensor-core QMM in f16 storage
       up.y_f16 = 1;
       dn.x16 = p.h;
+      dn.x16_perm = 1;
     }
   }
   TF_TRY(launch_qmm(up, s));
   trace(PH_GATE_UP, false, s);
   if (tc_dn && !up.y_f16) {
-    TF_TRY(launch_gather_f16(p.h, a->intermediate, a->act, nullptr, 1, N, a->intermediate, p.op16, s));
+    TF_TRY(launch_gather_f16(p.h, a->intermediate, a->act, nullptr, 1, N, a->intermediate, p.op16, 1, s));
     dn.x16 = p.op16;
+    dn.x16_perm = 1;
   }
   trace(PH_DOWN, true, s);
   TF_TRY(launch_qmm(dn, s));
@@ -555,17 +558,20 @@ int tf_moe_expert_gpu(const void* x, int64_t x_rows, int32_t hidden, const int32
   d.y_stride = hidden;
   const bool tc_up = qmm_uses_tc(p), tc_dn = qmm_uses_tc(d);
   if (tc_up) {
-    TF_TRY(launch_gather_f16(x, hidden, act, xrow, 1, n, hidden, w.x16, s));
+    TF_TRY(launch_gather_f16(x, hidden, act, xrow, 1, n, hidden, w.x16, 1, s));
     p.x16 = w.x16;
+    p.x16_perm = 1;
     if (tc_dn) {
       p.y_f16 = 1;
       d.x16 = h;
+      d.x16_perm = 1;
     }
   }
   TF_TRY(launch_qmm(p, s));
   if (tc_dn && !p.y_f16) {
-    TF_TRY(launch_gather_f16(h, intermediate, act, nullptr, 1, n, intermediate, w.h16, s));
+    TF_TRY(launch_gather_f16(h, intermediate, act, nullptr, 1, n, intermediate, w.h16, 1, s));
     d.x16 = w.h16;
+    d.x16_perm = 1;
   }
   return launch_qmm(d, s);
 }

@@ -130,22 +130,22 @@ struct QmmProblem {
   int64_t residual_stride = 0;
   // Tensor-core operand: an f16 copy of the activations with contiguous rows
   // (dense bf16: x converted, same stride; grouped: slot-ordered rows of
-  // width in_features), and for EPI_SWIGLU whether y is written in f16.
+  // width in_features).  x16_perm: the copy holds each group of 8 columns in
+  // the order [0,4,1,5,2,6,3,7] (the tensor-core dequant's own order).
   const void* x16 = nullptr;
+  int x16_perm = 0;
+  // EPI_SWIGLU: y is written in f16 in the x16_perm order, as the operand of
+  // a following tensor-core QMM.
   int y_f16 = 0;
-  // Optional split-K workspace for dense tensor-core problems with few tiles
-  // (fp32 partials, then 1024 int counters at its end that must be zero
-  // before first use; each launch leaves them zero again).
-  void* splitk_ws = nullptr;
-  size_t splitk_bytes = 0;
 };
-constexpr size_t kSplitKWorkspaceBytes = (size_t)16 << 20;
 // Path launch_qmm would take for this problem (true = tensor cores).
 bool qmm_uses_tc(const QmmProblem& p);
-tf_status launch_bf16_to_f16(const void* x, int64_t n, void* y, cudaStream_t s);
-// y[i][:] = f16(x[perm ? perm[i] / div : i][:]) for i < rows (tensor-core operand).
+// f16 copy of n bf16 values (rows of 2048), optionally in the x16_perm order.
+tf_status launch_bf16_to_f16(const void* x, int64_t n, void* y, int permute, cudaStream_t s);
+// y[i][:] = f16(x[perm ? perm[i] / div : i][:]) for i < rows (tensor-core
+// operand), optionally in the x16_perm column order.
 tf_status launch_gather_f16(const void* x, int64_t x_stride, int act, const int32_t* perm, int div, int64_t rows,
-                            int width, void* y, cudaStream_t s);
+                            int width, void* y, int permute, cudaStream_t s);
 // Dispatches to the tensor-core kernel (launch_qmm_tc) when the problem has
 // enough tokens per weight matrix, else to the CUDA-core GEMV.
 tf_status launch_qmm(const QmmProblem& p, cudaStream_t s);

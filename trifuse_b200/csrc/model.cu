@@ -139,7 +139,6 @@ struct tf_session {
   void* qkv = nullptr;
   void* attn = nullptr;
   void* x16 = nullptr;  // f16 operand copy (bf16 models, tensor-core projections)
-  void* splitk = nullptr;  // split-K partials + counters for the dense projections
   int64_t* ids = nullptr;
   int32_t* pos = nullptr;
   int32_t* req = nullptr;
@@ -365,7 +364,6 @@ int tf_session_create(tf_model* model, int32_t max_batch, int32_t capacity, int3
     s->qkv = k.take<char>((size_t)R * (W + 2 * Wkv) * 2);
     s->attn = k.take<char>((size_t)R * W * 2);
     s->x16 = k.take<char>((size_t)R * (H > W ? H : W) * 2);
-    s->splitk = k.take<char>(kSplitKWorkspaceBytes);
     s->ids = k.take<int64_t>((size_t)R * 8);
     s->pos = k.take<int32_t>((size_t)R * 4);
     s->req = k.take<int32_t>((size_t)R * 4);
@@ -390,14 +388,6 @@ int tf_session_create(tf_model* model, int32_t max_batch, int32_t capacity, int3
   }
   Carve real(s->scratch, cv.used);
   plan(real);
-  // Split-K tile counters start at zero; every launch leaves them zero.
-  e = cudaMemset(s->splitk, 0, kSplitKWorkspaceBytes);
-  if (e != cudaSuccess) {
-    cudaFree(s->kv);
-    cudaFree(s->scratch);
-    delete s;
-    return set_error(TF_ERR_CUDA, "session scratch init: %s", cudaGetErrorString(e));
-  }
   for (int l = 0; l < c.layers; ++l) {
     s->k.push_back(s->kv + per_cache * (2 * l));
     s->v.push_back(s->kv + per_cache * (2 * l + 1));
@@ -460,13 +450,13 @@ int tf_session_reset(tf_session* s) {
 namespace {
 
 // Dense projection; with bf16 activations on the tensor-core path the input
-// rows are first copied to f16 (the MMA operand dtype).
+// rows are first copied to f16 (the MMA operand dtype) in the tensor-core
+// operand order.  f16 activations are read in place.
 tf_status dense_qmm(tf_session* s, QmmProblem& q, int64_t x_rows, cudaStream_t st) {
-  q.splitk_ws = s->splitk;
-  q.splitk_bytes = kSplitKWorkspaceBytes;
   if (q.act == TF_DTYPE_BF16 && qmm_uses_tc(q)) {
-    TF_TRY(launch_bf16_to_f16(q.x, x_rows * q.x_stride, s->x16, st));
+    TF_TRY(launch_bf16_to_f16(q.x, x_rows * q.x_stride, s->x16, 1, st));
     q.x16 = s->x16;
+    q.x16_perm = 1;
   }
   return launch_qmm(q, st);
 }

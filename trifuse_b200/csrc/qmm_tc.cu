@@ -13,22 +13,37 @@
 // native_affine_ops.py:36); activations arrive in f16 (bf16 models pass an
 // exact f16 copy).
 //
-// Persistent, warp-specialized block (448 threads, one block per SM):
-//   warp 12 (loader)  one thread issues every TMA: packed codes of a k-step
-//                     (box 8 words x 128 rows) into a PK-deep ring, the
-//                     tile's scales/biases (two slots), and the activation
-//                     tile (box 64 x NT, 128B-swizzled = the MMA's K-major
-//                     layout) into an SB-deep ring.
-//   warps 0-7 (dequant) two threads per A row turn 16 packed bytes into 32
-//                     f16 weights (magic-number half2 extraction + HFMA2)
-//                     and store them 128B-swizzled into an SA-deep A ring.
-//   warp 13 (MMA)     allocates 2 x NT TMEM columns; lane 0 issues
+// Persistent, warp-specialized block (480 threads, one block per SM).  Work
+// moves in stages of KS k-steps (a k-step is 64 inputs = one quantization
+// group):
+//   warp 12 (code loader)  TMA of each stage's packed codes (box 8*KS words x
+//                     128 rows) into a PK-deep ring, and of the scales and
+//                     biases of every 8 k-steps (box 8 x 128) into two slots.
+//   warp 14 (activation loader)  TMA of each stage's activation tiles (box
+//                     64 x NT, 128B-swizzled = the MMA's K-major layout).
+//   warps 0-7 (dequant) two threads per A row turn packed words into f16
+//                     weights (magic-number half2 extraction + HFMA2) and
+//                     store them 128B-swizzled into the SA-deep stage ring.
+//   warp 13 (MMA)     allocates 2 x NT TMEM columns; one elected lane issues
 //                     tcgen05.mma (4 x K=16 per k-step) into one of two
-//                     accumulators and commits stage releases.
+//                     accumulators and one commit per stage.
 //   warps 8-11 (epilogue) tcgen05.ld the finished accumulator while the next
 //                     tile accumulates into the other one; SwiGLU tiles keep
 //                     gate row j and up row j in adjacent TMEM lanes, so one
 //                     shuffle pairs them.
+// A stage's A tile (dequant warps) and B tile (activation TMA) complete one
+// barrier, which the MMA warp waits on once per stage; one commit releases
+// both.  Small-N decode tiles give the tensor core little work per k-step,
+// so the number of barrier round trips per k-step sets the pace there.
+//
+// Operand order: with PERM the dequant writes each group of 8 inputs in the
+// order [0,4,1,5,2,6,3,7] (what the magic-number extraction yields without
+// byte permutes), and the activation operand was written in the same order
+// by its producer (gather_f16 / the SwiGLU epilogue with y_f16); without
+// PERM the dequant regroups to natural order with byte permutes.  A dot
+// product does not depend on the order of its terms' positions, only on both
+// operands using the same one; the tensor core's f32 accumulation order over
+// K is not specified either way.
 // Tiles are (token block, row block) pairs, enumerated token-block-major so
 // blocks working at the same time share the activation tile through L2.
 // Every wait is bounded (about one second of SM clock); an expired wait
@@ -51,23 +66,26 @@ namespace tc {
 
 constexpr int kDeqWarps = 8;
 constexpr int kEpiWarps = 4;
-constexpr int kLoadWarp = kDeqWarps + kEpiWarps;  // 12
+constexpr int kLoadWarp = kDeqWarps + kEpiWarps;  // 12: packed codes + scales
 constexpr int kMmaWarp = kLoadWarp + 1;           // 13
-constexpr int kThreads = (kMmaWarp + 1) * 32;     // 448
-constexpr int kDeqThreads = kDeqWarps * 32;
-constexpr int kEpiThreads = kEpiWarps * 32;
+constexpr int kActWarp = kMmaWarp + 1;            // 14: activation tiles
+constexpr int kThreads = (kActWarp + 1) * 32;     // 480
 constexpr int kM = 128;
 constexpr int kKStep = 64;
+constexpr int kSK = 8;          // k-steps per scale slot (16 bytes of f16 per row)
 constexpr int kMaxTiles = 256;  // per-block tile table
 constexpr long long kWaitCycles = 2000000000LL;
+// try_wait suspends the thread until the phase completes or this many ns
+// pass, so a waiting role takes no issue slots from the dequant warps.
+constexpr uint32_t kSuspendNs = 1000000;
 
 struct TileInfo {
   int e, s0, cnt, rb;
 };
 
 struct Params {
-  CUtensorMap tm_q0, tm_q1;  // packed codes, box {8 words, 128 (or 64) rows}
-  CUtensorMap tm_s0, tm_s1;  // scales, box {groups, 128 (or 64) rows}
+  CUtensorMap tm_q0, tm_q1;  // packed codes, box {8*KS words, 128 (or 64) rows}
+  CUtensorMap tm_s0, tm_s1;  // scales, box {8 groups, 128 (or 64) rows}
   CUtensorMap tm_b0, tm_b1;  // biases
   CUtensorMap tm_x;          // f16 activations [rows][in], box {64, NT}, 128B swizzle
   const int32_t* offsets;
@@ -103,10 +121,10 @@ __device__ __forceinline__ bool mbar_try(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(ok)
-      : "r"(smem_addr(bar)), "r"(parity)
+      : "r"(smem_addr(bar)), "r"(parity), "r"(kSuspendNs)
       : "memory");
   return ok != 0;
 }
@@ -124,6 +142,10 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
     }
   }
   return true;
+}
+// Warp-uniform bounded wait (every lane waits; all agree on the result).
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volatile int* abort, int code) {
+  return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort, code));
 }
 __device__ __forceinline__ void tma_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
   asm volatile(
@@ -151,51 +173,95 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
 __device__ __forceinline__ uint32_t idesc_f16(int m, int n) {
   return (1u << 4) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
 }
-__device__ __forceinline__ void mma_f16(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
-  uint32_t m0 = 0, m1 = 0, m2 = 0, m3 = 0;
+// One lane of a converged warp (elect.sync picks the same lane every time).
+// The MMA warp runs its loop with all 32 lanes so that descriptors and
+// indices stay warp-uniform; only the elected lane issues tcgen05 work, and
+// tcgen05.commit tracks the MMAs that this same lane issued.
+__device__ __forceinline__ uint32_t elect_one() {
+  uint32_t e;
   asm volatile(
-      "{\n\t.reg .pred p;\n\t"
+      "{\n\t.reg .pred e;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "selp.u32 %0, 1, 0, e;\n\t}"
+      : "=r"(e));
+  return e;
+}
+__device__ __forceinline__ void mma_f16(uint32_t leader, uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc,
+                                        uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p, e;\n\t"
       "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}" ::"r"(tmem_d),
-      "l"(a), "l"(b), "r"(idesc), "r"(acc), "r"(m0), "r"(m1), "r"(m2), "r"(m3)
+      "setp.ne.b32 e, %5, 0;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(a), "l"(b), "r"(idesc), "r"(acc), "r"(leader)
       : "memory");
 }
-__device__ __forceinline__ void mma_commit(uint64_t* bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_addr(bar))
-               : "memory");
+__device__ __forceinline__ void mma_commit(uint32_t leader, uint64_t* bar) {
+  asm volatile(
+      "{\n\t.reg .pred e;\n\t"
+      "setp.ne.b32 e, %1, 0;\n\t"
+      "@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}" ::"r"(smem_addr(bar)),
+      "r"(leader)
+      : "memory");
 }
+// The destination registers of tcgen05.ld are valid only after
+// tcgen05.wait::ld; both sit in one asm statement so that no use of the
+// outputs can be scheduled between them.
 __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
   uint32_t r[16];
   asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
       : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
         "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-      : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+      : "r"(taddr)
+      : "memory");
 #pragma unroll
   for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
-// Eight codes of one packed word -> eight f16 weights fp16(code*s + b) in k
-// order.  (w >> 4i) & 0x000F000F | 0x64006400 is the f16 pair (1024 + c_i,
-// 1024 + c_{i+4}); byte_perm regroups the pairs as (c0,c1) (c2,c3) (c4,c5)
-// (c6,c7); subtracting 1024 is exact and one HFMA2 rounds c*s + b once.
+// Eight codes of one packed word (code i at bits 4i) -> eight f16 weights
+// fp16(code*s + b).  The f16 halves of
+//   t0 = w & 0x000F000F | 0x6400 (1024 + c0, 1024 + c4)
+//   t1 = w & 0x00F000F0 | 0x5400 (  64 + c1,   64 + c5)   [ulp of 64 is 1/16]
+//   t2, t3 = the same on w >> 8  (c2, c6) and (c3, c7)
+// are exact; subtracting the magic is exact and one HFMA2 rounds c*s + b
+// once.  PERM keeps the pairs as they come (order 0,4,1,5,2,6,3,7: one shift
+// and four LOP3 per word); otherwise four byte permutes restore 0..7.
+template <bool PERM>
 __device__ __forceinline__ uint4 dequant8(uint32_t w, __half2 s2, __half2 b2) {
+  const uint32_t w8 = w >> 8;
   const uint32_t t0 = (w & 0x000F000Fu) | 0x64006400u;
-  const uint32_t t1 = ((w >> 4) & 0x000F000Fu) | 0x64006400u;
-  const uint32_t t2 = ((w >> 8) & 0x000F000Fu) | 0x64006400u;
-  const uint32_t t3 = ((w >> 12) & 0x000F000Fu) | 0x64006400u;
-  const uint32_t q[4] = {__byte_perm(t0, t1, 0x5410), __byte_perm(t2, t3, 0x5410), __byte_perm(t0, t1, 0x7632),
-                         __byte_perm(t2, t3, 0x7632)};
-  const __half2 k1024 = __half2half2(__ushort_as_half(0x6400));
+  const uint32_t t1 = (w & 0x00F000F0u) | 0x54005400u;
+  const uint32_t t2 = (w8 & 0x000F000Fu) | 0x64006400u;
+  const uint32_t t3 = (w8 & 0x00F000F0u) | 0x54005400u;
+  uint32_t q[4];
+  __half2 m[4];
+  if (PERM) {
+    q[0] = t0, q[1] = t1, q[2] = t2, q[3] = t3;
+    const __half2 hi = __half2half2(__ushort_as_half(0x6400)), lo = __half2half2(__ushort_as_half(0x5400));
+    m[0] = hi, m[1] = lo, m[2] = hi, m[3] = lo;
+  } else {
+    q[0] = __byte_perm(t0, t1, 0x5410);  // (c0, c1)
+    q[1] = __byte_perm(t2, t3, 0x5410);  // (c2, c3)
+    q[2] = __byte_perm(t0, t1, 0x7632);  // (c4, c5)
+    q[3] = __byte_perm(t2, t3, 0x7632);  // (c6, c7)
+    const __half2 mm = __halves2half2(__ushort_as_half(0x6400), __ushort_as_half(0x5400));
+    m[0] = m[1] = m[2] = m[3] = mm;
+  }
   uint32_t o[4];
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
-    const __half2 n = __hsub2(*reinterpret_cast<const __half2*>(&q[i]), k1024);
+    const __half2 n = __hsub2(*reinterpret_cast<const __half2*>(&q[i]), m[i]);
     const __half2 h = __hfma2(n, s2, b2);
     o[i] = *reinterpret_cast<const uint32_t*>(&h);
   }
   return make_uint4(o[0], o[1], o[2], o[3]);
+}
+// Column of element f in an operand written in the PERM order.
+__host__ __device__ __forceinline__ int perm_col(int f) {
+  const int q = f & 7;
+  return (f & ~7) | ((q & 3) << 1) | (q >> 2);
 }
 
 // Tile t -> (expert, first slot, token count, row block); e = -1 past the end.
@@ -245,46 +311,45 @@ __device__ TileInfo lookup_tile(const Params& p, int64_t t, int nt, int lane) {
   return ti;
 }
 
-template <int NT, int PK, int SA, int SB>
+template <int NT, int KS, int PK, int SA>
 struct Layout {
-  static constexpr int kP = kM * 32;   // packed codes of one k-step
-  static constexpr int kA = kM * 128;  // f16 A tile
-  static constexpr int kB = NT * 128;  // f16 activation tile
+  static constexpr int kP = kM * 32 * KS;     // packed codes of one stage
+  static constexpr int kS = 2 * kM * kSK * 2;  // scales | biases of 8 k-steps
+  static constexpr int kA = kM * 128 * KS;     // f16 A stage (KS swizzled 128 x 64 tiles)
+  static constexpr int kB = NT * 128 * KS;     // f16 activation stage
   static constexpr int kHead = 1024 + kMaxTiles * 16;
-  __host__ __device__ static size_t scales(int in) { return (size_t)2 * 2 * kM * (in / 64) * 2; }
-  __host__ __device__ static size_t off_scales() { return kHead; }
-  __host__ __device__ static size_t off_p(int in) { return (kHead + scales(in) + 1023) / 1024 * 1024; }
-  __host__ __device__ static size_t off_a(int in) { return off_p(in) + (size_t)PK * kP; }
-  __host__ __device__ static size_t off_b(int in) { return off_a(in) + (size_t)SA * kA; }
-  __host__ __device__ static size_t bytes(int in) { return off_b(in) + (size_t)SB * kB + 1024; }
+  static constexpr int kOffS = kHead;
+  static constexpr int kOffP = (kOffS + 2 * kS + 1023) / 1024 * 1024;
+  static constexpr int kOffA = kOffP + PK * kP;
+  static constexpr int kOffB = kOffA + SA * kA;
+  static constexpr int kBytes = kOffB + SA * kB + 1024;  // + alignment slack
+  static_assert(kP % 1024 == 0 && kA % 1024 == 0 && kB % 1024 == 0, "stage sizes keep 1024-byte alignment");
+  static_assert(kSK % KS == 0, "a scale slot holds whole stages");
 };
 
-template <typename T, int EPI, int NT, int PK, int SA, int SB>
+template <typename T, int EPI, bool PERM, int NT, int KS, int PK, int SA>
 __global__ void __launch_bounds__(kThreads, 1) qmm_tc_kernel(const __grid_constant__ Params p) {
-  using L = Layout<NT, PK, SA, SB>;
+  using L = Layout<NT, KS, PK, SA>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* p_full = reinterpret_cast<uint64_t*>(base);
   uint64_t* p_empty = p_full + PK;
   uint64_t* s_full = p_empty + PK;
   uint64_t* s_empty = s_full + 2;
-  uint64_t* a_full = s_empty + 2;
-  uint64_t* a_empty = a_full + SA;
-  uint64_t* b_full = a_empty + SA;
-  uint64_t* b_empty = b_full + SB;
-  uint64_t* acc_full = b_empty + SB;
+  uint64_t* ab_full = s_empty + 2;
+  uint64_t* ab_empty = ab_full + SA;
+  uint64_t* acc_full = ab_empty + SA;
   uint64_t* acc_empty = acc_full + 2;
   uint64_t* drain = acc_empty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   int* ntiles_s = const_cast<int*>(abort_flag) + 1;
   TileInfo* table = reinterpret_cast<TileInfo*>(base + 1024);
-  __half* scl = reinterpret_cast<__half*>(base + L::off_scales());  // [2 slots][s | b][kM][G]
-  uint8_t* ring_p = base + L::off_p(p.in);
-  uint8_t* ring_a = base + L::off_a(p.in);
-  uint8_t* ring_b = base + L::off_b(p.in);
-  const int G = p.in / 64;
-  const int nk = p.in / kKStep;
+  uint8_t* ring_s = base + L::kOffS;  // [2 slots][s | b][kM rows][8 k-steps] f16
+  uint8_t* ring_p = base + L::kOffP;
+  uint8_t* ring_a = base + L::kOffA;
+  uint8_t* ring_b = base + L::kOffB;
+  const int nk = p.in / kKStep;  // a multiple of 8
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   constexpr uint32_t kTmemCols = 2 * NT < 32 ? 32 : 2 * NT;
 
@@ -292,21 +357,17 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_tc_kernel(const __grid_consta
   if (tid == 0) {
     for (int i = 0; i < PK; ++i) {
       mbar_init(&p_full[i], 1);
-      mbar_init(&p_empty[i], kDeqThreads);
+      mbar_init(&p_empty[i], kDeqWarps);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
-      mbar_init(&s_empty[i], kDeqThreads);
+      mbar_init(&s_empty[i], kDeqWarps);
       mbar_init(&acc_full[i], 1);
-      mbar_init(&acc_empty[i], kEpiThreads);
+      mbar_init(&acc_empty[i], kEpiWarps);
     }
     for (int i = 0; i < SA; ++i) {
-      mbar_init(&a_full[i], kDeqThreads);
-      mbar_init(&a_empty[i], 1);
-    }
-    for (int i = 0; i < SB; ++i) {
-      mbar_init(&b_full[i], 1);
-      mbar_init(&b_empty[i], 1);
+      mbar_init(&ab_full[i], kDeqWarps + 1);  // dequant warps + the activation loader's expect_tx
+      mbar_init(&ab_empty[i], 1);
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -337,119 +398,147 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_tc_kernel(const __grid_consta
   constexpr int kTileRows = kSw ? kM / 2 : kM;  // rows of each weight matrix per tile
 
   if (warp == kLoadWarp) {
-    // ---- loader: lane 0 streams packed codes (PK ahead of the dequant warps)
-    // and each tile's scales; lane 1 streams activation tiles (SB ahead of
-    // the MMA).  Separate issuers keep the weight stream from waiting on the
-    // MMA, so up to PK k-steps of codes are in flight.
+    // ---- code loader: lane 0 streams packed codes (PK stages ahead of the
+    // dequant warps) and the scales of every 8 k-steps.  Activation tiles
+    // have their own warp, so the weight stream never waits on the MMA.
     if (lane == 0) {
-      int64_t g = 0;
+      int64_t g = 0, gs = 0;
       bool ok = true;
       for (int li = 0; li < ntiles && ok; ++li) {
         const TileInfo ti = table[li];
         const int row0 = ti.e * p.out + ti.rb * kTileRows;
-        const int ss = li & 1;
-        if (li >= 2) ok = mbar_wait(&s_empty[ss], ((li >> 1) - 1) & 1, abort_flag, 11);
-        if (!ok) break;
-        __half* sdst = scl + (size_t)ss * 2 * kM * G;
-        mbar_expect_tx(&s_full[ss], (uint32_t)(2 * kM * G * 2));
-        tma_2d(sdst, &p.tm_s0, 0, row0, &s_full[ss]);
-        tma_2d(sdst + (size_t)kM * G, &p.tm_b0, 0, row0, &s_full[ss]);
-        if (kSw) {
-          tma_2d(sdst + (size_t)64 * G, &p.tm_s1, 0, row0, &s_full[ss]);
-          tma_2d(sdst + (size_t)kM * G + (size_t)64 * G, &p.tm_b1, 0, row0, &s_full[ss]);
-        }
-        for (int k = 0; k < nk && ok; ++k, ++g) {
-          const int ps = (int)(g % PK);
-          if (g >= PK) ok = mbar_wait(&p_empty[ps], (uint32_t)(((g / PK) - 1) & 1), abort_flag, 12);
-          if (!ok) break;
-          uint8_t* pdst = ring_p + (size_t)ps * L::kP;
-          mbar_expect_tx(&p_full[ps], (uint32_t)L::kP);
-          tma_2d(pdst, &p.tm_q0, k * 8, row0, &p_full[ps]);
-          if (kSw) tma_2d(pdst + 64 * 32, &p.tm_q1, k * 8, row0, &p_full[ps]);
-        }
-      }
-    } else if (lane == 1) {
-      int64_t g = 0;
-      bool ok = true;
-      for (int li = 0; li < ntiles && ok; ++li) {
-        const int s0 = table[li].s0;
-        for (int k = 0; k < nk && ok; ++k, ++g) {
-          const int bs = (int)(g % SB);
-          if (g >= SB) ok = mbar_wait(&b_empty[bs], (uint32_t)(((g / SB) - 1) & 1), abort_flag, 13);
-          if (!ok) break;
-          mbar_expect_tx(&b_full[bs], (uint32_t)L::kB);
-          tma_2d(ring_b + (size_t)bs * L::kB, &p.tm_x, k * kKStep, s0, &b_full[bs]);
+        for (int k8 = 0; k8 < nk && ok; k8 += kSK, ++gs) {
+          const int ss = (int)(gs & 1);
+          if (gs >= 2 && !(ok = mbar_wait(&s_empty[ss], (uint32_t)(((gs >> 1) - 1) & 1), abort_flag, 11))) break;
+          uint8_t* sdst = ring_s + (size_t)ss * L::kS;
+          mbar_expect_tx(&s_full[ss], (uint32_t)L::kS);
+          tma_2d(sdst, &p.tm_s0, k8, row0, &s_full[ss]);
+          tma_2d(sdst + kM * kSK * 2, &p.tm_b0, k8, row0, &s_full[ss]);
+          if (kSw) {
+            tma_2d(sdst + 64 * kSK * 2, &p.tm_s1, k8, row0, &s_full[ss]);
+            tma_2d(sdst + kM * kSK * 2 + 64 * kSK * 2, &p.tm_b1, k8, row0, &s_full[ss]);
+          }
+          for (int ks = 0; ks < kSK && ok; ks += KS, ++g) {
+            const int ps = (int)(g % PK);
+            if (g >= PK && !(ok = mbar_wait(&p_empty[ps], (uint32_t)(((g / PK) - 1) & 1), abort_flag, 12))) break;
+            uint8_t* pdst = ring_p + (size_t)ps * L::kP;
+            mbar_expect_tx(&p_full[ps], (uint32_t)L::kP);
+            tma_2d(pdst, &p.tm_q0, (k8 + ks) * 8, row0, &p_full[ps]);
+            if (kSw) tma_2d(pdst + 64 * 32 * KS, &p.tm_q1, (k8 + ks) * 8, row0, &p_full[ps]);
+          }
         }
       }
     }
-  } else if (warp < kDeqWarps) {
-    // ---- dequant: thread pair per A row, 4 words each per k-step
-    const int r = tid >> 1, h = tid & 1;
-    // A row r <- packed/scale row pr.  SwiGLU tiles interleave gate row j
-    // (A row 2j) and up row j (A row 2j+1); the packed slot holds gate rows
-    // 0..63 then up rows 64..127.
-    const int pr = kSw ? ((r & 1) * 64 + (r >> 1)) : r;
-    int64_t g = 0;
-    bool ok = true;
-    for (int li = 0; li < ntiles && ok; ++li) {
-      const int ss = li & 1;
-      ok = mbar_wait(&s_full[ss], (li >> 1) & 1, abort_flag, 21);
-      if (!ok) break;
-      const __half* srow = scl + (size_t)ss * 2 * kM * G + (size_t)pr * G;
-      const __half* brow = srow + (size_t)kM * G;
-      for (int k = 0; k < nk; ++k, ++g) {
-        const int ps = (int)(g % PK);
-        if (!(ok = mbar_wait(&p_full[ps], (uint32_t)((g / PK) & 1), abort_flag, 22))) break;
-        const uint4 words = *reinterpret_cast<const uint4*>(ring_p + (size_t)ps * L::kP + pr * 32 + h * 16);
-        const __half2 s2 = __half2half2(srow[k]);
-        const __half2 b2 = __half2half2(brow[k]);
-        mbar_arrive(&p_empty[ps]);
-        const int as = (int)(g % SA);
-        if (g >= SA && !(ok = mbar_wait(&a_empty[as], (uint32_t)(((g / SA) - 1) & 1), abort_flag, 23))) break;
-        uint8_t* arow = ring_a + (size_t)as * L::kA + r * 128;
-        const uint32_t wv[4] = {words.x, words.y, words.z, words.w};
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const int ch = 4 * h + i;
-          *reinterpret_cast<uint4*>(arow + ((ch ^ (r & 7)) << 4)) = dequant8(wv[i], s2, b2);
-        }
-        fence_proxy_async();
-        mbar_arrive(&a_full[as]);
-      }
-      if (ok) mbar_arrive(&s_empty[ss]);
-    }
-  } else if (warp == kMmaWarp) {
-    // ---- MMA issuer
+  } else if (warp == kActWarp) {
+    // ---- activation loader: lane 0 streams each stage's activation tiles
+    // (SA stages ahead of the MMA); its expect_tx is one of the stage
+    // barrier's arrivals.
     if (lane == 0) {
       int64_t g = 0;
       bool ok = true;
       for (int li = 0; li < ntiles && ok; ++li) {
-        const TileInfo ti = table[li];
-        const int buf = li & 1;
-        if (li >= 2 && !(ok = mbar_wait(&acc_empty[buf], ((li >> 1) - 1) & 1, abort_flag, 31))) break;
-        tc_fence_after();
-        const int n_mma = (ti.cnt + 15) / 16 * 16;
-        const uint32_t idesc = idesc_f16(kM, n_mma);
-        const uint32_t d = tmem + (uint32_t)(buf * NT);
-        for (int k = 0; k < nk; ++k, ++g) {
-          const int as = (int)(g % SA), bs = (int)(g % SB);
-          if (!(ok = mbar_wait(&a_full[as], (uint32_t)((g / SA) & 1), abort_flag, 32))) break;
-          if (!(ok = mbar_wait(&b_full[bs], (uint32_t)((g / SB) & 1), abort_flag, 33))) break;
-          tc_fence_after();
-          const uint32_t aa = smem_addr(ring_a + (size_t)as * L::kA);
-          const uint32_t ba = smem_addr(ring_b + (size_t)bs * L::kB);
+        const int s0 = table[li].s0;
+        for (int k = 0; k < nk && ok; k += KS, ++g) {
+          const int as = (int)(g % SA);
+          if (g >= SA && !(ok = mbar_wait(&ab_empty[as], (uint32_t)(((g / SA) - 1) & 1), abort_flag, 13))) break;
+          uint8_t* bdst = ring_b + (size_t)as * L::kB;
+          mbar_expect_tx(&ab_full[as], (uint32_t)L::kB);
 #pragma unroll
-          for (int j = 0; j < kKStep / 16; ++j)
-            mma_f16(d, sw128_desc(aa + 32 * j), sw128_desc(ba + 32 * j), idesc, (k > 0 || j > 0) ? 1u : 0u);
-          mma_commit(&a_empty[as]);
-          mma_commit(&b_empty[bs]);
+          for (int kk = 0; kk < KS; ++kk) tma_2d(bdst + kk * NT * 128, &p.tm_x, (k + kk) * kKStep, s0, &ab_full[as]);
         }
-        if (ok) mma_commit(&acc_full[buf]);
       }
-      // Every MMA issued by this thread completes before TMEM is released.
-      mma_commit(drain);
-      mbar_wait(drain, 0, abort_flag, 34);
     }
+  } else if (warp < kDeqWarps) {
+    // ---- dequant: thread pair per A row, 4 words each per k-step.  Every
+    // lane waits on the full barriers (warp-uniform result); one lane per
+    // warp arrives on the release barriers after __syncwarp (the barriers
+    // count warps).
+    const int r = tid >> 1, h = tid & 1;
+    // A row r <- packed/scale row pr.  SwiGLU tiles interleave gate row j
+    // (A row 2j) and up row j (A row 2j+1); the packed and scale slots hold
+    // gate rows 0..63 then up rows 64..127.
+    const int pr = kSw ? ((r & 1) * 64 + (r >> 1)) : r;
+    const int swz = r & 7;
+    int64_t g = 0, gs = 0;
+    bool ok = true;
+    for (int li = 0; li < ntiles && ok; ++li) {
+      for (int k8 = 0; k8 < nk && ok; k8 += kSK, ++gs) {
+        const int ss = (int)(gs & 1);
+        if (!(ok = warp_wait(&s_full[ss], (uint32_t)((gs >> 1) & 1), abort_flag, 21))) break;
+        const uint8_t* sslot = ring_s + (size_t)ss * L::kS;
+        const uint4 sv = *reinterpret_cast<const uint4*>(sslot + pr * 16);
+        const uint4 bv = *reinterpret_cast<const uint4*>(sslot + kM * kSK * 2 + pr * 16);
+        const __half* sh = reinterpret_cast<const __half*>(&sv);
+        const __half* bh = reinterpret_cast<const __half*>(&bv);
+#pragma unroll
+        for (int ks = 0; ks < kSK; ks += KS, ++g) {
+          const int ps = (int)(g % PK);
+          if (!(ok = warp_wait(&p_full[ps], (uint32_t)((g / PK) & 1), abort_flag, 22))) break;
+          uint4 wv[KS];
+#pragma unroll
+          for (int kk = 0; kk < KS; ++kk)
+            wv[kk] = *reinterpret_cast<const uint4*>(ring_p + (size_t)ps * L::kP + pr * (32 * KS) + kk * 32 + h * 16);
+          const int as = (int)(g % SA);
+          if (g >= SA && !(ok = warp_wait(&ab_empty[as], (uint32_t)(((g / SA) - 1) & 1), abort_flag, 23))) break;
+          uint8_t* arow = ring_a + (size_t)as * L::kA + r * 128;
+#pragma unroll
+          for (int kk = 0; kk < KS; ++kk) {
+            const __half2 s2 = __half2half2(sh[ks + kk]);
+            const __half2 b2 = __half2half2(bh[ks + kk]);
+            const uint32_t w4[4] = {wv[kk].x, wv[kk].y, wv[kk].z, wv[kk].w};
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+              *reinterpret_cast<uint4*>(arow + kk * (kM * 128) + (((4 * h + i) ^ swz) << 4)) =
+                  dequant8<PERM>(w4[i], s2, b2);
+          }
+          fence_proxy_async();
+          __syncwarp();
+          // The packed words were consumed above, so every lane's shared
+          // loads of this slot have completed before it is released (a
+          // release right after issuing the loads let the next TMA fill
+          // overtake a load still in flight on another lane).
+          if (lane == 0) {
+            mbar_arrive(&ab_full[as]);
+            mbar_arrive(&p_empty[ps]);
+          }
+        }
+        // Scales and biases of this block were consumed by the stages above.
+        __syncwarp();
+        if (ok && lane == 0) mbar_arrive(&s_empty[ss]);
+      }
+    }
+  } else if (warp == kMmaWarp) {
+    // ---- MMA issuer (whole warp, one elected lane issues)
+    const uint32_t leader = elect_one();
+    int64_t g = 0;
+    bool ok = true;
+    for (int li = 0; li < ntiles && ok; ++li) {
+      const TileInfo ti = table[li];
+      const int buf = li & 1;
+      if (li >= 2 && !(ok = warp_wait(&acc_empty[buf], (uint32_t)(((li >> 1) - 1) & 1), abort_flag, 31))) break;
+      tc_fence_after();
+      const int n_mma = (ti.cnt + 15) / 16 * 16;
+      const uint32_t idesc = idesc_f16(kM, n_mma);
+      const uint32_t d = tmem + (uint32_t)(buf * NT);
+      for (int k = 0; k < nk; k += KS, ++g) {
+        const int as = (int)(g % SA);
+        if (!(ok = warp_wait(&ab_full[as], (uint32_t)((g / SA) & 1), abort_flag, 32))) break;
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < KS; ++kk) {
+          const uint64_t ad = sw128_desc(smem_addr(ring_a + (size_t)as * L::kA + kk * (kM * 128)));
+          const uint64_t bd = sw128_desc(smem_addr(ring_b + (size_t)as * L::kB + kk * (NT * 128)));
+#pragma unroll
+          for (int j = 0; j < kKStep / 16; ++j)  // +32 B per K=16 slice = +2 in the address field
+            mma_f16(leader, d, ad + 2 * j, bd + 2 * j, idesc, (k + kk > 0 || j > 0) ? 1u : 0u);
+        }
+        mma_commit(leader, &ab_empty[as]);
+      }
+      if (ok) mma_commit(leader, &acc_full[buf]);
+    }
+    // Every MMA issued by this warp completes before TMEM is released.
+    mma_commit(leader, drain);
+    mbar_wait(drain, 0, abort_flag, 34);
   } else {
     // ---- epilogue: warps 8-11 read TMEM lane quarters 0-3
     const int q = tid - kDeqWarps * 32;  // TMEM lane 0..127
@@ -458,10 +547,7 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_tc_kernel(const __grid_consta
     for (int li = 0; li < ntiles && ok; ++li) {
       const TileInfo ti = table[li];
       const int buf = li & 1;
-      ok = mbar_wait(&acc_full[buf], (li >> 1) & 1, abort_flag, 41);
-      // Keep every thread of the warp on the same path for tcgen05.ld.
-      ok = __all_sync(0xffffffffu, ok);
-      if (!ok) break;
+      if (!(ok = warp_wait(&acc_full[buf], (uint32_t)((li >> 1) & 1), abort_flag, 41))) break;
       tc_fence_after();
       const int n_mma = (ti.cnt + 15) / 16 * 16;
       const uint32_t taddr = tmem + ((uint32_t)(wq * 32) << 16) + (uint32_t)(buf * NT);
@@ -470,6 +556,7 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_tc_kernel(const __grid_consta
         tmem_ld16(taddr + c0, v);
         if (kSw) {
           const int f = ti.rb * (kM / 2) + (q >> 1);
+          const int fo = p.y_f16 ? perm_col(f) : f;  // an f16 operand for the next tensor-core QMM
 #pragma unroll
           for (int i = 0; i < 16; ++i) {
             const float other = __shfl_xor_sync(0xffffffffu, v[i], 1);
@@ -479,15 +566,26 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_tc_kernel(const __grid_consta
               const float uu = round_act<T>(other);
               const float sl = round_act<T>(gg / (1.0f + expf(-gg)));
               const float hv = round_act<T>(sl * uu);
-              const int64_t at = (int64_t)(ti.s0 + tok) * p.y_stride + f;
+              const int64_t row = (int64_t)(ti.s0 + tok) * p.y_stride;
               if (p.y_f16)
-                static_cast<__half*>(p.y)[at] = __float2half_rn(hv);
+                static_cast<__half*>(p.y)[row + fo] = __float2half_rn(hv);
               else
-                static_cast<T*>(p.y)[at] = from_f<T>(hv);
+                static_cast<T*>(p.y)[row + f] = from_f<T>(hv);
             }
           }
         } else {
           const int f = ti.rb * kM + q;
+          float res[16];
+          if (EPI == EPI_RESIDUAL) {
+            // All 16 residual loads before any store (y may alias residual).
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              const int tok = c0 + i;
+              res[i] = tok < ti.cnt && f < p.out
+                           ? to_f(static_cast<const T*>(p.residual)[(int64_t)(ti.s0 + tok) * p.residual_stride + f])
+                           : 0.f;
+            }
+          }
 #pragma unroll
           for (int i = 0; i < 16; ++i) {
             const int tok = c0 + i;
@@ -496,8 +594,7 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_tc_kernel(const __grid_consta
               if (EPI == EPI_F32) {
                 static_cast<float*>(p.y)[slot * p.y_stride + f] = round_act<T>(v[i]);
               } else if (EPI == EPI_RESIDUAL) {
-                const float res = to_f(static_cast<const T*>(p.residual)[slot * p.residual_stride + f]);
-                static_cast<T*>(p.y)[slot * p.y_stride + f] = from_f<T>(res + round_act<T>(v[i]));
+                static_cast<T*>(p.y)[slot * p.y_stride + f] = from_f<T>(res[i] + round_act<T>(v[i]));
               } else {
                 static_cast<T*>(p.y)[slot * p.y_stride + f] = from_f<T>(v[i]);
               }
@@ -506,7 +603,8 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_tc_kernel(const __grid_consta
         }
       }
       tc_fence_before();
-      mbar_arrive(&acc_empty[buf]);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[buf]);
     }
   }
   tc_fence_before();
@@ -565,38 +663,59 @@ int num_sms() {
   return sms;
 }
 
-template <typename T, int EPI, int NT, int PK, int SA, int SB>
-tf_status launch_cfg(const tc::Params& p, cudaStream_t s) {
-  using L = tc::Layout<NT, PK, SA, SB>;
-  const size_t smem = L::bytes(p.in);
-  if (smem > 227 * 1024) return set_error(TF_ERR_UNSUPPORTED, "qmm_tc: %zu bytes of shared memory", smem);
-  static size_t attr = 0;
-  if (smem > attr) {
-    TF_CUDA(cudaFuncSetAttribute(tc::qmm_tc_kernel<T, EPI, NT, PK, SA, SB>,
+// Weight maps (codes box {8*KS words, rows}, scales/biases box {8, rows}) and
+// the launch of one configuration.
+template <typename T, int EPI, bool PERM, int NT, int KS, int PK, int SA>
+tf_status launch_cfg(tc::Params& p, const QmmProblem& q, cudaStream_t s) {
+  using L = tc::Layout<NT, KS, PK, SA>;
+  const bool sw = EPI == EPI_SWIGLU;
+  const int in = p.in;
+  const int64_t rows_total = (int64_t)(q.w0.experts > 0 ? q.w0.experts : 1) * p.out;
+  const int tile_rows = sw ? 64 : 128;
+  const tf_affine_weight* ws[2] = {&q.w0, &q.w1};
+  CUtensorMap* mq[2] = {&p.tm_q0, &p.tm_q1};
+  CUtensorMap* ms[2] = {&p.tm_s0, &p.tm_s1};
+  CUtensorMap* mb[2] = {&p.tm_b0, &p.tm_b1};
+  for (int i = 0; i < (sw ? 2 : 1); ++i) {
+    TF_TRY(make_map(mq[i], ws[i]->q, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, in / 8, rows_total, in / 2, 8 * KS, tile_rows,
+                    CU_TENSOR_MAP_SWIZZLE_NONE));
+    TF_TRY(make_map(ms[i], ws[i]->scales, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, in / 64, rows_total, in / 32, tc::kSK,
+                    tile_rows, CU_TENSOR_MAP_SWIZZLE_NONE));
+    TF_TRY(make_map(mb[i], ws[i]->biases, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, in / 64, rows_total, in / 32, tc::kSK,
+                    tile_rows, CU_TENSOR_MAP_SWIZZLE_NONE));
+  }
+  const void* xs = q.x16 ? q.x16 : q.x;
+  const int64_t pitch = q.x16 && q.mode == QMM_GROUPED ? in : q.x_stride;
+  TF_TRY(make_map(&p.tm_x, xs, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, in, q.n, pitch * 2, 64, NT,
+                  CU_TENSOR_MAP_SWIZZLE_128B));
+  constexpr size_t smem = L::kBytes;
+  static_assert(smem <= 227 * 1024, "qmm_tc: shared memory budget");
+  static bool attr = false;
+  if (!attr) {
+    TF_CUDA(cudaFuncSetAttribute(tc::qmm_tc_kernel<T, EPI, PERM, NT, KS, PK, SA>,
                                  cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    attr = smem;
+    attr = true;
   }
   int64_t grid = p.tiles_bound < num_sms() ? p.tiles_bound : num_sms();
   const int64_t need = (p.tiles_bound + tc::kMaxTiles - 1) / tc::kMaxTiles;
   if (grid < need) grid = need;
   if (grid <= 0) return TF_OK;
-  tc::qmm_tc_kernel<T, EPI, NT, PK, SA, SB><<<(unsigned)grid, tc::kThreads, smem, s>>>(p);
+  tc::qmm_tc_kernel<T, EPI, PERM, NT, KS, PK, SA><<<(unsigned)grid, tc::kThreads, smem, s>>>(p);
   return check_launch("qmm_tc");
 }
 
-template <typename T, int EPI>
-tf_status launch_nt(tc::Params& p, const QmmProblem& q, int nt, int64_t tiles_bound, cudaStream_t s) {
-  const int in = q.w0.in_features;
-  const void* xs = q.x16 ? q.x16 : q.x;
-  const int64_t pitch = q.x16 && q.mode == QMM_GROUPED ? in : q.x_stride;
-  TF_TRY(make_map(&p.tm_x, xs, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, in, q.n, pitch * 2, 64, nt,
-                  CU_TENSOR_MAP_SWIZZLE_128B));
-  p.tiles_bound = tiles_bound;
+template <typename T, int EPI, bool PERM>
+tf_status launch_nt(tc::Params& p, const QmmProblem& q, int nt, cudaStream_t s) {
   switch (nt) {
-    case 32: return launch_cfg<T, EPI, 32, 8, 4, 8>(p, s);
-    case 64: return launch_cfg<T, EPI, 64, 8, 4, 6>(p, s);
-    default: return launch_cfg<T, EPI, 256, 4, 3, 3>(p, s);
+    case 32: return launch_cfg<T, EPI, PERM, 32, 2, 4, 4>(p, q, s);
+    case 64: return launch_cfg<T, EPI, PERM, 64, 2, 4, 3>(p, q, s);
+    default: return launch_cfg<T, EPI, PERM, 256, 1, 6, 3>(p, q, s);
   }
+}
+
+template <typename T, int EPI>
+tf_status launch_perm(tc::Params& p, const QmmProblem& q, int nt, cudaStream_t s) {
+  return q.x16 && q.x16_perm ? launch_nt<T, EPI, true>(p, q, nt, s) : launch_nt<T, EPI, false>(p, q, nt, s);
 }
 
 }  // namespace
@@ -615,24 +734,9 @@ tf_status launch_qmm_tc(const QmmProblem& q, cudaStream_t s) {
   const bool sw = q.epilogue == EPI_SWIGLU;
   const int experts = q.w0.experts > 0 ? q.w0.experts : 1;
   const int out = q.w0.out_features;
-  const int64_t rows_total = (int64_t)experts * out;
   const int tile_rows = sw ? 64 : 128;
   tc::Params p;
   memset(&p, 0, sizeof(p));
-  TF_TRY(make_map(&p.tm_q0, q.w0.q, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, in / 8, rows_total, in / 2, 8, tile_rows,
-                  CU_TENSOR_MAP_SWIZZLE_NONE));
-  TF_TRY(make_map(&p.tm_s0, q.w0.scales, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, in / 64, rows_total, in / 32, in / 64,
-                  tile_rows, CU_TENSOR_MAP_SWIZZLE_NONE));
-  TF_TRY(make_map(&p.tm_b0, q.w0.biases, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, in / 64, rows_total, in / 32, in / 64,
-                  tile_rows, CU_TENSOR_MAP_SWIZZLE_NONE));
-  if (sw) {
-    TF_TRY(make_map(&p.tm_q1, q.w1.q, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, in / 8, rows_total, in / 2, 8, tile_rows,
-                    CU_TENSOR_MAP_SWIZZLE_NONE));
-    TF_TRY(make_map(&p.tm_s1, q.w1.scales, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, in / 64, rows_total, in / 32,
-                    in / 64, tile_rows, CU_TENSOR_MAP_SWIZZLE_NONE));
-    TF_TRY(make_map(&p.tm_b1, q.w1.biases, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, in / 64, rows_total, in / 32,
-                    in / 64, tile_rows, CU_TENSOR_MAP_SWIZZLE_NONE));
-  }
   p.offsets = q.offsets;
   p.active = q.active;
   p.active_count = q.active_count;
@@ -650,10 +754,10 @@ tf_status launch_qmm_tc(const QmmProblem& q, cudaStream_t s) {
   const int64_t per_matrix = p.grouped ? (q.n + experts - 1) / experts : q.n;
   const int nt = per_matrix <= 24 ? 32 : per_matrix <= 64 ? 64 : 256;
   const int64_t token_tiles = p.grouped ? experts + q.n / nt + 1 : (q.n + nt - 1) / nt;
-  const int64_t tiles_bound = token_tiles * p.row_blocks;
-#define TF_TC_EPI(E)                                                                     \
-  return q.act == TF_DTYPE_F16 ? launch_nt<__half, E>(p, q, nt, tiles_bound, s)          \
-                               : launch_nt<__nv_bfloat16, E>(p, q, nt, tiles_bound, s);
+  p.tiles_bound = token_tiles * p.row_blocks;
+#define TF_TC_EPI(E)                                                                \
+  return q.act == TF_DTYPE_F16 ? launch_perm<__half, E>(p, q, nt, s)                \
+                               : launch_perm<__nv_bfloat16, E>(p, q, nt, s);
   switch (q.epilogue) {
     case EPI_PLAIN: TF_TC_EPI(EPI_PLAIN)
     case EPI_SWIGLU: TF_TC_EPI(EPI_SWIGLU)
@@ -666,12 +770,14 @@ tf_status launch_qmm_tc(const QmmProblem& q, cudaStream_t s) {
 // ---------------------------------------------------------------------------
 // Operand preparation for the tensor-core path.
 
-// y[i] = f16(x[src(i)]) row by row, src(i) = perm ? perm[i] / div : i.  bf16
-// -> f16 is exact for |x| in [2^-14, 65504]; beyond the f16 range the value
-// would become inf, so such rows record error code 5.
+// y[i] = f16(x[src(i)]) row by row, src(i) = perm ? perm[i] / div : i, with
+// each group of 8 columns in the tensor-core operand order [0,4,1,5,2,6,3,7]
+// when `permute` is set.  bf16 -> f16 is exact for |x| in [2^-14, 65504];
+// beyond the f16 range the value would become inf, so such rows record error
+// code 5.
 template <typename Tin>
 __global__ void gather_f16_kernel(const Tin* __restrict__ x, int64_t x_stride, const int32_t* __restrict__ perm,
-                                  int div, int64_t rows, int width, __half* __restrict__ y) {
+                                  int div, int64_t rows, int width, int permute, __half* __restrict__ y) {
   const int cpr = (width / 8 + blockDim.x - 1) / blockDim.x;  // blocks per row
   const int64_t row = blockIdx.x / cpr;
   const int c = (int)(blockIdx.x % cpr) * blockDim.x + threadIdx.x;
@@ -683,28 +789,34 @@ __global__ void gather_f16_kernel(const Tin* __restrict__ x, int64_t x_stride, c
 #pragma unroll
   for (int j = 0; j < 8; ++j) bad |= fabsf(f[j]) > 65504.f;
   if (bad) atomicCAS(&g_tc_error, 0, 5);
-  *reinterpret_cast<uint4*>(y + row * width + 8 * c) = pack8<__half>(f);
+  if (permute) {
+    const float g[8] = {f[0], f[4], f[1], f[5], f[2], f[6], f[3], f[7]};
+    *reinterpret_cast<uint4*>(y + row * width + 8 * c) = pack8<__half>(g);
+  } else {
+    *reinterpret_cast<uint4*>(y + row * width + 8 * c) = pack8<__half>(f);
+  }
 }
 
 tf_status launch_gather_f16(const void* x, int64_t x_stride, int act, const int32_t* perm, int div, int64_t rows,
-                            int width, void* y, cudaStream_t s) {
+                            int width, void* y, int permute, cudaStream_t s) {
   if (rows == 0) return TF_OK;
   if (width % 8) return set_error(TF_ERR_SHAPE, "gather_f16: width %d", width);
   const int64_t cpr = (width / 8 + 127) / 128;
   if (rows * cpr > 2147483647) return set_error(TF_ERR_UNSUPPORTED, "gather_f16: too many rows");
   const unsigned grid = (unsigned)(rows * cpr);
   if (act == TF_DTYPE_F16)
-    gather_f16_kernel<__half><<<grid, 128, 0, s>>>((const __half*)x, x_stride, perm, div, rows, width, (__half*)y);
+    gather_f16_kernel<__half><<<grid, 128, 0, s>>>((const __half*)x, x_stride, perm, div, rows, width, permute,
+                                                   (__half*)y);
   else
     gather_f16_kernel<__nv_bfloat16><<<grid, 128, 0, s>>>((const __nv_bfloat16*)x, x_stride, perm, div, rows, width,
-                                                          (__half*)y);
+                                                          permute, (__half*)y);
   return check_launch("gather_f16");
 }
 
-tf_status launch_bf16_to_f16(const void* x, int64_t n, void* y, cudaStream_t s) {
+tf_status launch_bf16_to_f16(const void* x, int64_t n, void* y, int permute, cudaStream_t s) {
   if (n == 0) return TF_OK;
   if (n % 2048) return set_error(TF_ERR_SHAPE, "bf16_to_f16: count %lld not a multiple of 2048", (long long)n);
-  return launch_gather_f16(x, 2048, TF_DTYPE_BF16, nullptr, 1, n / 2048, 2048, y, s);
+  return launch_gather_f16(x, 2048, TF_DTYPE_BF16, nullptr, 1, n / 2048, 2048, y, permute, s);
 }
 
 int read_tc_error(bool clear) {
