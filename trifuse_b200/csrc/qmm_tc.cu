@@ -21,20 +21,25 @@
 //                     biases of every 8 k-steps (box 8 x 128) into two slots.
 //   warp 14 (activation loader)  TMA of each stage's activation tiles (box
 //                     64 x NT, 128B-swizzled = the MMA's K-major layout).
-//   warps 0-7 (dequant) two threads per A row turn packed words into f16
-//                     weights (magic-number half2 extraction + HFMA2) and
-//                     store them 128B-swizzled into the SA-deep stage ring.
-//   warp 13 (MMA)     allocates 2 x NT TMEM columns; one elected lane issues
-//                     tcgen05.mma (4 x K=16 per k-step) into one of two
-//                     accumulators and one commit per stage.
+//   warps 0-7 (dequant) one thread per A row and half k-step (warp w owns
+//                     TMEM lanes 32(w%4).. and k half w/4) turns packed words
+//                     into f16 weights (magic-number half2 extraction +
+//                     HFMA2) and writes them with tcgen05.st straight into
+//                     tensor memory: the A operand of each stage lives in
+//                     TMEM (row = lane, two k per 32-bit column).
+//   warp 13 (MMA)     allocates all 512 TMEM columns (two NT-column
+//                     accumulators, then SA stages of A); one elected lane
+//                     issues tcgen05.mma with A from TMEM and B from shared
+//                     memory (4 x K=16 per k-step), one commit per stage.
 //   warps 8-11 (epilogue) tcgen05.ld the finished accumulator while the next
 //                     tile accumulates into the other one; SwiGLU tiles keep
 //                     gate row j and up row j in adjacent TMEM lanes, so one
 //                     shuffle pairs them.
-// A stage's A tile (dequant warps) and B tile (activation TMA) complete one
-// barrier, which the MMA warp waits on once per stage; one commit releases
-// both.  Small-N decode tiles give the tensor core little work per k-step,
-// so the number of barrier round trips per k-step sets the pace there.
+// Keeping A out of shared memory matters: a dequantized k-step is 16 KB per
+// 128 rows against 4 KB of packed codes, and writing it to shared memory and
+// reading it back for the MMA made shared-memory bandwidth the limit.  A
+// stage's A (dequant warps) and B (activation TMA) complete one barrier,
+// which the MMA warp waits on once per stage; one commit releases both.
 //
 // Operand order: with PERM the dequant writes each group of 8 inputs in the
 // order [0,4,1,5,2,6,3,7] (what the magic-number extraction yields without
@@ -74,6 +79,8 @@ constexpr int kM = 128;
 constexpr int kKStep = 64;
 constexpr int kSK = 8;          // k-steps per scale slot (16 bytes of f16 per row)
 constexpr int kMaxTiles = 256;  // per-block tile table
+constexpr uint32_t kTmemCols = 512;  // whole tensor memory: accumulators + A stages
+constexpr int kACols = kKStep / 2;   // TMEM columns of one k-step of A (two f16 per column)
 constexpr long long kWaitCycles = 2000000000LL;
 // try_wait suspends the thread until the phase completes or this many ns
 // pass, so a waiting role takes no issue slots from the dequant warps.
@@ -220,6 +227,28 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
   for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+// 16 consecutive TMEM columns of this warp's 32 lanes <- v (warp-wide).
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t* v) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
+          taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
+      "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
+      : "memory");
+}
+__device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+// D (TMEM) += A (TMEM) * B (shared memory descriptor).
+__device__ __forceinline__ void mma_f16_ts(uint32_t leader, uint32_t tmem_d, uint32_t tmem_a, uint64_t b,
+                                           uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p, e;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "setp.ne.b32 e, %5, 0;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "r"(tmem_a), "l"(b), "r"(idesc), "r"(acc), "r"(leader)
+      : "memory");
+}
+
 // Eight codes of one packed word (code i at bits 4i) -> eight f16 weights
 // fp16(code*s + b).  The f16 halves of
 //   t0 = w & 0x000F000F | 0x6400 (1024 + c0, 1024 + c4)
@@ -315,16 +344,18 @@ template <int NT, int KS, int PK, int SA>
 struct Layout {
   static constexpr int kP = kM * 32 * KS;     // packed codes of one stage
   static constexpr int kS = 2 * kM * kSK * 2;  // scales | biases of 8 k-steps
-  static constexpr int kA = kM * 128 * KS;     // f16 A stage (KS swizzled 128 x 64 tiles)
   static constexpr int kB = NT * 128 * KS;     // f16 activation stage
   static constexpr int kHead = 1024 + kMaxTiles * 16;
   static constexpr int kOffS = kHead;
   static constexpr int kOffP = (kOffS + 2 * kS + 1023) / 1024 * 1024;
-  static constexpr int kOffA = kOffP + PK * kP;
-  static constexpr int kOffB = kOffA + SA * kA;
+  static constexpr int kOffB = kOffP + PK * kP;
   static constexpr int kBytes = kOffB + SA * kB + 1024;  // + alignment slack
-  static_assert(kP % 1024 == 0 && kA % 1024 == 0 && kB % 1024 == 0, "stage sizes keep 1024-byte alignment");
+  // TMEM columns: accumulators [0, 2 NT), A stages from 2 NT on.
+  static constexpr int kAStage = KS * kACols;
+  static constexpr int kACol0 = 2 * NT;
+  static_assert(kP % 1024 == 0 && kB % 1024 == 0, "stage sizes keep 1024-byte alignment");
   static_assert(kSK % KS == 0, "a scale slot holds whole stages");
+  static_assert(kACol0 + SA * kAStage <= (int)kTmemCols, "accumulators and A stages fit tensor memory");
 };
 
 template <typename T, int EPI, bool PERM, int NT, int KS, int PK, int SA>
@@ -347,11 +378,9 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_tc_kernel(const __grid_consta
   TileInfo* table = reinterpret_cast<TileInfo*>(base + 1024);
   uint8_t* ring_s = base + L::kOffS;  // [2 slots][s | b][kM rows][8 k-steps] f16
   uint8_t* ring_p = base + L::kOffP;
-  uint8_t* ring_a = base + L::kOffA;
   uint8_t* ring_b = base + L::kOffB;
   const int nk = p.in / kKStep;  // a multiple of 8
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  constexpr uint32_t kTmemCols = 2 * NT < 32 ? 32 : 2 * NT;
 
   // ---- setup
   if (tid == 0) {
@@ -449,16 +478,18 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_tc_kernel(const __grid_consta
       }
     }
   } else if (warp < kDeqWarps) {
-    // ---- dequant: thread pair per A row, 4 words each per k-step.  Every
-    // lane waits on the full barriers (warp-uniform result); one lane per
-    // warp arrives on the release barriers after __syncwarp (the barriers
-    // count warps).
-    const int r = tid >> 1, h = tid & 1;
+    // ---- dequant: warp w owns TMEM lanes (A rows) 32(w%4).. and k half
+    // w/4 of every k-step: each thread turns 4 packed words (32 codes) per
+    // k-step into 16 TMEM columns of its row.  Every lane waits on the full
+    // barriers (warp-uniform result); one lane per warp arrives on the
+    // release barriers after __syncwarp (the barriers count warps).
+    const int quarter = warp & 3, kh = warp >> 2;
+    const int r = quarter * 32 + lane;
     // A row r <- packed/scale row pr.  SwiGLU tiles interleave gate row j
     // (A row 2j) and up row j (A row 2j+1); the packed and scale slots hold
     // gate rows 0..63 then up rows 64..127.
     const int pr = kSw ? ((r & 1) * 64 + (r >> 1)) : r;
-    const int swz = r & 7;
+    const uint32_t tlane = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(L::kACol0 + kh * (kACols / 2));
     int64_t g = 0, gs = 0;
     bool ok = true;
     for (int li = 0; li < ntiles && ok; ++li) {
@@ -477,21 +508,25 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_tc_kernel(const __grid_consta
           uint4 wv[KS];
 #pragma unroll
           for (int kk = 0; kk < KS; ++kk)
-            wv[kk] = *reinterpret_cast<const uint4*>(ring_p + (size_t)ps * L::kP + pr * (32 * KS) + kk * 32 + h * 16);
+            wv[kk] = *reinterpret_cast<const uint4*>(ring_p + (size_t)ps * L::kP + pr * (32 * KS) + kk * 32 + kh * 16);
           const int as = (int)(g % SA);
           if (g >= SA && !(ok = warp_wait(&ab_empty[as], (uint32_t)(((g / SA) - 1) & 1), abort_flag, 23))) break;
-          uint8_t* arow = ring_a + (size_t)as * L::kA + r * 128;
+          tc_fence_after();
 #pragma unroll
           for (int kk = 0; kk < KS; ++kk) {
             const __half2 s2 = __half2half2(sh[ks + kk]);
             const __half2 b2 = __half2half2(bh[ks + kk]);
             const uint32_t w4[4] = {wv[kk].x, wv[kk].y, wv[kk].z, wv[kk].w};
+            uint32_t cols[16];
 #pragma unroll
-            for (int i = 0; i < 4; ++i)
-              *reinterpret_cast<uint4*>(arow + kk * (kM * 128) + (((4 * h + i) ^ swz) << 4)) =
-                  dequant8<PERM>(w4[i], s2, b2);
+            for (int i = 0; i < 4; ++i) {
+              const uint4 d = dequant8<PERM>(w4[i], s2, b2);
+              cols[4 * i] = d.x, cols[4 * i + 1] = d.y, cols[4 * i + 2] = d.z, cols[4 * i + 3] = d.w;
+            }
+            tmem_st16(tlane + (uint32_t)(as * L::kAStage + kk * kACols), cols);
           }
-          fence_proxy_async();
+          tmem_st_wait();
+          tc_fence_before();
           __syncwarp();
           // The packed words were consumed above, so every lane's shared
           // loads of this slot have completed before it is released (a
@@ -526,11 +561,11 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_tc_kernel(const __grid_consta
         tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < KS; ++kk) {
-          const uint64_t ad = sw128_desc(smem_addr(ring_a + (size_t)as * L::kA + kk * (kM * 128)));
+          const uint32_t ta = tmem + (uint32_t)(L::kACol0 + as * L::kAStage + kk * kACols);
           const uint64_t bd = sw128_desc(smem_addr(ring_b + (size_t)as * L::kB + kk * (NT * 128)));
 #pragma unroll
-          for (int j = 0; j < kKStep / 16; ++j)  // +32 B per K=16 slice = +2 in the address field
-            mma_f16(leader, d, ad + 2 * j, bd + 2 * j, idesc, (k + kk > 0 || j > 0) ? 1u : 0u);
+          for (int j = 0; j < kKStep / 16; ++j)  // K=16 slice: 8 TMEM columns of A, +32 B (+2) of B
+            mma_f16_ts(leader, d, ta + 8 * j, bd + 2 * j, idesc, (k + kk > 0 || j > 0) ? 1u : 0u);
         }
         mma_commit(leader, &ab_empty[as]);
       }
@@ -707,9 +742,9 @@ tf_status launch_cfg(tc::Params& p, const QmmProblem& q, cudaStream_t s) {
 template <typename T, int EPI, bool PERM>
 tf_status launch_nt(tc::Params& p, const QmmProblem& q, int nt, cudaStream_t s) {
   switch (nt) {
-    case 32: return launch_cfg<T, EPI, PERM, 32, 2, 4, 4>(p, q, s);
-    case 64: return launch_cfg<T, EPI, PERM, 64, 2, 4, 3>(p, q, s);
-    default: return launch_cfg<T, EPI, PERM, 256, 1, 6, 3>(p, q, s);
+    case 32: return launch_cfg<T, EPI, PERM, 32, 2, 8, 4>(p, q, s);
+    case 64: return launch_cfg<T, EPI, PERM, 64, 2, 8, 4>(p, q, s);
+    default: return launch_cfg<T, EPI, PERM, 128, 2, 6, 4>(p, q, s);
   }
 }
 
@@ -752,7 +787,7 @@ tf_status launch_qmm_tc(const QmmProblem& q, cudaStream_t s) {
   p.residual_stride = q.residual_stride;
   // Token tile: about the tokens each weight matrix serves.
   const int64_t per_matrix = p.grouped ? (q.n + experts - 1) / experts : q.n;
-  const int nt = per_matrix <= 24 ? 32 : per_matrix <= 64 ? 64 : 256;
+  const int nt = per_matrix <= 24 ? 32 : per_matrix <= 64 ? 64 : 128;
   const int64_t token_tiles = p.grouped ? experts + q.n / nt + 1 : (q.n + nt - 1) / nt;
   p.tiles_bound = token_tiles * p.row_blocks;
 #define TF_TC_EPI(E)                                                                \
