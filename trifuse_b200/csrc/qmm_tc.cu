@@ -13,25 +13,28 @@
 // native_affine_ops.py:36); activations arrive in f16 (bf16 models pass an
 // exact f16 copy).
 //
-// Persistent, warp-specialized block (480 threads, one block per SM).  Work
+// Persistent, warp-specialized block (736 threads, one block per SM).  Work
 // moves in stages of KS k-steps (a k-step is 64 inputs = one quantization
 // group):
-//   warp 12 (code loader)  TMA of each stage's packed codes (box 8*KS words x
+//   warp 20 (code loader)  TMA of each stage's packed codes (box 8*KS words x
 //                     128 rows) into a PK-deep ring, and of the scales and
 //                     biases of every 8 k-steps (box 8 x 128) into two slots.
-//   warp 14 (activation loader)  TMA of each stage's activation tiles (box
+//   warp 22 (activation loader)  TMA of each stage's activation tiles (box
 //                     64 x NT, 128B-swizzled = the MMA's K-major layout).
-//   warps 0-7 (dequant) one thread per A row and half k-step (warp w owns
-//                     TMEM lanes 32(w%4).. and k half w/4) turns packed words
-//                     into f16 weights (magic-number half2 extraction +
-//                     HFMA2) and writes them with tcgen05.st straight into
-//                     tensor memory: the A operand of each stage lives in
-//                     TMEM (row = lane, two k per 32-bit column).
-//   warp 13 (MMA)     allocates all 512 TMEM columns (two NT-column
+//   warps 0-15 (dequant) two groups of 8 warps take alternate stages (the
+//                     dequant is latency-bound, so two stages in flight
+//                     nearly double its rate).  In a group, one thread per A
+//                     row and half k-step (warp w owns TMEM lanes 32(w%4)..
+//                     and k half (w/4)%2) turns packed words into f16
+//                     weights (magic-number half2 extraction + HFMA2) and
+//                     writes them with tcgen05.st straight into tensor
+//                     memory: the A operand of each stage lives in TMEM
+//                     (row = lane, two k per 32-bit column).
+//   warp 21 (MMA)     allocates all 512 TMEM columns (two NT-column
 //                     accumulators, then SA stages of A); one elected lane
 //                     issues tcgen05.mma with A from TMEM and B from shared
 //                     memory (4 x K=16 per k-step), one commit per stage.
-//   warps 8-11 (epilogue) tcgen05.ld the finished accumulator while the next
+//   warps 16-19 (epilogue) tcgen05.ld the finished accumulator while the next
 //                     tile accumulates into the other one; SwiGLU tiles keep
 //                     gate row j and up row j in adjacent TMEM lanes, so one
 //                     shuffle pairs them.
@@ -69,12 +72,13 @@ __device__ int g_tc_error = 0;  // first error code recorded by a bounded wait
 
 namespace tc {
 
-constexpr int kDeqWarps = 8;
+constexpr int kDeqGroups = 2;                     // dequant groups take alternate stages
+constexpr int kDeqWarps = 8 * kDeqGroups;         // 8 warps cover one stage
 constexpr int kEpiWarps = 4;
-constexpr int kLoadWarp = kDeqWarps + kEpiWarps;  // 12: packed codes + scales
-constexpr int kMmaWarp = kLoadWarp + 1;           // 13
-constexpr int kActWarp = kMmaWarp + 1;            // 14: activation tiles
-constexpr int kThreads = (kActWarp + 1) * 32;     // 480
+constexpr int kLoadWarp = kDeqWarps + kEpiWarps;  // 20: packed codes + scales
+constexpr int kMmaWarp = kLoadWarp + 1;           // 21
+constexpr int kActWarp = kMmaWarp + 1;            // 22: activation tiles
+constexpr int kThreads = (kActWarp + 1) * 32;     // 736
 constexpr int kM = 128;
 constexpr int kKStep = 64;
 constexpr int kSK = 8;          // k-steps per scale slot (16 bytes of f16 per row)
@@ -386,16 +390,16 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_tc_kernel(const __grid_consta
   if (tid == 0) {
     for (int i = 0; i < PK; ++i) {
       mbar_init(&p_full[i], 1);
-      mbar_init(&p_empty[i], kDeqWarps);
+      mbar_init(&p_empty[i], kDeqWarps / kDeqGroups);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
-      mbar_init(&s_empty[i], kDeqWarps);
+      mbar_init(&s_empty[i], kDeqWarps);  // both groups use every scale block
       mbar_init(&acc_full[i], 1);
       mbar_init(&acc_empty[i], kEpiWarps);
     }
     for (int i = 0; i < SA; ++i) {
-      mbar_init(&ab_full[i], kDeqWarps + 1);  // dequant warps + the activation loader's expect_tx
+      mbar_init(&ab_full[i], kDeqWarps / kDeqGroups + 1);  // one group + the activation loader's expect_tx
       mbar_init(&ab_empty[i], 1);
     }
     mbar_init(drain, 1);
@@ -478,68 +482,71 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_tc_kernel(const __grid_consta
       }
     }
   } else if (warp < kDeqWarps) {
-    // ---- dequant: warp w owns TMEM lanes (A rows) 32(w%4).. and k half
-    // w/4 of every k-step: each thread turns 4 packed words (32 codes) per
-    // k-step into 16 TMEM columns of its row.  Every lane waits on the full
-    // barriers (warp-uniform result); one lane per warp arrives on the
-    // release barriers after __syncwarp (the barriers count warps).
-    const int quarter = warp & 3, kh = warp >> 2;
+    // ---- dequant: group grp takes stages g = grp, grp + 2, ...; in a group
+    // warp w owns TMEM lanes (A rows) 32(w%4).. and k half (w/4)%2 of every
+    // k-step: each thread turns 4 packed words (32 codes) per k-step into 16
+    // TMEM columns of its row.  Every lane waits on the full barriers
+    // (warp-uniform result); one lane per warp arrives on the release
+    // barriers after __syncwarp (the barriers count warps).
+    static_assert(KS == 2 && kDeqGroups == 2 && kSK / KS == 4,
+                  "each group takes two stages (one scale pair each) of every scale block");
+    constexpr int kSpb = kSK / KS;  // stages per scale block
+    const int grp = warp >> 3, quarter = warp & 3, kh = (warp >> 2) & 1;
     const int r = quarter * 32 + lane;
     // A row r <- packed/scale row pr.  SwiGLU tiles interleave gate row j
     // (A row 2j) and up row j (A row 2j+1); the packed and scale slots hold
     // gate rows 0..63 then up rows 64..127.
     const int pr = kSw ? ((r & 1) * 64 + (r >> 1)) : r;
     const uint32_t tlane = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(L::kACol0 + kh * (kACols / 2));
-    int64_t g = 0, gs = 0;
+    const int64_t total = (int64_t)ntiles * (nk / KS);
+    uint4 sv = make_uint4(0, 0, 0, 0), bv = sv;
     bool ok = true;
-    for (int li = 0; li < ntiles && ok; ++li) {
-      for (int k8 = 0; k8 < nk && ok; k8 += kSK, ++gs) {
-        const int ss = (int)(gs & 1);
-        if (!(ok = warp_wait(&s_full[ss], (uint32_t)((gs >> 1) & 1), abort_flag, 21))) break;
-        const uint8_t* sslot = ring_s + (size_t)ss * L::kS;
-        const uint4 sv = *reinterpret_cast<const uint4*>(sslot + pr * 16);
-        const uint4 bv = *reinterpret_cast<const uint4*>(sslot + kM * kSK * 2 + pr * 16);
-        const __half* sh = reinterpret_cast<const __half*>(&sv);
-        const __half* bh = reinterpret_cast<const __half*>(&bv);
+    for (int64_t g = grp; g < total && ok; g += kDeqGroups) {
+      const int sb = (int)(g % kSpb);
+      const int64_t blk = g / kSpb;
+      if (sb == grp) {  // this group's first stage of a scale block
+        if (!(ok = warp_wait(&s_full[blk & 1], (uint32_t)((blk >> 1) & 1), abort_flag, 21))) break;
+        const uint8_t* sslot = ring_s + (size_t)(blk & 1) * L::kS;
+        sv = *reinterpret_cast<const uint4*>(sslot + pr * 16);
+        bv = *reinterpret_cast<const uint4*>(sslot + kM * kSK * 2 + pr * 16);
+      }
+      const int ps = (int)(g % PK);
+      if (!(ok = warp_wait(&p_full[ps], (uint32_t)((g / PK) & 1), abort_flag, 22))) break;
+      const uint4 w0 = *reinterpret_cast<const uint4*>(ring_p + (size_t)ps * L::kP + pr * (32 * KS) + kh * 16);
+      const uint4 w1 = *reinterpret_cast<const uint4*>(ring_p + (size_t)ps * L::kP + pr * (32 * KS) + 32 + kh * 16);
+      const int as = (int)(g % SA);
+      if (g >= SA && !(ok = warp_wait(&ab_empty[as], (uint32_t)(((g / SA) - 1) & 1), abort_flag, 23))) break;
+      tc_fence_after();
+      // k-steps 2 sb and 2 sb + 1 of the scale block: one f16 pair of s and b.
+      const uint32_t spw = sb < 2 ? (sb ? sv.y : sv.x) : (sb == 3 ? sv.w : sv.z);
+      const uint32_t bpw = sb < 2 ? (sb ? bv.y : bv.x) : (sb == 3 ? bv.w : bv.z);
+      const __half2 sp = *reinterpret_cast<const __half2*>(&spw);
+      const __half2 bp = *reinterpret_cast<const __half2*>(&bpw);
+      const uint32_t wa[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
 #pragma unroll
-        for (int ks = 0; ks < kSK; ks += KS, ++g) {
-          const int ps = (int)(g % PK);
-          if (!(ok = warp_wait(&p_full[ps], (uint32_t)((g / PK) & 1), abort_flag, 22))) break;
-          uint4 wv[KS];
+      for (int kk = 0; kk < 2; ++kk) {
+        const __half2 s2 = kk ? __high2half2(sp) : __low2half2(sp);
+        const __half2 b2 = kk ? __high2half2(bp) : __low2half2(bp);
+        uint32_t cols[16];
 #pragma unroll
-          for (int kk = 0; kk < KS; ++kk)
-            wv[kk] = *reinterpret_cast<const uint4*>(ring_p + (size_t)ps * L::kP + pr * (32 * KS) + kk * 32 + kh * 16);
-          const int as = (int)(g % SA);
-          if (g >= SA && !(ok = warp_wait(&ab_empty[as], (uint32_t)(((g / SA) - 1) & 1), abort_flag, 23))) break;
-          tc_fence_after();
-#pragma unroll
-          for (int kk = 0; kk < KS; ++kk) {
-            const __half2 s2 = __half2half2(sh[ks + kk]);
-            const __half2 b2 = __half2half2(bh[ks + kk]);
-            const uint32_t w4[4] = {wv[kk].x, wv[kk].y, wv[kk].z, wv[kk].w};
-            uint32_t cols[16];
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              const uint4 d = dequant8<PERM>(w4[i], s2, b2);
-              cols[4 * i] = d.x, cols[4 * i + 1] = d.y, cols[4 * i + 2] = d.z, cols[4 * i + 3] = d.w;
-            }
-            tmem_st16(tlane + (uint32_t)(as * L::kAStage + kk * kACols), cols);
-          }
-          tmem_st_wait();
-          tc_fence_before();
-          __syncwarp();
-          // The packed words were consumed above, so every lane's shared
-          // loads of this slot have completed before it is released (a
-          // release right after issuing the loads let the next TMA fill
-          // overtake a load still in flight on another lane).
-          if (lane == 0) {
-            mbar_arrive(&ab_full[as]);
-            mbar_arrive(&p_empty[ps]);
-          }
+        for (int i = 0; i < 4; ++i) {
+          const uint4 d = dequant8<PERM>(wa[4 * kk + i], s2, b2);
+          cols[4 * i] = d.x, cols[4 * i + 1] = d.y, cols[4 * i + 2] = d.z, cols[4 * i + 3] = d.w;
         }
-        // Scales and biases of this block were consumed by the stages above.
-        __syncwarp();
-        if (ok && lane == 0) mbar_arrive(&s_empty[ss]);
+        tmem_st16(tlane + (uint32_t)(as * L::kAStage + kk * kACols), cols);
+      }
+      tmem_st_wait();
+      tc_fence_before();
+      __syncwarp();
+      // The packed words and (at the group's last stage of a block) the
+      // scales were consumed above, so every lane's shared loads of those
+      // slots have completed before they are released (a release right
+      // after issuing the loads let the next TMA fill overtake a load still
+      // in flight on another lane).
+      if (lane == 0) {
+        mbar_arrive(&ab_full[as]);
+        mbar_arrive(&p_empty[ps]);
+        if (sb + kDeqGroups >= kSpb) mbar_arrive(&s_empty[blk & 1]);
       }
     }
   } else if (warp == kMmaWarp) {
