@@ -17,6 +17,7 @@ larger than L2, so no flush is needed between steps.
 from __future__ import annotations
 
 import argparse
+import datetime
 import json
 import os
 import statistics
@@ -30,6 +31,11 @@ sys.path.insert(0, str(ROOT))
 
 METRIC = "OLMoE-4bit decode & prefill tok/s per B200; MoE GB/s vs HBM peak"
 FALLBACK_HBM_GBS = 6650.0
+# DRAM bytes (read + written) per algorithmic byte of the attention phase,
+# from an ncu capture of attn_split at B=64, L=512 (269.76 MB read + 3.84 MB
+# of partials written for 268.96 MB of K/V); both terms grow with the KV
+# length, so the ratio carries over to the benchmark's L.
+ATTN_TRAFFIC_PER_ALGO_BYTE = (269.763072 + 3.841536) / 268.959744
 
 # Algorithmic bytes per launch of each traced phase (per layer), batch B, KV
 # length L (keys read per request = L + 1 including this step's slot).
@@ -71,8 +77,9 @@ def measured_peaks():
 
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled every 200 ms."""
-    FIELDS = ("index,uuid,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+    """nvidia-smi clocks / throttle reasons sampled every 100 ms; only the
+    samples taken inside the timed window (wall clock) are summarised."""
+    FIELDS = ("timestamp,index,uuid,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
@@ -85,11 +92,14 @@ class ClockSampler:
         try:
             self.f = open(self.path, "w")
             self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                                          "-lms", "200"], stdout=self.f, stderr=subprocess.DEVNULL)
+                                          "-lms", "100"], stdout=self.f, stderr=subprocess.DEVNULL)
         except Exception:
             self.proc = None
+        # nvidia-smi needs a moment before its first sample
+        time.sleep(0.5)
 
-    def stop(self):
+    def stop(self, t0, t1):
+        """Summary of the samples stamped inside [t0, t1] (time.time())."""
         if not self.proc:
             return None
         self.proc.terminate()
@@ -102,16 +112,19 @@ class ClockSampler:
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         for line in self.path.read_text().splitlines():
             parts = [x.strip() for x in line.split(",")]
-            if len(parts) < 10:
+            if len(parts) < 11:
                 continue
-            if self.uuid and self.uuid not in parts[1]:
+            if self.uuid and self.uuid not in parts[2]:
                 continue
             try:
-                sm.append(float(parts[2]))
-                mx.append(float(parts[3]))
+                ts = datetime.datetime.strptime(parts[0], "%Y/%m/%d %H:%M:%S.%f").timestamp()
+                if not t0 <= ts <= t1:
+                    continue
+                sm.append(float(parts[3]))
+                mx.append(float(parts[4]))
             except ValueError:
                 continue
-            for n, v in zip(names, parts[6:10]):
+            for n, v in zip(names, parts[7:11]):
                 if v.lower() == "active":
                     reasons.add(n)
         if not sm:
@@ -160,43 +173,62 @@ def time_steps(sess, ids, logits, steps, warmup, L, B, stream, barrier):
     return e0.elapsed_time(e1) / steps
 
 
+class CpuWorkload:
+    """Random-init weights of one OLMoE decoder layer plus the lm_head and a
+    shared N(0,1) K/V block, built once; the oracle's decode layer and head
+    are then timed on them (the reference's CPU path, numpy)."""
+
+    def __init__(self, B, L, seed=5):
+        import numpy as np
+
+        import oracle
+        self.oracle = oracle
+        rng = np.random.default_rng(seed)
+        self.cfg = oracle.OLMoEConfig(act="f16")
+
+        def rand_affine(shape):
+            *lead, rows, cols = shape
+            q = rng.integers(0, 2 ** 32, size=(*lead, rows, cols // 8), dtype=np.uint32)
+            s = (rng.random((*lead, rows, cols // 64)) * 0.004 + 0.001).astype(np.float16)
+            b = (-7.5 * s.astype(np.float32)).astype(np.float16)
+            return q, s, b
+
+        norm = lambda n: (1 + 0.1 * rng.standard_normal(n)).astype(np.float16)  # noqa: E731
+        self.layer = dict(input_norm=norm(H), post_norm=norm(H), q_norm=norm(W), k_norm=norm(W),
+                          q=rand_affine((W, H)), k=rand_affine((W, H)), v=rand_affine((W, H)),
+                          o=rand_affine((H, W)), router=rand_affine((E, H)),
+                          experts={"gate": rand_affine((E, I, H)), "up": rand_affine((E, I, H)),
+                                   "down": rand_affine((E, H, I))})
+        self.head = rand_affine((V, H))
+        self.final_norm = norm(H)
+        # One N(0,1) K and V block shared by every request: the timed math is
+        # the same per request and host memory stays bounded.
+        k1 = rng.standard_normal((16, L + 1, 128), dtype=np.float32).astype(np.float16).astype(np.float32)
+        v1 = rng.standard_normal((16, L + 1, 128), dtype=np.float32).astype(np.float16).astype(np.float32)
+        self.kc, self.vc = [k1] * B, [v1] * B
+        self.h = oracle.round_f16(rng.standard_normal((B, H)).astype(np.float32))
+        self.B, self.L = B, L
+
+    def layer_s(self):
+        t0 = time.perf_counter()
+        self.out = self.oracle.decode_layer_batched(self.h, self.layer, self.cfg, self.kc, self.vc,
+                                                    [self.L] * self.B, fast=True)
+        return time.perf_counter() - t0
+
+    def head_s(self):
+        o = self.oracle
+        t0 = time.perf_counter()
+        o.affine_qmm(o.rms_norm(self.out, self.final_norm, 1e-5, "f16"), *self.head, "f16")
+        return time.perf_counter() - t0
+
+
 def cpu_sample(B, L, seed=5):
     """One decode layer of the oracle for B requests at KV length L, plus the
     lm_head; returns (seconds for the extrapolated 16-layer step, details)."""
-    import numpy as np
-
-    import oracle
-    rng = np.random.default_rng(seed)
-    cfg = oracle.OLMoEConfig(act="f16")
-
-    def rand_affine(shape):
-        *lead, rows, cols = shape
-        q = rng.integers(0, 2 ** 32, size=(*lead, rows, cols // 8), dtype=np.uint32)
-        s = (rng.random((*lead, rows, cols // 64)) * 0.004 + 0.001).astype(np.float16)
-        b = (-7.5 * s.astype(np.float32)).astype(np.float16)
-        return q, s, b
-
-    norm = lambda n: (1 + 0.1 * rng.standard_normal(n)).astype(np.float16)  # noqa: E731
-    layer = dict(input_norm=norm(H), post_norm=norm(H), q_norm=norm(W), k_norm=norm(W),
-                 q=rand_affine((W, H)), k=rand_affine((W, H)), v=rand_affine((W, H)), o=rand_affine((H, W)),
-                 router=rand_affine((E, H)),
-                 experts={"gate": rand_affine((E, I, H)), "up": rand_affine((E, I, H)),
-                          "down": rand_affine((E, H, I))})
-    head = rand_affine((V, H))
-    # One N(0,1) K and V block shared by every request: the timed math is the
-    # same per request and host memory stays bounded.
-    k1 = rng.standard_normal((16, L + 1, 128), dtype=np.float32).astype(np.float16).astype(np.float32)
-    v1 = rng.standard_normal((16, L + 1, 128), dtype=np.float32).astype(np.float16).astype(np.float32)
-    kc = [k1] * B
-    vc = [v1] * B
-    h = oracle.round_f16(rng.standard_normal((B, H)).astype(np.float32))
-    t0 = time.perf_counter()
-    out = oracle.decode_layer_batched(h, layer, cfg, kc, vc, [L] * B, fast=True)
-    t1 = time.perf_counter()
-    oracle.affine_qmm(oracle.rms_norm(out, norm(H), 1e-5, "f16"), *head, "f16")
-    t2 = time.perf_counter()
-    step = 16 * (t1 - t0) + (t2 - t1)
-    return step, {"layer_s": t1 - t0, "head_s": t2 - t1}
+    w = CpuWorkload(B, L, seed)
+    layer = w.layer_s()
+    head = w.head_s()
+    return 16 * layer + head, {"layer_s": layer, "head_s": head}
 
 
 def cpu_threads():
@@ -211,27 +243,30 @@ def cpu_threads():
 
 def run_reference(args, rank, world):
     """CPU reference arm: the oracle port of the reference's operators on the
-    host cores, same metric/config; rank 0 only."""
+    host cores, same metric/config; rank 0 only.  Each step is a bounded
+    sample: one of the 16 decode layers for all B requests (weights built
+    once); the lm_head is timed once after warm-up, and a step is estimated
+    as 16 x layer + head."""
     if rank != 0:
         return
-    samples = []
+    w = CpuWorkload(args.batch, args.kv_len)
     for _ in range(args.warmup):
-        cpu_sample(args.batch, args.kv_len)
-    for _ in range(args.steps):
-        s, _d = cpu_sample(args.batch, args.kv_len)
-        samples.append(s)
-    step_s = sum(samples) / len(samples)
+        w.layer_s()
+    head = w.head_s() if args.warmup or args.steps else 0.0
+    layers = [w.layer_s() for _ in range(args.steps)]
+    step_s = 16 * (sum(layers) / max(1, len(layers))) + head
     value = args.batch / step_s
     cores = cpu_threads()
     line = {"metric": METRIC, "impl": "reference", "value": value, "unit": "tok/s", "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": step_s * 1000,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
             "data": "synthetic",
-            "config": {"workload": f"decode B={args.batch} L={args.kv_len} OLMoE-1B-7B 4-bit (config 2)",
-                       "batch": args.batch, "kv_len": args.kv_len, "layers": 16},
+            "config": {"workload": f"decode B={args.batch}/GPU L={args.kv_len} OLMoE-1B-7B 4-bit (config 2)",
+                       "batch_per_gpu": args.batch, "kv_len": args.kv_len, "layers": 16},
             "cpu_baseline": {"value": value, "unit": "tok/s", "cores": cores, "kind": "port",
-                             "sample": f"one of 16 decode layers + lm_head for {args.batch} requests at "
-                                       f"L={args.kv_len}, numpy oracle, step time = 16 x layer + head"},
+                             "sample": f"per step one of 16 decode layers for {args.batch} requests at "
+                                       f"L={args.kv_len} (numpy oracle, weights built once); lm_head timed "
+                                       f"once ({head:.2f}s); step = 16 x mean layer + head"},
             "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
@@ -239,7 +274,7 @@ def run_reference(args, rank, world):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--steps", type=int, default=30)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--batch", type=int, default=64)
@@ -304,8 +339,9 @@ def main():
     # 1) device-resident throughput
     launches0 = lib().tf_launch_count()
     clocks.start()
+    w0 = time.time()
     ms = time_steps(sess, ids, logits, args.steps, args.warmup, L, B, stream, barrier)
-    clk = clocks.stop()
+    clk = clocks.stop(w0, time.time())
     launches = (lib().tf_launch_count() - launches0) // (args.steps + args.warmup)
     if world > 1:
         t = torch.tensor([ms], device="cuda")
@@ -314,8 +350,9 @@ def main():
     value = B * world / (ms / 1000.0)
 
     # 2) phase trace of the same workload (roofline of the dominant kernel)
+    n_trace = min(args.steps, 4)
     sess.trace(True)
-    time_steps(sess, ids, logits, min(args.steps, 4), 1, L, B, stream, barrier)
+    time_steps(sess, ids, logits, n_trace, 1, L, B, stream, barrier)  # traces the warm-up step too
     sess.trace(False)
     phases = sess.trace_read()
     sess.trace_read()
@@ -327,10 +364,13 @@ def main():
     if nbytes and cnt:
         avg_ms = tot / cnt
         achieved = nbytes / (avg_ms / 1000.0) / 1e9
+        traffic = nbytes * ATTN_TRAFFIC_PER_ALGO_BYTE if dom == "attention" else None
         roof = {"bound": "hbm", "kernel": dom, "achieved": achieved, "peak": peak, "unit": "GB/s",
-                "frac": achieved / peak, "peak_source": peak_kind, "traffic": None,
+                "frac": achieved / peak, "peak_source": peak_kind, "traffic": traffic,
+                "traffic_source": "ncu dram bytes of attn_split at B=64 L=512, scaled by KV length"
+                if traffic else None,
                 "algorithmic_bytes_per_launch": nbytes, "avg_launch_ms": avg_ms}
-    step_phase_ms = {p: round(v[0] / max(1, min(args.steps, 4)), 4) for p, v in phases.items() if v[1]}
+    step_phase_ms = {p: round(v[0] / (n_trace + 1), 4) for p, v in phases.items() if v[1]}
 
     # 3) end to end through the C-ABI call with host buffers
     ids_host = ids.cpu().pin_memory()
