@@ -317,6 +317,13 @@ int tf_session_get_lengths(tf_session* session, int32_t* lengths, int32_t batch)
 #define TF_HOST_INPUTS 1  /* token ids are host pointers                   */
 #define TF_HOST_OUTPUT 2  /* logits / next-token output is a host pointer  */
 
+/* Greedy next tokens: tokens[r] = all(isfinite(logits[r])) ? argmax(logits[r])
+ * : -1 (int64, device memory), argmax taking the lowest index among equal
+ * maxima; logits f32 [rows][vocab] in device memory.
+ * Replaces the greedy submission's where(all(isfinite(logits)),
+ * argmax(logits), -1) (patches/executorch.patch:1350-1353). */
+int tf_greedy_tokens(const float* logits, int64_t rows, int64_t vocab, int64_t* tokens, void* stream);
+
 /* One decode token for each of `batch` requests (requests 0..batch-1).
  * positions (always a host array, or NULL for "the committed lengths") must
  * equal each request's committed length; on success each length grows by
@@ -328,6 +335,21 @@ int tf_session_get_lengths(tf_session* session, int32_t* lengths, int32_t batch)
  * (MLXNativeGraniteMoEPrefill.h:347-493). */
 int tf_session_decode(tf_session* session, const int64_t* token_ids, const int32_t* positions,
                       int32_t batch, float* logits, int flags, void* stream);
+
+/* tf_session_decode followed by greedy selection on the device: tokens[b] =
+ * all(isfinite(logits[b])) ? argmax : -1 (int64; device memory, or host
+ * memory with TF_HOST_OUTPUT, in which case the call returns after the copy).
+ * logits (optional, may be NULL) receives the f32 logits like
+ * tf_session_decode.  Device-memory token_ids may be the `tokens` of the
+ * previous greedy step, so step t+1 can be submitted before the host reads
+ * step t's token (one-ahead submission); a negative id is read as token 0
+ * (the reference's maximum(token, 0)) and the caller rejects the -1 it reads.
+ * Host token ids must lie in [0, vocab).
+ * Replaces nextGreedyPipelineExpectedGeneration: (src/apple/
+ * TFETResidentSession.mm:1113-1189) and the resident greedy submission
+ * (patches/executorch.patch:1341-1375, 1119-1127). */
+int tf_session_decode_greedy(tf_session* session, const int64_t* token_ids, const int32_t* positions,
+                             int32_t batch, int64_t* tokens, float* logits, int flags, void* stream);
 
 /* Prefill a batch of requests: request requests[i] receives token_counts[i]
  * ids (concatenated in token_ids) starting at its committed length.  Writes

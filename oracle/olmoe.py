@@ -351,6 +351,19 @@ def olmoe_route(logits, k, act):
     return idx, gates
 
 
+def greedy_token(logits):
+    """Greedy next token per row of fp32 logits: argmax (first occurrence on
+    ties) when every logit of the row is finite, else -1.
+
+    Restates the greedy submission's ``where(all(isfinite(logits)),
+    argmax(logits), -1)`` (``patches/executorch.patch:1350-1353``)."""
+    lg = np.asarray(logits, np.float32)
+    lg2 = lg.reshape(-1, lg.shape[-1])
+    ok = np.isfinite(lg2).all(axis=1)
+    idx = np.argmax(np.where(np.isfinite(lg2), lg2, -np.inf), axis=1)
+    return np.where(ok, idx, -1).astype(np.int64).reshape(lg.shape[:-1])
+
+
 def route_sort(indices, num_experts):
     """Stable grouping of the flat routes by expert.
 

@@ -134,3 +134,120 @@ def test_full_geometry_layer_tensor_core_path(act):
     assert ops.device_error() == 0
     sess.close()
     model.close()
+
+
+def test_greedy_tokens_kernel_matches_oracle():
+    from trifuse_b200 import ops
+    rng = np.random.default_rng(31)
+    lg = rng.standard_normal((9, 50304)).astype(np.float32)
+    lg[1, [100, 40000]] = 9.0            # tie -> lower index
+    lg[2, 7] = np.nan
+    lg[3, 50303] = np.inf
+    lg[4, 0] = -np.inf
+    lg[5, :] = 1.0                       # all equal -> index 0
+    lg[6, 50303] = 50.0                  # maximum in the last slot
+    got = ops.greedy_tokens(torch.from_numpy(lg).cuda())
+    assert host(got).tolist() == oracle.greedy_token(lg).tolist()
+    assert ops.device_error() == 0
+
+
+def test_decode_greedy_and_one_ahead_pipeline(tiny):
+    """decode_greedy == argmax of decode's logits, and the pipelined
+    generation (next step submitted with the device tokens before the host
+    reads them) yields the same tokens as a host loop."""
+    cfg, model, sess, ow, ocfg = tiny
+    prompts = [[3, 7, 11], [5, 1]]
+
+    def host_loop(n):
+        sess.reset()
+        sess.prefill([0, 1], prompts)
+        ids = torch.tensor([9, 4], dtype=torch.int64)
+        out = []
+        for _ in range(n):
+            lg = sess.decode(ids)
+            ids = torch.as_tensor(oracle.greedy_token(lg.numpy()), dtype=torch.int64)
+            out.append(ids.tolist())
+        return out
+
+    want = host_loop(6)
+    sess.reset()
+    sess.prefill([0, 1], prompts)
+    tok = sess.decode_greedy(torch.tensor([9, 4], dtype=torch.int64), tokens=torch.empty(2, dtype=torch.int64))
+    assert tok.tolist() == want[0]
+    sess.reset()
+    sess.prefill([0, 1], prompts)
+    got = sess.generate_greedy([9, 4], 6)
+    assert got == want
+    assert sess.lengths(2) == [3 + 6, 2 + 6]
+    assert model_device_error_clear() == 0
+
+
+def model_device_error_clear():
+    from trifuse_b200 import ops
+    return ops.device_error()
+
+
+def test_embedding_reads_row_zero_for_out_of_range_device_ids(tiny):
+    """Device ids are not checked on the host: a negative id (the greedy -1
+    fed back) reads row 0 like the reference's maximum(token, 0); an id past
+    the table reads row 0 and records device error 6."""
+    from trifuse_b200 import ops
+    from trifuse_b200.quant import random_affine
+    g = torch.Generator(device="cuda")
+    g.manual_seed(3)
+    q, s, b = random_affine((64, 256), g, "cuda")
+    row0 = ops.native_affine_embedding(torch.tensor([0], device="cuda"), q, s, b, 64, 4)
+    import ctypes as C
+    from trifuse_b200._lib import check, lib
+    from trifuse_b200.ops import affine_desc
+    w = affine_desc(q, s, b, 64, 4)
+    ids = torch.tensor([-1, 64], dtype=torch.int64, device="cuda")
+    y = torch.empty((2, 256), dtype=torch.float16, device="cuda")
+    assert ops.device_error(clear=True) == 0
+    check(lib().tf_affine_embedding(C.c_void_p(ids.data_ptr()), 2, C.byref(w), 1, C.c_void_p(y.data_ptr()),
+                                    C.c_void_p(torch.cuda.current_stream().cuda_stream)))
+    assert torch.equal(y[0], row0[0]) and torch.equal(y[1], row0[0])
+    assert ops.device_error(clear=True) == 6
+    assert ops.device_error() == 0
+
+
+def test_model_from_checkpoint_matches_model_from_tensors(tmp_path):
+    """A checkpoint directory written in the reference's layout (experts one
+    per tensor, two safetensors files) loads into a model whose logits equal,
+    bit for bit, those of the same weights bound directly."""
+    import json
+
+    from trifuse_b200 import checkpoint as ck
+    from trifuse_b200.model import Model, Session
+    from trifuse_b200.quant import synthetic_olmoe
+    cfg = tiny_cfg()
+    w = synthetic_olmoe(cfg, seed=11, device="cuda")
+    src = {k: v.cpu().numpy() if v.dtype != torch.uint32 else v.cpu().view(torch.int32).numpy().view(np.uint32)
+           for k, v in w.items()}
+    per = {}
+    for name, a in src.items():
+        if ".mlp.switch_mlp." in name:
+            layer, rest = name.split(".mlp.switch_mlp.")
+            for e in range(a.shape[0]):
+                per[f"{layer}.mlp.experts.{e}.{rest}"] = a[e]
+        else:
+            per[name] = a
+    names = sorted(per)
+    ck.write_safetensors(tmp_path / "a.safetensors", {n: per[n] for n in names[::2]})
+    ck.write_safetensors(tmp_path / "b.safetensors", {n: per[n] for n in names[1::2]})
+    (tmp_path / "config.json").write_text(json.dumps(dict(
+        model_type="olmoe", num_hidden_layers=cfg.layers, hidden_size=cfg.hidden, intermediate_size=cfg.intermediate,
+        num_attention_heads=cfg.heads, num_key_value_heads=cfg.kv_heads, head_dim=cfg.head_dim,
+        vocab_size=cfg.vocab, num_experts=cfg.experts, num_experts_per_tok=cfg.top_k, rms_norm_eps=cfg.rms_eps,
+        rope_theta=cfg.rope_theta, norm_topk_prob=False, quantization={"bits": 4, "group_size": 64})))
+    m1 = Model(cfg, w)
+    m2 = ck.load_model(tmp_path, capacity=cfg.capacity)
+    out = []
+    for m in (m1, m2):
+        s = Session(m, max_batch=2, capacity=64, max_prefill_tokens=32)
+        s.prefill([0, 1], [[1, 2, 3], [4, 5]])
+        out.append(host(s.decode(torch.tensor([7, 8], dtype=torch.int64))))
+        s.close()
+    m1.close()
+    m2.close()
+    assert np.array_equal(out[0], out[1])

@@ -61,6 +61,7 @@ SIGNATURES = {
     "tf_affine_qmm": [P, I64, C.POINTER(AffineWeight), C.c_int, P, P],
     "tf_affine_gather_qmm": [P, I64, I32, P, P, I64, C.POINTER(AffineWeight), C.c_int, C.c_int, P, P],
     "tf_affine_embedding": [P, I64, C.POINTER(AffineWeight), C.c_int, P, P],
+    "tf_greedy_tokens": [P, I64, I64, P, P],
     "tf_olmoe_softmax": [P, I64, I32, C.c_int, P, P],
     "tf_olmoe_topk_indices": [P, I64, I32, I32, C.c_int, P, P],
     "tf_take_along_last": [P, I64, I32, P, I32, C.c_int, P, P],
@@ -87,6 +88,7 @@ SIGNATURES = {
     "tf_session_set_lengths": [P, P, I32],
     "tf_session_get_lengths": [P, P, I32],
     "tf_session_decode": [P, P, P, I32, P, C.c_int, P],
+    "tf_session_decode_greedy": [P, P, P, I32, P, P, C.c_int, P],
     "tf_session_prefill": [P, P, P, I32, P, P, C.c_int, P],
     "tf_session_cancel": [P],
     "tf_launch_count": [],

@@ -94,7 +94,9 @@ int tf_set_qmm_path(int path) {
 
 int tf_device_error(int clear) {
   TF_CUDA(cudaDeviceSynchronize());
-  return read_tc_error(clear != 0);
+  const int tc = read_tc_error(clear != 0);
+  const int emb = read_embed_error(clear != 0);
+  return tc ? tc : emb;
 }
 
 const char* tf_last_error(void) { return g_error.c_str(); }
@@ -189,6 +191,13 @@ int tf_affine_gather_qmm(const void* x, int64_t x_rows, int32_t rows_per_x, cons
   p.y = y;
   p.y_stride = w->out_features;
   return launch_qmm(p, st(stream));
+}
+
+int tf_greedy_tokens(const float* logits, int64_t rows, int64_t vocab, int64_t* tokens, void* stream) {
+  if (rows < 0 || vocab <= 0) return set_error(TF_ERR_SHAPE, "greedy: rows %lld vocab %lld", (long long)rows,
+                                               (long long)vocab);
+  if (rows && (!logits || !tokens)) return set_error(TF_ERR_INVALID_ARGUMENT, "greedy: NULL pointer");
+  return launch_greedy(logits, rows, vocab, tokens, st(stream));
 }
 
 int tf_affine_embedding(const int64_t* ids, int64_t n, const tf_affine_weight* table, int out_dtype,

@@ -154,6 +154,9 @@ tf_status launch_qmm_tc(const QmmProblem& p, cudaStream_t s);
 // 0 = automatic, 1 = CUDA-core GEMV only, 2 = tensor cores whenever eligible.
 extern int g_qmm_path;
 int read_tc_error(bool clear);
+int read_embed_error(bool clear);
+// tokens[r] = all(isfinite(logits[r])) ? argmax (lowest index on ties) : -1.
+tf_status launch_greedy(const float* logits, int64_t rows, int64_t vocab, int64_t* tokens, cudaStream_t s);
 
 // ---------------------------------------------------------------- combine
 tf_status launch_combine(const void* y_sorted, const int32_t* inverse, const void* gates,

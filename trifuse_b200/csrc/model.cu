@@ -144,6 +144,7 @@ struct tf_session {
   int32_t* req = nullptr;
   int32_t* last_rows = nullptr;
   float* logits = nullptr;  // [max_batch][vocab]
+  int64_t* greedy = nullptr;  // [max_batch] greedy tokens before a host copy
   void* attn_ws = nullptr;
   size_t attn_ws_bytes = 0;
   void* moe_ws = nullptr;
@@ -369,6 +370,7 @@ int tf_session_create(tf_model* model, int32_t max_batch, int32_t capacity, int3
     s->req = k.take<int32_t>((size_t)R * 4);
     s->last_rows = k.take<int32_t>((size_t)max_batch * 4);
     s->logits = k.take<float>((size_t)max_batch * c.vocab * 4);
+    s->greedy = k.take<int64_t>((size_t)max_batch * 8);
     s->attn_ws = k.take<char>(s->attn_ws_bytes);
     s->moe_ws = k.take<char>(s->moe_ws_bytes);
   };
@@ -578,8 +580,14 @@ tf_status head_rows(tf_session* s, int64_t rows, const int32_t* sel, int64_t n, 
 
 extern "C" {
 
-int tf_session_decode(tf_session* s, const int64_t* token_ids, const int32_t* positions, int32_t batch,
-                      float* logits, int flags, void* stream) {
+}  // extern "C"
+
+namespace {
+
+// Shared body of the decode entry points: checks, input copies, the layer
+// stack and (when `head`) the final norm + lm_head into s->logits.
+tf_status decode_step(tf_session* s, const int64_t* token_ids, const int32_t* positions, int32_t batch, int flags,
+                      bool head, cudaStream_t st) {
   if (!s || !token_ids) return set_error(TF_ERR_INVALID_ARGUMENT, "decode: NULL argument");
   if (batch <= 0 || batch > s->max_batch)
     return set_error(TF_ERR_INVALID_ARGUMENT, "decode: batch %d outside [1, %d]", batch, s->max_batch);
@@ -594,19 +602,53 @@ int tf_session_decode(tf_session* s, const int64_t* token_ids, const int32_t* po
                        b, s->lengths[b]);
     if (pos[b] >= s->capacity) return set_error(TF_ERR_CAPACITY, "absolute capacity exceeded (request %d)", b);
     if (pos[b] + 1 > max_len) max_len = pos[b] + 1;
+    if ((flags & TF_HOST_INPUTS) && (token_ids[b] < 0 || token_ids[b] >= c.vocab))
+      return set_error(TF_ERR_INVALID_ARGUMENT, "token id %lld of request %d outside the vocabulary",
+                       (long long)token_ids[b], b);
   }
-  DeviceGuard g(s->m->device);
-  TraceScope ts(s->tracing ? &s->tracer : nullptr);
-  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   TF_CUDA(cudaMemcpyAsync(s->ids, token_ids, (size_t)batch * 8,
                           (flags & TF_HOST_INPUTS) ? cudaMemcpyHostToDevice : cudaMemcpyDeviceToDevice, st));
   TF_CUDA(cudaMemcpyAsync(s->pos, pos.data(), (size_t)batch * 4, cudaMemcpyHostToDevice, st));
   TF_TRY(forward_rows(s, batch, true, max_len, st));
+  if (head) TF_TRY(head_rows(s, batch, nullptr, batch, st));
+  return TF_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int tf_session_decode(tf_session* s, const int64_t* token_ids, const int32_t* positions, int32_t batch,
+                      float* logits, int flags, void* stream) {
+  DeviceGuard g(s ? s->m->device : 0);
+  TraceScope ts(s && s->tracing ? &s->tracer : nullptr);
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  TF_TRY(decode_step(s, token_ids, positions, batch, flags, logits != nullptr, st));
   if (logits) {
-    TF_TRY(head_rows(s, batch, nullptr, batch, st));
-    TF_CUDA(cudaMemcpyAsync(logits, s->logits, (size_t)batch * c.vocab * 4,
+    TF_CUDA(cudaMemcpyAsync(logits, s->logits, (size_t)batch * s->m->c.vocab * 4,
                             (flags & TF_HOST_OUTPUT) ? cudaMemcpyDeviceToHost : cudaMemcpyDeviceToDevice, st));
     if (flags & TF_HOST_OUTPUT) TF_CUDA(cudaStreamSynchronize(st));
+  }
+  for (int b = 0; b < batch; ++b) s->lengths[b] += 1;
+  return TF_OK;
+}
+
+int tf_session_decode_greedy(tf_session* s, const int64_t* token_ids, const int32_t* positions, int32_t batch,
+                             int64_t* tokens, float* logits, int flags, void* stream) {
+  if (!tokens) return set_error(TF_ERR_INVALID_ARGUMENT, "decode_greedy: NULL tokens");
+  DeviceGuard g(s ? s->m->device : 0);
+  TraceScope ts(s && s->tracing ? &s->tracer : nullptr);
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  TF_TRY(decode_step(s, token_ids, positions, batch, flags, true, st));
+  const int64_t vocab = s->m->c.vocab;
+  const bool host_out = (flags & TF_HOST_OUTPUT) != 0;
+  TF_TRY(launch_greedy(s->logits, batch, vocab, host_out ? s->greedy : tokens, st));
+  if (logits)
+    TF_CUDA(cudaMemcpyAsync(logits, s->logits, (size_t)batch * vocab * 4,
+                            host_out ? cudaMemcpyDeviceToHost : cudaMemcpyDeviceToDevice, st));
+  if (host_out) {
+    TF_CUDA(cudaMemcpyAsync(tokens, s->greedy, (size_t)batch * 8, cudaMemcpyDeviceToHost, st));
+    TF_CUDA(cudaStreamSynchronize(st));
   }
   for (int b = 0; b < batch; ++b) s->lengths[b] += 1;
   return TF_OK;

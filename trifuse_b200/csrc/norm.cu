@@ -56,15 +56,25 @@ tf_status launch_rms_norm(const void* x, int64_t rows, int width, const void* w,
 // Embedding: row ids[n] of the packed table, dequantized as fp16(code*s + b)
 // (native_affine_ops.py:29-36, 77-87) and converted to the output dtype.
 // One thread per packed word (8 values).
+__device__ int g_embed_error = 0;  // 6: a token id past the embedding table
+
 template <typename T>
 __global__ void embedding_kernel(const int64_t* __restrict__ ids, const uint32_t* __restrict__ q,
                                  const __half* __restrict__ sc, const __half* __restrict__ bi,
-                                 int width, T* __restrict__ y) {
+                                 int width, int64_t rows, T* __restrict__ y) {
   const int bpr = (width / 8 + blockDim.x - 1) / blockDim.x;  // blocks per row
   const int64_t n = blockIdx.x / bpr;
   const int word = (int)(blockIdx.x % bpr) * blockDim.x + threadIdx.x;
   if (word >= width / 8) return;
-  const int64_t row = ids[n];
+  // A negative id (the greedy "non-finite logits" token fed back on the
+  // device) reads row 0, as the reference's maximum(token, 0); an id past the
+  // table reads row 0 too and records error code 6 (tf_device_error).
+  int64_t row = ids[n];
+  if (row >= rows) {
+    if (word == 0) atomicCAS(&g_embed_error, 0, 6);
+    row = 0;
+  }
+  if (row < 0) row = 0;
   const uint32_t wv = q[row * (width / 8) + word];
   const int g = word / 8;
   const float s = __half2float(sc[row * (width / 64) + g]);
@@ -85,11 +95,23 @@ tf_status launch_embedding(const int64_t* ids, int64_t n, const tf_affine_weight
   const unsigned grid = (unsigned)(n * ((width / 8 + 255) / 256));
   if (out == TF_DTYPE_F16)
     embedding_kernel<__half><<<grid, 256, 0, s>>>(ids, t.q, (const __half*)t.scales,
-                                                   (const __half*)t.biases, width, (__half*)y);
+                                                   (const __half*)t.biases, width, t.out_features,
+                                                   (__half*)y);
   else
     embedding_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>(
-        ids, t.q, (const __half*)t.scales, (const __half*)t.biases, width, (__nv_bfloat16*)y);
+        ids, t.q, (const __half*)t.scales, (const __half*)t.biases, width, t.out_features,
+        (__nv_bfloat16*)y);
   return check_launch("embedding");
+}
+
+int read_embed_error(bool clear) {
+  int v = 0;
+  cudaMemcpyFromSymbol(&v, g_embed_error, sizeof(int));
+  if (clear) {
+    const int z = 0;
+    cudaMemcpyToSymbol(g_embed_error, &z, sizeof(int));
+  }
+  return v;
 }
 
 // True when this library's sm_100a image loads on the current device.

@@ -13,7 +13,7 @@ from dataclasses import dataclass
 
 import torch
 
-from ._lib import DTYPE_BF16, DTYPE_F16, HOST_INPUTS, HOST_OUTPUT, OLMoEConfig, check, lib
+from ._lib import DTYPE_BF16, DTYPE_F16, HOST_INPUTS, HOST_OUTPUT, OLMoEConfig, TriFuseError, check, lib
 
 
 @dataclass
@@ -126,6 +126,70 @@ class Session:
                                       C.c_void_p(logits.data_ptr()), flags,
                                       C.c_void_p(torch.cuda.current_stream().cuda_stream)))
         return logits
+
+    def decode_greedy(self, token_ids: torch.Tensor, positions=None, tokens: torch.Tensor | None = None,
+                      logits: torch.Tensor | None = None):
+        """One decode token per request followed by greedy selection on the
+        device: returns int64 tokens [B] (argmax, or -1 for rows with a
+        non-finite logit) on the device unless `tokens` is a host tensor.
+        token_ids may be the device tokens of the previous greedy step."""
+        B = token_ids.numel()
+        ids = token_ids.to(torch.int64).contiguous()
+        flags = 0 if ids.is_cuda else HOST_INPUTS
+        if tokens is None:
+            tokens = torch.empty(B, dtype=torch.int64, device=f"cuda:{self.model.device}")
+        if not tokens.is_cuda:
+            flags |= HOST_OUTPUT
+            if logits is not None and logits.is_cuda:
+                raise ValueError("decode_greedy: logits and tokens must be on the same side")
+        elif logits is not None and not logits.is_cuda:
+            raise ValueError("decode_greedy: logits and tokens must be on the same side")
+        pos = None
+        if positions is not None:
+            pos = (C.c_int32 * B)(*[int(p) for p in positions])
+        check(lib().tf_session_decode_greedy(self.handle, C.c_void_p(ids.data_ptr()), pos, B,
+                                             C.c_void_p(tokens.data_ptr()),
+                                             C.c_void_p(logits.data_ptr()) if logits is not None else None,
+                                             flags, C.c_void_p(torch.cuda.current_stream().cuda_stream)))
+        return tokens
+
+    def generate_greedy(self, first_ids, steps: int):
+        """Greedy generation with one-ahead submission (the reference's greedy
+        pipeline, TFETResidentSession.mm:1113-1189): step t+1 is submitted with
+        the device-resident tokens of step t before the host reads them, so
+        the host copy of each token overlaps the next step.  Returns the
+        tokens as a list of int lists [steps][B]; raises if a step produced
+        a non-finite row (-1) or a token outside the vocabulary."""
+        dev = f"cuda:{self.model.device}"
+        ids = torch.as_tensor(first_ids, dtype=torch.int64).reshape(-1).to(dev)
+        B = ids.numel()
+        stream = torch.cuda.current_stream()
+        bufs = [torch.empty(B, dtype=torch.int64, device=dev) for _ in range(2)]
+        host = [torch.empty(B, dtype=torch.int64, pin_memory=True) for _ in range(2)]
+        done = [torch.cuda.Event(), torch.cuda.Event()]
+        out = []
+        prev = None
+        for t in range(steps):
+            cur = bufs[t & 1]
+            self.decode_greedy(ids, tokens=cur)
+            host[t & 1].copy_(cur, non_blocking=True)
+            done[t & 1].record(stream)
+            ids = cur
+            if prev is not None:  # read step t-1 while step t runs
+                out.append(self._read_tokens(host[prev], done[prev]))
+            prev = t & 1
+        if prev is not None:
+            out.append(self._read_tokens(host[prev], done[prev]))
+        return out
+
+    def _read_tokens(self, host: torch.Tensor, event) -> list:
+        event.synchronize()
+        toks = host.tolist()
+        V = self.model.cfg.vocab
+        for tok in toks:
+            if not 0 <= tok < V:
+                raise TriFuseError(9, "Greedy pipeline token outside vocabulary")
+        return toks
 
     def prefill(self, requests, token_lists, want_logits=True):
         """Prefill several requests; token_lists: list of int64 tensors/lists."""

@@ -140,6 +140,21 @@ def native_affine_embedding(indices: Tensor, q: Tensor, scales: Tensor, biases: 
     return y
 
 
+def greedy_tokens(logits: Tensor) -> Tensor:
+    """Greedy next tokens of fp32 logits [..., vocab]: argmax (lowest index on
+    ties) where every logit of the row is finite, else -1 (int64); the
+    reference's where(all(isfinite(logits)), argmax(logits), -1)
+    (patches/executorch.patch:1350-1353)."""
+    if logits.dtype != torch.float32:
+        raise ValueError("greedy: logits must be float32")
+    _cuda(logits)
+    V = logits.shape[-1]
+    lc = logits.contiguous().reshape(-1, V)
+    out = torch.empty(lc.shape[0], dtype=torch.int64, device=logits.device)
+    check(lib().tf_greedy_tokens(_ptr(lc), lc.shape[0], V, _ptr(out), _stream()))
+    return out.reshape(logits.shape[:-1])
+
+
 def native_olmoe_softmax(x: Tensor) -> Tensor:
     """``mlx::native_olmoe_softmax`` (native_affine_ops.py:128-138): fp32
     softmax over the last axis, rounded to the storage dtype."""
