@@ -153,6 +153,14 @@ int tf_olmoe_topk_indices(const void* probs, int64_t rows, int32_t experts, int3
 int tf_take_along_last(const void* x, int64_t rows, int32_t width, const int32_t* indices,
                        int32_t k, int act, void* out, void* stream);
 
+/* Top-k combine + residual: out[t] = act(residual[t] + act(sum_k act(y[inverse[t*k+j]]
+ * * gates[t][j]))), the fp32 sum taken in k order from the k = 0 product.
+ * y_sorted act [tokens*k][hidden] (rows in route-sort order), inverse int32
+ * [tokens*k], gates act [tokens][k]; hidden % 8 == 0.
+ * Replaces the combine of moe() (MLXNativeGraniteMoEPrefill.h:688-695). */
+int tf_moe_combine(const void* y_sorted, const int32_t* inverse, const void* gates, const void* residual,
+                   int64_t tokens, int32_t k, int32_t hidden, int act, void* out, void* stream);
+
 /* Softmax + rank + take in one launch: (indices int32 [T][k] in rank order,
  * gates act [T][k]).  No top-k renormalisation.
  * Replaces olmoe_route (overlays/executorch/backends/mlx/runtime/

@@ -62,6 +62,7 @@ SIGNATURES = {
     "tf_affine_gather_qmm": [P, I64, I32, P, P, I64, C.POINTER(AffineWeight), C.c_int, C.c_int, P, P],
     "tf_affine_embedding": [P, I64, C.POINTER(AffineWeight), C.c_int, P, P],
     "tf_greedy_tokens": [P, I64, I64, P, P],
+    "tf_moe_combine": [P, P, P, P, I64, I32, I32, C.c_int, P, P],
     "tf_olmoe_softmax": [P, I64, I32, C.c_int, P, P],
     "tf_olmoe_topk_indices": [P, I64, I32, I32, C.c_int, P, P],
     "tf_take_along_last": [P, I64, I32, P, I32, C.c_int, P, P],

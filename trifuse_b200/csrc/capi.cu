@@ -193,6 +193,17 @@ int tf_affine_gather_qmm(const void* x, int64_t x_rows, int32_t rows_per_x, cons
   return launch_qmm(p, st(stream));
 }
 
+int tf_moe_combine(const void* y_sorted, const int32_t* inverse, const void* gates, const void* residual,
+                   int64_t tokens, int32_t k, int32_t hidden, int act, void* out, void* stream) {
+  TF_TRY(check_act(act));
+  if (tokens < 0 || k <= 0 || hidden <= 0 || hidden % 8)
+    return set_error(TF_ERR_SHAPE, "combine: tokens %lld k %d hidden %d", (long long)tokens, k, hidden);
+  if (tokens && (!y_sorted || !inverse || !gates || !residual || !out || !aligned16(y_sorted) ||
+                 !aligned16(residual) || !aligned16(out)))
+    return set_error(TF_ERR_INVALID_ARGUMENT, "combine: NULL or unaligned pointer");
+  return launch_combine(y_sorted, inverse, gates, residual, tokens, k, hidden, act, out, st(stream));
+}
+
 int tf_greedy_tokens(const float* logits, int64_t rows, int64_t vocab, int64_t* tokens, void* stream) {
   if (rows < 0 || vocab <= 0) return set_error(TF_ERR_SHAPE, "greedy: rows %lld vocab %lld", (long long)rows,
                                                (long long)vocab);

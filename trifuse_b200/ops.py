@@ -253,6 +253,23 @@ def moe_route_sort(indices: Tensor, experts: int):
     return order, inverse, offsets
 
 
+def moe_combine(y_sorted: Tensor, inverse: Tensor, gates: Tensor, residual: Tensor) -> Tensor:
+    """Top-k combine + residual (MLXNativeGraniteMoEPrefill.h:688-695): rows of
+    y_sorted are in route-sort order, inverse maps each route t*k+j to its row."""
+    _cuda(y_sorted, inverse, gates, residual)
+    T, K = gates.shape
+    H = residual.shape[-1]
+    if y_sorted.shape != (T * K, H) or inverse.numel() != T * K or residual.shape != (T, H):
+        raise ValueError("moe_combine: shape mismatch")
+    if not (y_sorted.dtype == gates.dtype == residual.dtype):
+        raise ValueError("moe_combine: y, gates and residual share the activation dtype")
+    out = torch.empty_like(residual)
+    check(lib().tf_moe_combine(_ptr(y_sorted.contiguous()), _ptr(inverse.to(torch.int32).contiguous()),
+                               _ptr(gates.contiguous()), _ptr(residual.contiguous()), T, K, H,
+                               _act(residual), _ptr(out), _stream()))
+    return out
+
+
 def moe_args(x, residual, out, router, gate, up, down, top_k, logits=None, indices=None, gates=None):
     H = x.shape[-1]
     T = x.numel() // H
