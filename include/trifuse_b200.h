@@ -369,6 +369,20 @@ int tf_session_prefill(tf_session* session, const int32_t* requests, const int32
                        int32_t num_requests, const int64_t* token_ids, float* last_logits,
                        int flags, void* stream);
 
+/* Prefill of one request's prompt in chunks of chunk_tokens (<= the
+ * session's max_prefill_tokens): every token id (host memory,
+ * TF_HOST_INPUTS required) is checked against the vocabulary before the
+ * first chunk runs; intermediate chunks only extend the KV cache, the last
+ * one also writes the last row's logits (f32 [vocab], host or device per
+ * TF_HOST_OUTPUT; a host copy containing a non-finite logit returns
+ * TF_ERR_STATE).  Cancellation is honoured between chunks.  On an error the
+ * chunks already run stay in the cache (tf_session_get_lengths tells).
+ * Replaces prefillTokenIDs:nativeConfiguration:'s chunk loop (src/apple/
+ * TFETResidentSession.mm:1546-1645: cache-only intermediate chunks, final
+ * chunk with logits, finite check). */
+int tf_session_prefill_chunked(tf_session* session, int32_t request, const int64_t* token_ids, int64_t count,
+                               int32_t chunk_tokens, float* last_logits, int flags, void* stream);
+
 /* Phase tracing (replaces the env-gated TRIFUSE_PREFILL_TIMING stderr lines,
  * src/apple/TFETResidentSession.mm:48-76, with device timing): while enabled,
  * each forward phase (embed, input_norm, qkv_proj, attention, o_proj,

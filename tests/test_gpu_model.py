@@ -251,3 +251,36 @@ def test_model_from_checkpoint_matches_model_from_tensors(tmp_path):
     m1.close()
     m2.close()
     assert np.array_equal(out[0], out[1])
+
+
+def test_chunked_prefill_matches_one_shot_and_oracle(tiny):
+    """A 29-token prompt in chunks of 8 (3 cache-only chunks + a final one)
+    gives the last-row logits of the one-shot prefill and of the oracle, and
+    leaves the same KV length; decode continues identically afterwards."""
+    cfg, model, sess, ow, ocfg = tiny
+    rng = np.random.default_rng(41)
+    prompt = rng.integers(0, cfg.vocab, size=29)
+    sess.reset()
+    one = host(sess.prefill([0], [prompt]))[0]
+    after_one = host(sess.decode(torch.tensor([5], dtype=torch.int64)))[0]
+    sess.reset()
+    chunked = sess.prefill_chunked(0, prompt, chunk=8).numpy()
+    assert sess.lengths(1) == [29]
+    after_chunked = host(sess.decode(torch.tensor([5], dtype=torch.int64)))[0]
+    kc = [np.zeros((cfg.heads, 64, cfg.head_dim), np.float32) for _ in range(cfg.layers)]
+    vc = [np.zeros((cfg.heads, 64, cfg.head_dim), np.float32) for _ in range(cfg.layers)]
+    ref = oracle.model_forward(prompt, ow, ocfg, kc, vc, 0)
+    assert_logits_close(chunked, ref, "f16")
+    assert_logits_close(chunked, one, "f16")
+    assert_logits_close(after_chunked, after_one, "f16")
+
+
+def test_chunked_prefill_validates_before_running(tiny):
+    from trifuse_b200._lib import TriFuseError
+    cfg, model, sess, ow, ocfg = tiny
+    sess.reset()
+    with pytest.raises((ValueError, TriFuseError)):
+        sess.prefill_chunked(0, [1, 2, cfg.vocab], chunk=2)    # last token outside the vocabulary
+    assert sess.lengths(1) == [0]                              # nothing ran
+    with pytest.raises((ValueError, TriFuseError)):
+        sess.prefill_chunked(0, [1, 2, 3], chunk=0)

@@ -16,6 +16,7 @@
 #include <atomic>
 #include <map>
 #include <string>
+#include <cmath>
 #include <vector>
 
 #include "common.cuh"
@@ -700,6 +701,38 @@ int tf_session_prefill(tf_session* s, const int32_t* requests, const int32_t* to
   // The host vectors above are pageable; make sure the copies finished.
   TF_CUDA(cudaStreamSynchronize(st));
   for (int i = 0; i < num_requests; ++i) s->lengths[requests[i]] += token_counts[i];
+  return TF_OK;
+}
+
+int tf_session_prefill_chunked(tf_session* s, int32_t request, const int64_t* token_ids, int64_t count,
+                               int32_t chunk_tokens, float* last_logits, int flags, void* stream) {
+  if (!s || !token_ids) return set_error(TF_ERR_INVALID_ARGUMENT, "chunked prefill: NULL argument");
+  if (!(flags & TF_HOST_INPUTS))
+    return set_error(TF_ERR_INVALID_ARGUMENT, "chunked prefill: token ids must be host memory (validated first)");
+  if (request < 0 || request >= s->max_batch)
+    return set_error(TF_ERR_INVALID_ARGUMENT, "chunked prefill: request %d outside [0, %d)", request, s->max_batch);
+  if (count <= 0) return set_error(TF_ERR_INVALID_ARGUMENT, "chunked prefill: %lld tokens", (long long)count);
+  if (chunk_tokens <= 0 || chunk_tokens > s->max_rows)
+    return set_error(TF_ERR_INVALID_ARGUMENT, "chunked prefill: chunk of %d tokens outside [1, %d]", chunk_tokens,
+                     s->max_rows);
+  if ((int64_t)s->lengths[request] + count > s->capacity)
+    return set_error(TF_ERR_CAPACITY, "absolute capacity exceeded");
+  const int64_t vocab = s->m->c.vocab;
+  // Every input is validated before the first chunk is dispatched.
+  for (int64_t i = 0; i < count; ++i)
+    if (token_ids[i] < 0 || token_ids[i] >= vocab)
+      return set_error(TF_ERR_INVALID_ARGUMENT, "chunked prefill: token %lld at %lld outside the vocabulary",
+                       (long long)token_ids[i], (long long)i);
+  for (int64_t off = 0; off < count; off += chunk_tokens) {
+    const int32_t n = (int32_t)((count - off) < chunk_tokens ? (count - off) : chunk_tokens);
+    const bool last = off + n == count;
+    // Intermediate chunks only extend the KV cache (no logits).
+    const int rc = tf_session_prefill(s, &request, &n, 1, token_ids + off, last ? last_logits : nullptr, flags, stream);
+    if (rc != TF_OK) return rc;
+  }
+  if (last_logits && (flags & TF_HOST_OUTPUT))
+    for (int64_t i = 0; i < vocab; ++i)
+      if (!std::isfinite(last_logits[i])) return set_error(TF_ERR_STATE, "non-finite final prefill logits");
   return TF_OK;
 }
 

@@ -207,6 +207,19 @@ class Session:
                                        C.c_void_p(torch.cuda.current_stream().cuda_stream)))
         return logits
 
+    def prefill_chunked(self, request: int, tokens, chunk: int = 128, want_logits: bool = True):
+        """One request's prompt in chunks of `chunk` tokens (the reference's
+        chunked prefill: cache-only intermediate chunks, logits of the last
+        row from the final chunk); returns host fp32 logits [vocab] or None."""
+        ids = torch.as_tensor(tokens, dtype=torch.int64).reshape(-1).cpu().contiguous()
+        logits = torch.empty(self.model.cfg.vocab, dtype=torch.float32) if want_logits else None
+        check(lib().tf_session_prefill_chunked(self.handle, int(request), C.c_void_p(ids.data_ptr()), ids.numel(),
+                                               int(chunk),
+                                               C.c_void_p(logits.data_ptr()) if logits is not None else None,
+                                               HOST_INPUTS | HOST_OUTPUT,
+                                               C.c_void_p(torch.cuda.current_stream().cuda_stream)))
+        return logits
+
     def trace(self, enable: bool):
         """Turn phase tracing (CUDA events around each forward phase) on/off."""
         check(lib().tf_session_trace(self.handle, int(enable)))
