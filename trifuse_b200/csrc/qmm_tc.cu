@@ -72,18 +72,26 @@ __device__ int g_tc_error = 0;  // first error code recorded by a bounded wait
 
 namespace tc {
 
-constexpr int kDeqGroups = 2;                     // dequant groups take alternate stages
-constexpr int kDeqWarps = 8 * kDeqGroups;         // 8 warps cover one stage
-constexpr int kEpiWarps = 4;
-constexpr int kLoadWarp = kDeqWarps + kEpiWarps;  // 20: packed codes + scales
-constexpr int kMmaWarp = kLoadWarp + 1;           // 21
-constexpr int kActWarp = kMmaWarp + 1;            // 22: activation tiles
-constexpr int kThreads = (kActWarp + 1) * 32;     // 736
+// Warp roles of a block with G dequant groups.  G = 2 (prefill tiles): one
+// block per SM owning all of tensor memory.  G = 1 (decode tiles): two
+// blocks per SM, 256 TMEM columns each, so two MMA issuers run side by side
+// (a small-N MMA is issue-bound, about 50 cycles per instruction).
+template <int G>
+struct Roles {
+  static constexpr int kDeqGroups = G;                 // dequant groups take alternate stages
+  static constexpr int kDeqWarps = 8 * G;              // 8 warps cover one stage
+  static constexpr int kEpiWarps = 4;
+  static constexpr int kLoadWarp = kDeqWarps + kEpiWarps;  // packed codes + scales
+  static constexpr int kMmaWarp = kLoadWarp + 1;
+  static constexpr int kActWarp = kMmaWarp + 1;            // activation tiles
+  static constexpr int kThreads = (kActWarp + 1) * 32;     // 480 or 736
+  static constexpr int kBlocksPerSM = G == 1 ? 2 : 1;
+  static constexpr uint32_t kTmemCols = G == 1 ? 256 : 512;
+};
 constexpr int kM = 128;
 constexpr int kKStep = 64;
 constexpr int kSK = 8;          // k-steps per scale slot (16 bytes of f16 per row)
 constexpr int kMaxTiles = 256;  // per-block tile table
-constexpr uint32_t kTmemCols = 512;  // whole tensor memory: accumulators + A stages
 constexpr int kACols = kKStep / 2;   // TMEM columns of one k-step of A (two f16 per column)
 constexpr long long kWaitCycles = 2000000000LL;
 // try_wait suspends the thread until the phase completes or this many ns
@@ -344,7 +352,7 @@ __device__ TileInfo lookup_tile(const Params& p, int64_t t, int nt, int lane) {
   return ti;
 }
 
-template <int NT, int KS, int PK, int SA>
+template <int NT, int KS, int PK, int SA, int SB, int G>
 struct Layout {
   static constexpr int kP = kM * 32 * KS;     // packed codes of one stage
   static constexpr int kS = 2 * kM * kSK * 2;  // scales | biases of 8 k-steps
@@ -353,27 +361,34 @@ struct Layout {
   static constexpr int kOffS = kHead;
   static constexpr int kOffP = (kOffS + 2 * kS + 1023) / 1024 * 1024;
   static constexpr int kOffB = kOffP + PK * kP;
-  static constexpr int kBytes = kOffB + SA * kB + 1024;  // + alignment slack
+  static constexpr int kBytes = kOffB + SB * kB + 1024;  // + alignment slack
   // TMEM columns: accumulators [0, 2 NT), A stages from 2 NT on.
   static constexpr int kAStage = KS * kACols;
   static constexpr int kACol0 = 2 * NT;
   static_assert(kP % 1024 == 0 && kB % 1024 == 0, "stage sizes keep 1024-byte alignment");
   static_assert(kSK % KS == 0, "a scale slot holds whole stages");
-  static_assert(kACol0 + SA * kAStage <= (int)kTmemCols, "accumulators and A stages fit tensor memory");
+  static_assert(kACol0 + SA * kAStage <= (int)Roles<G>::kTmemCols, "accumulators and A stages fit tensor memory");
 };
 
-template <typename T, int EPI, bool PERM, int NT, int KS, int PK, int SA>
-__global__ void __launch_bounds__(kThreads, 1) qmm_tc_kernel(const __grid_constant__ Params p) {
-  using L = Layout<NT, KS, PK, SA>;
+template <typename T, int EPI, bool PERM, int NT, int KS, int PK, int SA, int SB, int G>
+__global__ void __launch_bounds__(Roles<G>::kThreads, Roles<G>::kBlocksPerSM)
+    qmm_tc_kernel(const __grid_constant__ Params p) {
+  using L = Layout<NT, KS, PK, SA, SB, G>;
+  using R = Roles<G>;
+  constexpr int kDeqGroups = R::kDeqGroups, kDeqWarps = R::kDeqWarps, kEpiWarps = R::kEpiWarps;
+  constexpr int kLoadWarp = R::kLoadWarp, kMmaWarp = R::kMmaWarp, kActWarp = R::kActWarp;
+  constexpr uint32_t kTmemCols = R::kTmemCols;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* p_full = reinterpret_cast<uint64_t*>(base);
   uint64_t* p_empty = p_full + PK;
   uint64_t* s_full = p_empty + PK;
   uint64_t* s_empty = s_full + 2;
-  uint64_t* ab_full = s_empty + 2;
-  uint64_t* ab_empty = ab_full + SA;
-  uint64_t* acc_full = ab_empty + SA;
+  uint64_t* a_full = s_empty + 2;  // A stage in TMEM written (dequant warps of one group)
+  uint64_t* a_empty = a_full + SA;  // A stage read by its MMAs (commit)
+  uint64_t* b_full = a_empty + SA;  // activation stage landed (TMA)
+  uint64_t* b_empty = b_full + SB;  // activation stage read by its MMAs (commit)
+  uint64_t* acc_full = b_empty + SB;
   uint64_t* acc_empty = acc_full + 2;
   uint64_t* drain = acc_empty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
@@ -399,8 +414,12 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_tc_kernel(const __grid_consta
       mbar_init(&acc_empty[i], kEpiWarps);
     }
     for (int i = 0; i < SA; ++i) {
-      mbar_init(&ab_full[i], kDeqWarps / kDeqGroups + 1);  // one group + the activation loader's expect_tx
-      mbar_init(&ab_empty[i], 1);
+      mbar_init(&a_full[i], kDeqWarps / kDeqGroups);
+      mbar_init(&a_empty[i], 1);
+    }
+    for (int i = 0; i < SB; ++i) {
+      mbar_init(&b_full[i], 1);
+      mbar_init(&b_empty[i], 1);
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -464,20 +483,19 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_tc_kernel(const __grid_consta
     }
   } else if (warp == kActWarp) {
     // ---- activation loader: lane 0 streams each stage's activation tiles
-    // (SA stages ahead of the MMA); its expect_tx is one of the stage
-    // barrier's arrivals.
+    // into their own SB-deep ring, independent of the A stages in TMEM.
     if (lane == 0) {
       int64_t g = 0;
       bool ok = true;
       for (int li = 0; li < ntiles && ok; ++li) {
         const int s0 = table[li].s0;
         for (int k = 0; k < nk && ok; k += KS, ++g) {
-          const int as = (int)(g % SA);
-          if (g >= SA && !(ok = mbar_wait(&ab_empty[as], (uint32_t)(((g / SA) - 1) & 1), abort_flag, 13))) break;
-          uint8_t* bdst = ring_b + (size_t)as * L::kB;
-          mbar_expect_tx(&ab_full[as], (uint32_t)L::kB);
+          const int bs = (int)(g % SB);
+          if (g >= SB && !(ok = mbar_wait(&b_empty[bs], (uint32_t)(((g / SB) - 1) & 1), abort_flag, 13))) break;
+          uint8_t* bdst = ring_b + (size_t)bs * L::kB;
+          mbar_expect_tx(&b_full[bs], (uint32_t)L::kB);
 #pragma unroll
-          for (int kk = 0; kk < KS; ++kk) tma_2d(bdst + kk * NT * 128, &p.tm_x, (k + kk) * kKStep, s0, &ab_full[as]);
+          for (int kk = 0; kk < KS; ++kk) tma_2d(bdst + kk * NT * 128, &p.tm_x, (k + kk) * kKStep, s0, &b_full[bs]);
         }
       }
     }
@@ -488,7 +506,7 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_tc_kernel(const __grid_consta
     // TMEM columns of its row.  Every lane waits on the full barriers
     // (warp-uniform result); one lane per warp arrives on the release
     // barriers after __syncwarp (the barriers count warps).
-    static_assert(KS == 2 && kDeqGroups == 2 && kSK / KS == 4,
+    static_assert(KS == 2 && (kDeqGroups == 1 || kDeqGroups == 2) && kSK / KS == 4,
                   "each group takes two stages (one scale pair each) of every scale block");
     constexpr int kSpb = kSK / KS;  // stages per scale block
     const int grp = warp >> 3, quarter = warp & 3, kh = (warp >> 2) & 1;
@@ -515,7 +533,7 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_tc_kernel(const __grid_consta
       const uint4 w0 = *reinterpret_cast<const uint4*>(ring_p + (size_t)ps * L::kP + pr * (32 * KS) + kh * 16);
       const uint4 w1 = *reinterpret_cast<const uint4*>(ring_p + (size_t)ps * L::kP + pr * (32 * KS) + 32 + kh * 16);
       const int as = (int)(g % SA);
-      if (g >= SA && !(ok = warp_wait(&ab_empty[as], (uint32_t)(((g / SA) - 1) & 1), abort_flag, 23))) break;
+      if (g >= SA && !(ok = warp_wait(&a_empty[as], (uint32_t)(((g / SA) - 1) & 1), abort_flag, 23))) break;
       tc_fence_after();
       // k-steps 2 sb and 2 sb + 1 of the scale block: one f16 pair of s and b.
       const uint32_t spw = sb < 2 ? (sb ? sv.y : sv.x) : (sb == 3 ? sv.w : sv.z);
@@ -544,7 +562,7 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_tc_kernel(const __grid_consta
       // after issuing the loads let the next TMA fill overtake a load still
       // in flight on another lane).
       if (lane == 0) {
-        mbar_arrive(&ab_full[as]);
+        mbar_arrive(&a_full[as]);
         mbar_arrive(&p_empty[ps]);
         if (sb + kDeqGroups >= kSpb) mbar_arrive(&s_empty[blk & 1]);
       }
@@ -564,17 +582,20 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_tc_kernel(const __grid_consta
       const uint32_t d = tmem + (uint32_t)(buf * NT);
       for (int k = 0; k < nk; k += KS, ++g) {
         const int as = (int)(g % SA);
-        if (!(ok = warp_wait(&ab_full[as], (uint32_t)((g / SA) & 1), abort_flag, 32))) break;
+        const int bs = (int)(g % SB);
+        if (!(ok = warp_wait(&a_full[as], (uint32_t)((g / SA) & 1), abort_flag, 32))) break;
+        if (!(ok = warp_wait(&b_full[bs], (uint32_t)((g / SB) & 1), abort_flag, 33))) break;
         tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < KS; ++kk) {
           const uint32_t ta = tmem + (uint32_t)(L::kACol0 + as * L::kAStage + kk * kACols);
-          const uint64_t bd = sw128_desc(smem_addr(ring_b + (size_t)as * L::kB + kk * (NT * 128)));
+          const uint64_t bd = sw128_desc(smem_addr(ring_b + (size_t)bs * L::kB + kk * (NT * 128)));
 #pragma unroll
           for (int j = 0; j < kKStep / 16; ++j)  // K=16 slice: 8 TMEM columns of A, +32 B (+2) of B
             mma_f16_ts(leader, d, ta + 8 * j, bd + 2 * j, idesc, (k + kk > 0 || j > 0) ? 1u : 0u);
         }
-        mma_commit(leader, &ab_empty[as]);
+        mma_commit(leader, &a_empty[as]);
+        mma_commit(leader, &b_empty[bs]);
       }
       if (ok) mma_commit(leader, &acc_full[buf]);
     }
@@ -617,28 +638,32 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_tc_kernel(const __grid_consta
           }
         } else {
           const int f = ti.rb * kM + q;
-          float res[16];
-          if (EPI == EPI_RESIDUAL) {
-            // All 16 residual loads before any store (y may alias residual).
 #pragma unroll
-            for (int i = 0; i < 16; ++i) {
-              const int tok = c0 + i;
-              res[i] = tok < ti.cnt && f < p.out
-                           ? to_f(static_cast<const T*>(p.residual)[(int64_t)(ti.s0 + tok) * p.residual_stride + f])
-                           : 0.f;
+          for (int i0 = 0; i0 < 16; i0 += 8) {
+            float res[8];
+            if (EPI == EPI_RESIDUAL) {
+              // All 8 residual loads before any store (y may alias residual).
+#pragma unroll
+              for (int i = 0; i < 8; ++i) {
+                const int tok = c0 + i0 + i;
+                res[i] = tok < ti.cnt && f < p.out
+                             ? to_f(static_cast<const T*>(p.residual)[(int64_t)(ti.s0 + tok) * p.residual_stride + f])
+                             : 0.f;
+              }
             }
-          }
 #pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const int tok = c0 + i;
-            if (tok < ti.cnt && f < p.out) {
-              const int64_t slot = ti.s0 + tok;
-              if (EPI == EPI_F32) {
-                static_cast<float*>(p.y)[slot * p.y_stride + f] = round_act<T>(v[i]);
-              } else if (EPI == EPI_RESIDUAL) {
-                static_cast<T*>(p.y)[slot * p.y_stride + f] = from_f<T>(res[i] + round_act<T>(v[i]));
-              } else {
-                static_cast<T*>(p.y)[slot * p.y_stride + f] = from_f<T>(v[i]);
+            for (int i = 0; i < 8; ++i) {
+              const int tok = c0 + i0 + i;
+              const float vi = v[i0 + i];
+              if (tok < ti.cnt && f < p.out) {
+                const int64_t slot = ti.s0 + tok;
+                if (EPI == EPI_F32) {
+                  static_cast<float*>(p.y)[slot * p.y_stride + f] = round_act<T>(vi);
+                } else if (EPI == EPI_RESIDUAL) {
+                  static_cast<T*>(p.y)[slot * p.y_stride + f] = from_f<T>(res[i] + round_act<T>(vi));
+                } else {
+                  static_cast<T*>(p.y)[slot * p.y_stride + f] = from_f<T>(vi);
+                }
               }
             }
           }
@@ -707,9 +732,10 @@ int num_sms() {
 
 // Weight maps (codes box {8*KS words, rows}, scales/biases box {8, rows}) and
 // the launch of one configuration.
-template <typename T, int EPI, bool PERM, int NT, int KS, int PK, int SA>
+template <typename T, int EPI, bool PERM, int NT, int KS, int PK, int SA, int SB, int G>
 tf_status launch_cfg(tc::Params& p, const QmmProblem& q, cudaStream_t s) {
-  using L = tc::Layout<NT, KS, PK, SA>;
+  using L = tc::Layout<NT, KS, PK, SA, SB, G>;
+  using R = tc::Roles<G>;
   const bool sw = EPI == EPI_SWIGLU;
   const int in = p.in;
   const int64_t rows_total = (int64_t)(q.w0.experts > 0 ? q.w0.experts : 1) * p.out;
@@ -731,27 +757,34 @@ tf_status launch_cfg(tc::Params& p, const QmmProblem& q, cudaStream_t s) {
   TF_TRY(make_map(&p.tm_x, xs, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, in, q.n, pitch * 2, 64, NT,
                   CU_TENSOR_MAP_SWIZZLE_128B));
   constexpr size_t smem = L::kBytes;
-  static_assert(smem <= 227 * 1024, "qmm_tc: shared memory budget");
+  static_assert(smem * R::kBlocksPerSM <= 226 * 1024, "qmm_tc: shared memory budget per SM");
   static bool attr = false;
   if (!attr) {
-    TF_CUDA(cudaFuncSetAttribute(tc::qmm_tc_kernel<T, EPI, PERM, NT, KS, PK, SA>,
+    TF_CUDA(cudaFuncSetAttribute(tc::qmm_tc_kernel<T, EPI, PERM, NT, KS, PK, SA, SB, G>,
                                  cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    TF_CUDA(cudaFuncSetAttribute(tc::qmm_tc_kernel<T, EPI, PERM, NT, KS, PK, SA, SB, G>,
+                                 cudaFuncAttributePreferredSharedMemoryCarveout, 100));
     attr = true;
   }
-  int64_t grid = p.tiles_bound < num_sms() ? p.tiles_bound : num_sms();
+  const int64_t slots = (int64_t)num_sms() * R::kBlocksPerSM;
+  int64_t grid = p.tiles_bound < slots ? p.tiles_bound : slots;
   const int64_t need = (p.tiles_bound + tc::kMaxTiles - 1) / tc::kMaxTiles;
   if (grid < need) grid = need;
   if (grid <= 0) return TF_OK;
-  tc::qmm_tc_kernel<T, EPI, PERM, NT, KS, PK, SA><<<(unsigned)grid, tc::kThreads, smem, s>>>(p);
+  tc::qmm_tc_kernel<T, EPI, PERM, NT, KS, PK, SA, SB, G><<<(unsigned)grid, R::kThreads, smem, s>>>(p);
   return check_launch("qmm_tc");
 }
 
 template <typename T, int EPI, bool PERM>
 tf_status launch_nt(tc::Params& p, const QmmProblem& q, int nt, cudaStream_t s) {
   switch (nt) {
-    case 32: return launch_cfg<T, EPI, PERM, 32, 2, 8, 4>(p, q, s);
-    case 64: return launch_cfg<T, EPI, PERM, 64, 2, 8, 4>(p, q, s);
-    default: return launch_cfg<T, EPI, PERM, 128, 2, 6, 4>(p, q, s);
+    // <NT, KS, PK, SA, SB, G>: expert tiles of a decode batch (many tiles,
+    // few tokens) run two blocks per SM (G = 1, 256 TMEM columns each); dense
+    // projections of a decode batch (few tiles) want one deep pipeline per
+    // block (G = 2, 4 A stages); prefill tiles one block with two groups.
+    case 32: return launch_cfg<T, EPI, PERM, 32, 2, 4, 3, 6, 1>(p, q, s);
+    case 64: return launch_cfg<T, EPI, PERM, 64, 2, 4, 4, 4, 2>(p, q, s);
+    default: return launch_cfg<T, EPI, PERM, 128, 2, 4, 4, 5, 2>(p, q, s);
   }
 }
 
