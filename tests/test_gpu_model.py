@@ -284,3 +284,39 @@ def test_chunked_prefill_validates_before_running(tiny):
     assert sess.lengths(1) == [0]                              # nothing ran
     with pytest.raises((ValueError, TriFuseError)):
         sess.prefill_chunked(0, [1, 2, 3], chunk=0)
+
+
+def test_long_prefill_tiled_attention_matches_oracle():
+    """Prompts of 150 and 77 tokens in one prefill call: several 64-row query
+    blocks and 64-key tiles per request, partial last blocks, causal masks
+    inside tiles; last-row logits against the oracle, then one decode step."""
+    import dataclasses
+
+    from trifuse_b200.model import Model, Session
+    from trifuse_b200.quant import synthetic_olmoe
+    cfg = dataclasses.replace(tiny_cfg(), capacity=256)
+    w = synthetic_olmoe(cfg, seed=17, device="cuda")
+    ow = oracle_weights(w, cfg)
+    ocfg = oracle.OLMoEConfig(layers=cfg.layers, hidden=cfg.hidden, heads=cfg.heads, head_dim=cfg.head_dim,
+                              intermediate=cfg.intermediate, vocab=cfg.vocab, experts=cfg.experts,
+                              top_k=cfg.top_k, capacity=256, act="f16")
+    model = Model(cfg, w)
+    sess = Session(model, max_batch=2, capacity=256, max_prefill_tokens=256)
+    rng = np.random.default_rng(53)
+    prompts = [rng.integers(0, cfg.vocab, size=150), rng.integers(0, cfg.vocab, size=77)]
+    try:
+        lg = host(sess.prefill([0, 1], prompts))
+        caches = [([np.zeros((cfg.heads, 256, cfg.head_dim), np.float32) for _ in range(cfg.layers)],
+                   [np.zeros((cfg.heads, 256, cfg.head_dim), np.float32) for _ in range(cfg.layers)])
+                  for _ in range(2)]
+        for r in range(2):
+            ref = oracle.model_forward(prompts[r], ow, ocfg, caches[r][0], caches[r][1], 0)
+            assert_logits_close(lg[r], ref, "f16")
+        toks = np.array([3, 4])
+        lg2 = host(sess.decode(torch.tensor(toks, dtype=torch.int64, device="cuda")))
+        for r in range(2):
+            ref = oracle.model_forward(toks[r:r + 1], ow, ocfg, caches[r][0], caches[r][1], len(prompts[r]))
+            assert_logits_close(lg2[r], ref, "f16")
+    finally:
+        sess.close()
+        model.close()

@@ -191,6 +191,12 @@ struct AttnProblem {
   void* out = nullptr;  // act [rows][heads * head_dim]
   void* ws = nullptr;
   size_t ws_bytes = 0;
+  // Optional (prefill): device int4 {first row, rows <= 64, request, first
+  // position} per query block; every row of a block belongs to one request
+  // and the rows' positions are consecutive.  With it the attention runs the
+  // tiled tensor-core kernel instead of the per-row split-K one.
+  const int4* qblocks = nullptr;
+  int nqblocks = 0;
 };
 size_t attention_ws_bytes(int64_t rows, int heads, int capacity, int act);
 tf_status launch_attention(const AttnProblem& a, cudaStream_t s);

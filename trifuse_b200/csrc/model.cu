@@ -146,6 +146,7 @@ struct tf_session {
   int32_t* last_rows = nullptr;
   float* logits = nullptr;  // [max_batch][vocab]
   int64_t* greedy = nullptr;  // [max_batch] greedy tokens before a host copy
+  int4* qblocks = nullptr;    // prefill query blocks {row, rows, request, position}
   void* attn_ws = nullptr;
   size_t attn_ws_bytes = 0;
   void* moe_ws = nullptr;
@@ -372,6 +373,7 @@ int tf_session_create(tf_model* model, int32_t max_batch, int32_t capacity, int3
     s->last_rows = k.take<int32_t>((size_t)max_batch * 4);
     s->logits = k.take<float>((size_t)max_batch * c.vocab * 4);
     s->greedy = k.take<int64_t>((size_t)max_batch * 8);
+    s->qblocks = k.take<int4>((size_t)(R / 64 + max_batch + 1) * sizeof(int4));
     s->attn_ws = k.take<char>(s->attn_ws_bytes);
     s->moe_ws = k.take<char>(s->moe_ws_bytes);
   };
@@ -467,7 +469,8 @@ tf_status dense_qmm(tf_session* s, QmmProblem& q, int64_t x_rows, cudaStream_t s
 // Forward `rows` token rows through every layer.  Inputs already on device:
 // s->ids [rows], s->pos [rows], s->req [rows] (or identity when req_ident).
 // Leaves the final hidden states in s->h0.
-tf_status forward_rows(tf_session* s, int64_t rows, bool req_ident, int max_len, cudaStream_t st) {
+tf_status forward_rows(tf_session* s, int64_t rows, bool req_ident, int max_len, cudaStream_t st,
+                       int nqblocks = 0) {
   const tf_model* m = s->m;
   const tf_olmoe_config& c = m->c;
   const int H = c.hidden, W = c.heads * c.head_dim;
@@ -513,6 +516,8 @@ tf_status forward_rows(tf_session* s, int64_t rows, bool req_ident, int max_len,
     a.out = s->attn;
     a.ws = s->attn_ws;
     a.ws_bytes = s->attn_ws_bytes;
+    a.qblocks = nqblocks ? s->qblocks : nullptr;
+    a.nqblocks = nqblocks;
     trace(PH_ATTENTION, true, st);
     TF_TRY(launch_attention(a, st));
     trace(PH_ATTENTION, false, st);
@@ -664,6 +669,7 @@ int tf_session_prefill(tf_session* s, const int32_t* requests, const int32_t* to
   if (s->cancelled.load()) return set_error(TF_ERR_CANCELLED, "session cancelled");
   const tf_olmoe_config& c = s->m->c;
   std::vector<int32_t> pos, req, last(num_requests);
+  std::vector<int4> qb;
   std::vector<char> seen(s->max_batch, 0);
   int max_len = 0;
   for (int i = 0; i < num_requests; ++i) {
@@ -674,6 +680,9 @@ int tf_session_prefill(tf_session* s, const int32_t* requests, const int32_t* to
     if (n <= 0) return set_error(TF_ERR_INVALID_ARGUMENT, "prefill: request %d has %d tokens", r, n);
     const int start = s->lengths[r];
     if ((int64_t)start + n > s->capacity) return set_error(TF_ERR_CAPACITY, "absolute capacity exceeded");
+    // query blocks of up to 64 rows of this request (tiled prefill attention)
+    for (int b0 = 0; b0 < n; b0 += 64)
+      qb.push_back(make_int4((int)pos.size() + b0, n - b0 < 64 ? n - b0 : 64, r, start + b0));
     for (int t = 0; t < n; ++t) {
       pos.push_back(start + t);
       req.push_back(r);
@@ -692,7 +701,8 @@ int tf_session_prefill(tf_session* s, const int32_t* requests, const int32_t* to
   TF_CUDA(cudaMemcpyAsync(s->pos, pos.data(), (size_t)rows * 4, cudaMemcpyHostToDevice, st));
   TF_CUDA(cudaMemcpyAsync(s->req, req.data(), (size_t)rows * 4, cudaMemcpyHostToDevice, st));
   TF_CUDA(cudaMemcpyAsync(s->last_rows, last.data(), (size_t)num_requests * 4, cudaMemcpyHostToDevice, st));
-  TF_TRY(forward_rows(s, rows, false, max_len, st));
+  TF_CUDA(cudaMemcpyAsync(s->qblocks, qb.data(), qb.size() * sizeof(int4), cudaMemcpyHostToDevice, st));
+  TF_TRY(forward_rows(s, rows, false, max_len, st, (int)qb.size()));
   if (last_logits) {
     TF_TRY(head_rows(s, rows, s->last_rows, num_requests, st));
     TF_CUDA(cudaMemcpyAsync(last_logits, s->logits, (size_t)num_requests * c.vocab * 4,
