@@ -383,6 +383,16 @@ int tf_session_prefill(tf_session* session, const int32_t* requests, const int32
 int tf_session_prefill_chunked(tf_session* session, int32_t request, const int64_t* token_ids, int64_t count,
                                int32_t chunk_tokens, float* last_logits, int flags, void* stream);
 
+/* Decode steps as CUDA graphs (default on): the first step of a shape
+ * (batch, with/without logits, KV length rounded up to 256, QMM path) runs
+ * eagerly, the second is captured on a session-owned stream, later ones
+ * replay it, ordered after and before the caller's stream by events.  Host
+ * inputs are copied before each replay; cancellation is checked before it.
+ * Tracing runs steps eagerly.  The reference's counterpart is its resident
+ * decode loop reusing the compiled MLX graph (patches/executorch.patch:
+ * 1341-1375). */
+int tf_session_graphs(tf_session* session, int enable);
+
 /* Phase tracing (replaces the env-gated TRIFUSE_PREFILL_TIMING stderr lines,
  * src/apple/TFETResidentSession.mm:48-76, with device timing): while enabled,
  * each forward phase (embed, input_norm, qkv_proj, attention, o_proj,

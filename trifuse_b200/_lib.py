@@ -91,6 +91,7 @@ SIGNATURES = {
     "tf_session_decode": [P, P, P, I32, P, C.c_int, P],
     "tf_session_decode_greedy": [P, P, P, I32, P, P, C.c_int, P],
     "tf_session_prefill_chunked": [P, I32, P, I64, I32, P, C.c_int, P],
+    "tf_session_graphs": [P, C.c_int],
     "tf_session_prefill": [P, P, P, I32, P, P, C.c_int, P],
     "tf_session_cancel": [P],
     "tf_launch_count": [],

@@ -34,6 +34,8 @@ const char* const kPhaseNames[PH_COUNT] = {"embed", "input_norm", "qkv_proj", "a
                                            "post_norm", "moe_router", "moe_sort", "moe_gate_up",
                                            "moe_down", "moe_combine", "final_norm", "lm_head"};
 void count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+uint64_t launch_count() { return g_launches.load(std::memory_order_relaxed); }
+void add_launches(int64_t n) { g_launches.fetch_add((uint64_t)n, std::memory_order_relaxed); }
 
 tf_status check_launch(const char* what) {
   count_launch();

@@ -16,6 +16,10 @@ namespace tf {
 tf_status set_error(tf_status status, const char* fmt, ...);
 void clear_error();
 tf_status check_launch(const char* what);
+// Kernels launched so far (the tf_launch_count counter); graph replays add
+// the number of kernels they hold.
+uint64_t launch_count();
+void add_launches(int64_t n);
 
 #define TF_TRY(expr)                          \
   do {                                        \

@@ -17,6 +17,7 @@
 #include <map>
 #include <string>
 #include <cmath>
+#include <tuple>
 #include <vector>
 
 #include "common.cuh"
@@ -154,6 +155,18 @@ struct tf_session {
   std::atomic<int> cancelled{0};
   bool tracing = false;
   SessionTracer tracer;
+  // Decode steps as CUDA graphs, one per (batch, with logits, attention
+  // splits of 256 keys, QMM path): the first step of a shape runs eagerly,
+  // the second is captured on gstream, later ones replay it.
+  struct DecodeGraph {
+    cudaGraphExec_t exec = nullptr;
+    int64_t launches = 0;
+    int eager_runs = 0;
+  };
+  bool graphs_on = true;
+  cudaStream_t gstream = nullptr;
+  cudaEvent_t ev_in = nullptr, ev_out = nullptr;
+  std::map<std::tuple<int, int, int, int>, DecodeGraph> graphs;
 };
 
 namespace {
@@ -397,6 +410,10 @@ int tf_session_create(tf_model* model, int32_t max_batch, int32_t capacity, int3
     s->k.push_back(s->kv + per_cache * (2 * l));
     s->v.push_back(s->kv + per_cache * (2 * l + 1));
   }
+  if (cudaStreamCreateWithFlags(&s->gstream, cudaStreamNonBlocking) != cudaSuccess ||
+      cudaEventCreateWithFlags(&s->ev_in, cudaEventDisableTiming) != cudaSuccess ||
+      cudaEventCreateWithFlags(&s->ev_out, cudaEventDisableTiming) != cudaSuccess)
+    s->graphs_on = false;  // decode then always runs eagerly
   model->sessions++;
   *session = s;
   return TF_OK;
@@ -405,6 +422,11 @@ int tf_session_create(tf_model* model, int32_t max_batch, int32_t capacity, int3
 int tf_session_destroy(tf_session* s) {
   if (!s) return TF_OK;
   DeviceGuard g(s->m->device);
+  for (auto& kv : s->graphs)
+    if (kv.second.exec) cudaGraphExecDestroy(kv.second.exec);
+  if (s->ev_in) cudaEventDestroy(s->ev_in);
+  if (s->ev_out) cudaEventDestroy(s->ev_out);
+  if (s->gstream) cudaStreamDestroy(s->gstream);
   cudaFree(s->kv);
   cudaFree(s->scratch);
   s->m->sessions--;
@@ -615,6 +637,46 @@ tf_status decode_step(tf_session* s, const int64_t* token_ids, const int32_t* po
   TF_CUDA(cudaMemcpyAsync(s->ids, token_ids, (size_t)batch * 8,
                           (flags & TF_HOST_INPUTS) ? cudaMemcpyHostToDevice : cudaMemcpyDeviceToDevice, st));
   TF_CUDA(cudaMemcpyAsync(s->pos, pos.data(), (size_t)batch * 4, cudaMemcpyHostToDevice, st));
+  if (s->graphs_on && !s->tracing) {
+    const int splits = (max_len + 255) / 256;
+    tf_session::DecodeGraph& gr = s->graphs[std::make_tuple(batch, head ? 1 : 0, splits, g_qmm_path)];
+    if (gr.exec || gr.eager_runs > 0) {
+      TF_CUDA(cudaEventRecord(s->ev_in, st));
+      TF_CUDA(cudaStreamWaitEvent(s->gstream, s->ev_in, 0));
+      if (!gr.exec) {
+        // The attention grid covers `splits` blocks of 256 keys; blocks past
+        // a row's length exit at once, so the graph serves every length up to
+        // splits * 256.
+        const int graph_len = splits * 256 < s->capacity ? splits * 256 : s->capacity;
+        const uint64_t c0 = launch_count();
+        TF_CUDA(cudaStreamBeginCapture(s->gstream, cudaStreamCaptureModeThreadLocal));
+        tf_status rc = forward_rows(s, batch, true, graph_len, s->gstream);
+        if (rc == TF_OK && head) rc = head_rows(s, batch, nullptr, batch, s->gstream);
+        cudaGraph_t graph = nullptr;
+        const cudaError_t ce = cudaStreamEndCapture(s->gstream, &graph);
+        const int64_t captured = (int64_t)(launch_count() - c0);
+        add_launches(-captured);  // recorded, not run
+        if (rc != TF_OK || ce != cudaSuccess) {
+          if (graph) cudaGraphDestroy(graph);
+          if (rc != TF_OK) return rc;
+          return set_error(TF_ERR_CUDA, "decode graph capture: %s", cudaGetErrorString(ce));
+        }
+        const cudaError_t ie = cudaGraphInstantiate(&gr.exec, graph, 0);
+        cudaGraphDestroy(graph);
+        if (ie != cudaSuccess) {
+          gr.exec = nullptr;
+          return set_error(TF_ERR_CUDA, "decode graph instantiate: %s", cudaGetErrorString(ie));
+        }
+        gr.launches = captured;
+      }
+      TF_CUDA(cudaGraphLaunch(gr.exec, s->gstream));
+      add_launches(gr.launches);
+      TF_CUDA(cudaEventRecord(s->ev_out, s->gstream));
+      TF_CUDA(cudaStreamWaitEvent(st, s->ev_out, 0));
+      return TF_OK;
+    }
+    gr.eager_runs++;  // first step of this shape: kernel attributes are set, nothing is captured
+  }
   TF_TRY(forward_rows(s, batch, true, max_len, st));
   if (head) TF_TRY(head_rows(s, batch, nullptr, batch, st));
   return TF_OK;
@@ -750,6 +812,14 @@ int tf_trace_phases(void) { return PH_COUNT; }
 
 const char* tf_trace_phase_name(int phase) {
   return (phase >= 0 && phase < PH_COUNT) ? kPhaseNames[phase] : "";
+}
+
+int tf_session_graphs(tf_session* s, int enable) {
+  if (!s) return set_error(TF_ERR_INVALID_ARGUMENT, "NULL session");
+  if (enable && (!s->gstream || !s->ev_in || !s->ev_out))
+    return set_error(TF_ERR_UNSUPPORTED, "graph stream/events could not be created");
+  s->graphs_on = enable != 0;
+  return TF_OK;
 }
 
 int tf_session_trace(tf_session* s, int enable) {

@@ -242,7 +242,9 @@ bool qmm_uses_tc(const QmmProblem& p) {
   if (g_qmm_path == 2) return true;
   if (p.mode == QMM_DENSE) return p.n >= 8;
   const int experts = p.w0.experts > 0 ? p.w0.experts : 1;
-  return p.n >= 4 * (int64_t)experts;  // >= 4 tokens per expert on average
+  // From about two routes per expert on, reading each expert's weights once
+  // (tensor cores) beats the GEMV, which streams them once per route.
+  return p.n >= 2 * (int64_t)experts;
 }
 
 tf_status launch_qmm(const QmmProblem& p, cudaStream_t s) {

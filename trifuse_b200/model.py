@@ -220,6 +220,10 @@ class Session:
                                                C.c_void_p(torch.cuda.current_stream().cuda_stream)))
         return logits
 
+    def graphs(self, enable: bool):
+        """Turn CUDA-graph replay of decode steps on/off (default on)."""
+        check(lib().tf_session_graphs(self.handle, int(enable)))
+
     def trace(self, enable: bool):
         """Turn phase tracing (CUDA events around each forward phase) on/off."""
         check(lib().tf_session_trace(self.handle, int(enable)))
