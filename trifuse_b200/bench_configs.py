@@ -70,25 +70,29 @@ def experts(gen, device, n_experts=E):
 
 
 def config1(args, dev):
-    """One MoE block: T=32 bf16 tokens, dense bf16 router, 64 experts top-8."""
+    """One MoE block: T=32 bf16 tokens (or --tokens), dense bf16 router, 64 experts top-8."""
     from . import ops
     g = torch.Generator(device=dev)
     g.manual_seed(20260101)
     ex = experts(g, dev)
     router = (torch.randn(E, H, generator=g, device=dev) * 0.02).to(torch.bfloat16)
-    x = torch.randn(32, H, generator=g, device=dev).to(torch.bfloat16)
-    res = torch.randn(32, H, generator=g, device=dev).to(torch.bfloat16)
+    T = args.tokens
+    x = torch.randn(T, H, generator=g, device=dev).to(torch.bfloat16)
+    res = torch.randn(T, H, generator=g, device=dev).to(torch.bfloat16)
     _, aux = ops.moe(x, res, router, ex["gate"], ex["up"], ex["down"], K, return_aux=True)
     unique = int(torch.unique(aux["indices"]).numel())
     ms = timed(lambda: ops.moe(x, res, router, ex["gate"], ex["up"], ex["down"], K), args.iters,
                l2_flusher(dev))
-    nbytes = unique * 3 * EXPERT_PROJ_BYTES + 32 * H * 2 * 2 + E * H * 2
-    hbm, _, src = peaks()
+    nbytes = unique * 3 * EXPERT_PROJ_BYTES + T * H * 2 * 2 + E * H * 2
+    flops = T * K * 3 * 2 * H * I
+    hbm, tf, src = peaks()
     gbs = nbytes / ms / 1e6
-    return {"config": 1, "workload": "MoE block T=32 bf16, dense bf16 router, E=64 top-8", "ms": ms,
-            "unique_experts": unique, "algorithmic_bytes": nbytes, "achieved_gbs": gbs,
-            "roofline": {"bound": "hbm", "peak": hbm, "frac": gbs / hbm, "peak_source": src},
-            "l2": "flushed (256 MB written) before each iteration"}
+    tflops = flops / ms / 1e9
+    roof = {"bound": "hbm", "peak": hbm, "frac": gbs / hbm, "peak_source": src} if T <= 256 else \
+        {"bound": "tensor", "peak": tf, "frac": tflops / tf, "peak_source": src}
+    return {"config": 1, "workload": f"MoE block T={T} bf16, dense bf16 router, E=64 top-8", "ms": ms,
+            "unique_experts": unique, "algorithmic_bytes": nbytes, "achieved_gbs": gbs, "achieved_tflops": tflops,
+            "roofline": roof, "l2": "flushed (256 MB written) before each iteration"}
 
 
 def config4(args, dev):
@@ -222,6 +226,7 @@ def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--config", type=int, nargs="+", default=[1, 4, 3])
     ap.add_argument("--iters", type=int, default=20)
+    ap.add_argument("--tokens", type=int, default=32, help="config 1: tokens in the MoE block")
     args = ap.parse_args(argv)
     local = int(os.environ.get("LOCAL_RANK", 0))
     torch.cuda.set_device(local)
