@@ -618,16 +618,23 @@ __global__ void __launch_bounds__(Roles<G>::kThreads, Roles<G>::kBlocksPerSM)
         float v[16];
         tmem_ld16(taddr + c0, v);
         if (kSw) {
+          // Lanes 2j (gate row j) and 2j+1 (up row j) split the 16 tokens:
+          // the even lane finishes tokens 0-7, the odd one 8-15, each getting
+          // the partner's value with one shuffle.  SiLU uses the fast
+          // exponential and division; the result is rounded to the
+          // activation dtype like the reference's compiled silu * up.
           const int f = ti.rb * (kM / 2) + (q >> 1);
           const int fo = p.y_f16 ? perm_col(f) : f;  // an f16 operand for the next tensor-core QMM
+          const int odd = q & 1;
 #pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const float other = __shfl_xor_sync(0xffffffffu, v[i], 1);
-            const int tok = c0 + i;
-            if ((q & 1) == 0 && tok < ti.cnt && f < p.out) {
-              const float gg = round_act<T>(v[i]);
-              const float uu = round_act<T>(other);
-              const float sl = round_act<T>(gg / (1.0f + expf(-gg)));
+          for (int i = 0; i < 8; ++i) {
+            const float mine = odd ? v[8 + i] : v[i];
+            const float theirs = __shfl_xor_sync(0xffffffffu, odd ? v[i] : v[8 + i], 1);
+            const int tok = c0 + i + 8 * odd;
+            if (tok < ti.cnt && f < p.out) {
+              const float gg = round_act<T>(odd ? theirs : mine);
+              const float uu = round_act<T>(odd ? mine : theirs);
+              const float sl = round_act<T>(__fdividef(gg, 1.0f + __expf(-gg)));
               const float hv = round_act<T>(sl * uu);
               const int64_t row = (int64_t)(ti.s0 + tok) * p.y_stride;
               if (p.y_f16)
