@@ -791,7 +791,7 @@ tf_status launch_nt(tc::Params& p, const QmmProblem& q, int nt, cudaStream_t s) 
     // block (G = 2, 4 A stages); prefill tiles one block with two groups.
     case 32: return launch_cfg<T, EPI, PERM, 32, 2, 4, 3, 6, 1>(p, q, s);
     case 64: return launch_cfg<T, EPI, PERM, 64, 2, 4, 4, 4, 2>(p, q, s);
-    default: return launch_cfg<T, EPI, PERM, 128, 2, 4, 4, 5, 2>(p, q, s);
+    default: return launch_cfg<T, EPI, PERM, 192, 2, 4, 2, 3, 2>(p, q, s);
   }
 }
 
@@ -834,7 +834,7 @@ tf_status launch_qmm_tc(const QmmProblem& q, cudaStream_t s) {
   p.residual_stride = q.residual_stride;
   // Token tile: about the tokens each weight matrix serves.
   const int64_t per_matrix = p.grouped ? (q.n + experts - 1) / experts : q.n;
-  const int nt = per_matrix <= 24 ? 32 : per_matrix <= 64 ? 64 : 128;
+  const int nt = per_matrix <= 24 ? 32 : per_matrix <= 64 ? 64 : 192;
   const int64_t token_tiles = p.grouped ? experts + q.n / nt + 1 : (q.n + nt - 1) / nt;
   p.tiles_bound = token_tiles * p.row_blocks;
 #define TF_TC_EPI(E)                                                                \
