@@ -454,7 +454,7 @@ __global__ void __launch_bounds__(Roles<G>::kThreads, Roles<G>::kBlocksPerSM)
     // dequant warps) and the scales of every 8 k-steps.  Activation tiles
     // have their own warp, so the weight stream never waits on the MMA.
     if (lane == 0) {
-      int64_t g = 0, gs = 0;
+      int g = 0, gs = 0;  // stage and scale-block counters (< 2^31 per block)
       bool ok = true;
       for (int li = 0; li < ntiles && ok; ++li) {
         const TileInfo ti = table[li];
@@ -485,7 +485,7 @@ __global__ void __launch_bounds__(Roles<G>::kThreads, Roles<G>::kBlocksPerSM)
     // ---- activation loader: lane 0 streams each stage's activation tiles
     // into their own SB-deep ring, independent of the A stages in TMEM.
     if (lane == 0) {
-      int64_t g = 0;
+      int g = 0;
       bool ok = true;
       for (int li = 0; li < ntiles && ok; ++li) {
         const int s0 = table[li].s0;
@@ -516,12 +516,12 @@ __global__ void __launch_bounds__(Roles<G>::kThreads, Roles<G>::kBlocksPerSM)
     // gate rows 0..63 then up rows 64..127.
     const int pr = kSw ? ((r & 1) * 64 + (r >> 1)) : r;
     const uint32_t tlane = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(L::kACol0 + kh * (kACols / 2));
-    const int64_t total = (int64_t)ntiles * (nk / KS);
+    const int total = ntiles * (nk / KS);
     uint4 sv = make_uint4(0, 0, 0, 0), bv = sv;
     bool ok = true;
-    for (int64_t g = grp; g < total && ok; g += kDeqGroups) {
+    for (int g = grp; g < total && ok; g += kDeqGroups) {
       const int sb = (int)(g % kSpb);
-      const int64_t blk = g / kSpb;
+      const int blk = g / kSpb;
       if (sb == grp) {  // this group's first stage of a scale block
         if (!(ok = warp_wait(&s_full[blk & 1], (uint32_t)((blk >> 1) & 1), abort_flag, 21))) break;
         const uint8_t* sslot = ring_s + (size_t)(blk & 1) * L::kS;
@@ -570,7 +570,7 @@ __global__ void __launch_bounds__(Roles<G>::kThreads, Roles<G>::kBlocksPerSM)
   } else if (warp == kMmaWarp) {
     // ---- MMA issuer (whole warp, one elected lane issues)
     const uint32_t leader = elect_one();
-    int64_t g = 0;
+    int g = 0;
     bool ok = true;
     for (int li = 0; li < ntiles && ok; ++li) {
       const TileInfo ti = table[li];
