@@ -13,36 +13,36 @@
 // native_affine_ops.py:36); activations arrive in f16 (bf16 models pass an
 // exact f16 copy).
 //
-// Persistent, warp-specialized block (736 threads, one block per SM).  Work
-// moves in stages of KS k-steps (a k-step is 64 inputs = one quantization
-// group):
-//   warp 20 (code loader)  TMA of each stage's packed codes (box 8*KS words x
-//                     128 rows) into a PK-deep ring, and of the scales and
-//                     biases of every 8 k-steps (box 8 x 128) into two slots.
-//   warp 22 (activation loader)  TMA of each stage's activation tiles (box
-//                     64 x NT, 128B-swizzled = the MMA's K-major layout).
-//   warps 0-15 (dequant) two groups of 8 warps take alternate stages (the
-//                     dequant is latency-bound, so two stages in flight
-//                     nearly double its rate).  In a group, one thread per A
-//                     row and half k-step (warp w owns TMEM lanes 32(w%4)..
-//                     and k half (w/4)%2) turns packed words into f16
-//                     weights (magic-number half2 extraction + HFMA2) and
-//                     writes them with tcgen05.st straight into tensor
-//                     memory: the A operand of each stage lives in TMEM
-//                     (row = lane, two k per 32-bit column).
-//   warp 21 (MMA)     allocates all 512 TMEM columns (two NT-column
-//                     accumulators, then SA stages of A); one elected lane
-//                     issues tcgen05.mma with A from TMEM and B from shared
-//                     memory (4 x K=16 per k-step), one commit per stage.
-//   warps 16-19 (epilogue) tcgen05.ld the finished accumulator while the next
-//                     tile accumulates into the other one; SwiGLU tiles keep
-//                     gate row j and up row j in adjacent TMEM lanes, so one
-//                     shuffle pairs them.
+// Persistent, warp-specialized blocks.  Work moves in stages of KS k-steps
+// (a k-step is 64 inputs = one quantization group).  A block has G dequant
+// groups of 8 warps, then 4 epilogue warps, the code loader, the MMA warp and
+// the activation loader (Roles<G>):
+//   dequant   groups take alternate stages.  In a group one thread per A row
+//             and half k-step (warp w owns TMEM lanes 32(w%4).. and k half
+//             (w/4)%2) turns packed words into f16 weights (magic-number half2
+//             extraction + HFMA2) and writes them with tcgen05.st straight
+//             into tensor memory: the A operand of each stage lives in TMEM
+//             (row = lane, two k per 32-bit column).
+//   epilogue  tcgen05.ld the finished accumulator while the next tile
+//             accumulates into the other one; SwiGLU tiles keep gate row j
+//             and up row j in adjacent TMEM lanes and the two lanes of a pair
+//             each finish half of the tokens.
+//   code loader  TMA of each stage's packed codes (box 8*KS words x 128 rows)
+//             into a PK-deep ring, and of the scales and biases of every 8
+//             k-steps (box 8 x 128) into two slots.
+//   MMA       allocates the block's TMEM columns (two NT-column accumulators,
+//             then SA stages of A); one elected lane issues tcgen05.mma with A
+//             from TMEM and B from shared memory (4 x K=16 per k-step), waits
+//             once on the A stage and once on the B stage, and commits each
+//             stage to both release barriers.
+//   activation loader  TMA of each stage's activation tiles (box 64 x NT,
+//             128B-swizzled = the MMA's K-major layout) into an SB-deep ring.
+// G = 1 (decode expert tiles): two blocks per SM with 256 TMEM columns each,
+// so two MMA issuers run side by side (a small-N MMA is issue-bound).  G = 2
+// (dense decode projections, prefill): one block per SM with all 512.
 // Keeping A out of shared memory matters: a dequantized k-step is 16 KB per
 // 128 rows against 4 KB of packed codes, and writing it to shared memory and
-// reading it back for the MMA made shared-memory bandwidth the limit.  A
-// stage's A (dequant warps) and B (activation TMA) complete one barrier,
-// which the MMA warp waits on once per stage; one commit releases both.
+// reading it back for the MMA made shared-memory bandwidth the limit.
 //
 // Operand order: with PERM the dequant writes each group of 8 inputs in the
 // order [0,4,1,5,2,6,3,7] (what the magic-number extraction yields without
