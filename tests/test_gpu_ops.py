@@ -70,8 +70,8 @@ def test_route_against_reference_golden(ops, golden_dir, act):
     assert bits_equal(host(took), bits_to_act(z[f"route_gates_{act}"], act))
 
 
-@pytest.mark.parametrize("T,K,E", [(0, 8, 64), (1, 8, 64), (3, 8, 64), (1000, 8, 64), (65536, 8, 64),
-                                   (37, 4, 16)])
+@pytest.mark.parametrize("T,K,E", [(0, 8, 64), (1, 8, 64), (3, 8, 64), (128, 8, 64), (129, 8, 64),
+                                   (1000, 8, 64), (65536, 8, 64), (37, 4, 16), (100, 8, 256)])
 def test_route_sort_matches_stable_argsort(ops, T, K, E):
     rng = np.random.default_rng(3)
     idx = rng.integers(0, E, size=(T, K)).astype(np.int32)

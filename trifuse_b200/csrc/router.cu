@@ -371,6 +371,59 @@ __global__ void __launch_bounds__(kSortTile)
   }
 }
 
+// All of the above in one block when the routes fit one tile (decode
+// batches): per-warp counts by match mask, per-expert totals, offsets and the
+// active list, then the same placement.
+__global__ void __launch_bounds__(kSortTile)
+    sort_one_tile_kernel(const int32_t* __restrict__ ids, int n, int E, int32_t* order, int32_t* inverse,
+                         int32_t* offsets, int32_t* active, int32_t* active_count) {
+  __shared__ int32_t warp_cnt[kSortTile / 32][kSortMaxExperts];
+  __shared__ int32_t total[kSortMaxExperts];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  for (int i = threadIdx.x; i < (kSortTile / 32) * E; i += blockDim.x) warp_cnt[i / E][i % E] = 0;
+  __syncthreads();
+  const int i = threadIdx.x;
+  const bool valid = i < n;
+  const int e = valid ? ids[i] : -1;
+  const unsigned peers = __match_any_sync(0xffffffffu, e);
+  const int rank = __popc(peers & ((1u << lane) - 1u));
+  if (valid && rank == 0) warp_cnt[warp][e] = __popc(peers);
+  __syncthreads();
+  for (int x = threadIdx.x; x < E; x += blockDim.x) {
+    int32_t sum = 0;
+    for (int w = 0; w < kSortTile / 32; ++w) sum += warp_cnt[w][x];
+    total[x] = sum;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int32_t run = 0, na = 0;
+    for (int x = 0; x < E; ++x) {
+      offsets[x] = run;
+      const int32_t c = total[x];
+      total[x] = run;
+      run += c;
+      if (c > 0) active[na++] = x;
+    }
+    offsets[E] = run;
+    *active_count = na;
+  }
+  __syncthreads();
+  for (int x = threadIdx.x; x < E; x += blockDim.x) {
+    int32_t run = total[x];
+    for (int w = 0; w < kSortTile / 32; ++w) {
+      const int32_t c = warp_cnt[w][x];
+      warp_cnt[w][x] = run;
+      run += c;
+    }
+  }
+  __syncthreads();
+  if (valid) {
+    const int32_t pos = warp_cnt[warp][e] + rank;
+    order[pos] = i;
+    inverse[i] = pos;
+  }
+}
+
 __global__ void gather_index_kernel(const int32_t* __restrict__ src, const int32_t* __restrict__ perm,
                                     int64_t n, int div, int32_t* dst) {
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -390,6 +443,10 @@ tf_status launch_route_sort(const int32_t* ids, int64_t n, int E, int32_t* order
   if (ws_bytes < sort_workspace_bytes(n, E))
     return set_error(TF_ERR_INVALID_ARGUMENT, "route sort workspace too small");
   const int64_t tiles = (n + kSortTile - 1) / kSortTile;
+  if (tiles == 1) {
+    sort_one_tile_kernel<<<1, kSortTile, 0, s>>>(ids, (int)n, E, order, inverse, offsets, active, active_count);
+    return check_launch("sort_one_tile");
+  }
   int32_t* tile_counts = (int32_t*)ws;
   if (tiles > 0) {
     sort_count_kernel<<<(unsigned)tiles, kSortTile, 0, s>>>(ids, n, E, tile_counts);
