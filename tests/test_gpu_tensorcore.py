@@ -45,8 +45,8 @@ def test_dense_tensor_core_qmm(ops, act, T, out, inn):
     assert_close(tc, gemv)
 
 
-@pytest.mark.parametrize("act,T,skew", [("f16", 64, False), ("bf16", 256, False), ("f16", 600, True),
-                                        ("bf16", 2048, True)])
+@pytest.mark.parametrize("act,T,skew", [("bf16", 2, False), ("f16", 12, True), ("f16", 64, False),
+                                        ("bf16", 256, False), ("f16", 600, True), ("bf16", 2048, True)])
 def test_moe_tensor_core_against_oracle(ops, act, T, skew):
     rng = np.random.default_rng(12)
     H, I, E, K = 2048, 1024, 64, 8
@@ -69,6 +69,9 @@ def test_moe_tensor_core_against_oracle(ops, act, T, skew):
     assert np.array_equal(host(aux["indices"]), raux["indices"])
     assert_close(host(moe_only), ref0)            # the gather_qmm path's own output
     assert_close(host(out), ref, ulp_act=act)     # with the residual stream
+    if T * K >= 16:  # the automatic choice takes the tensor cores from 16 routes on
+        auto = ops.moe(dev(x, act), dev(res, act), dev(w, act), d["gate"], d["up"], d["down"], K)
+        assert np.array_equal(host(auto), host(out))
 
 
 def test_expert_hook_tensor_core(ops):
