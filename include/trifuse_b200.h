@@ -18,7 +18,14 @@
  *    and contiguous, unless a parameter says "host".  `stream` is a
  *    cudaStream_t passed as void* (NULL = the legacy default stream).
  *  - Shape and argument checks happen before any launch; a failed check
- *    launches nothing and changes no output.
+ *    launches nothing and changes no output.  Index arrays that live on the
+ *    device (expert ids, token indices, route indices) are read only by the
+ *    kernels and are not range-checked on the host: ids outside [0, experts)
+ *    or rows outside [0, x_rows) are undefined behaviour, as out-of-range
+ *    indices are in MLX's gather_qmm.  Token ids of the embedding are the
+ *    exception: an id past the table reads row 0 and records device error 6
+ *    (tf_device_error).  The Python mirror (trifuse_b200.ops) checks ids on
+ *    the host before calling in.
  *  - Activation tensors ("act") are float16 or bfloat16 (tf_dtype).  Packed
  *    weights are uint32 words holding eight 4-bit codes, code j at bits 4j;
  *    scales and biases are float16, one per group of 64 inputs

@@ -191,6 +191,26 @@ def test_expert_hook_gpu_callable(ops, sorted_ids):
     assert empty_out.shape == (0, H) and empty_inv.shape == (0,)
 
 
+def test_out_of_range_device_ids_are_rejected_before_launch(ops):
+    """The mirror range-checks device index arrays on the host (the kernels
+    index with them unchecked), like the reference ops' indexing does."""
+    rng = np.random.default_rng(9)
+    T, H, I, E = 4, 256, 128, 8
+    d = experts_dev(experts_np(rng, E, H, I))
+    x = dev(rng.standard_normal((T, H)).astype(np.float32), "f16")
+    i32 = lambda v: torch.tensor(v, dtype=torch.int32, device="cuda")  # noqa: E731
+    with pytest.raises(ValueError, match="expert index out of range"):
+        ops.expert_gpu(x, i32([0, 1]), i32([0, E]), False, d["gate"], d["up"], d["down"])
+    with pytest.raises(ValueError, match="token index out of range"):
+        ops.expert_gpu(x, i32([0, T]), i32([0, 1]), False, d["gate"], d["up"], d["down"])
+    with pytest.raises(ValueError, match="expert index out of range"):
+        ops.moe_route_sort(i32([[0, -1]]), E)
+    with pytest.raises(ValueError, match="expert index out of range"):
+        ops.native_affine_gather_qmm(x.reshape(T, 1, H), *d["gate"], i32([0, 1, 2, E]), 64, 4)
+    out, inverse = ops.expert_gpu(x, i32([0, T - 1]), i32([0, E - 1]), False, d["gate"], d["up"], d["down"])
+    assert out.shape == (2, H) and sorted(host(inverse).tolist()) == [0, 1]
+
+
 def test_attention_against_torch_golden(ops, golden_dir):
     z = np.load(golden_dir / "attention.npz")
     m = json.loads(str(z["meta"]))

@@ -41,6 +41,13 @@ def _cuda(*ts):
             raise ValueError("trifuse_b200 ops take CUDA tensors (no CPU path)")
 
 
+def _check_range(ids: Tensor, limit: int, message: str):
+    """ids must lie in [0, limit): the kernels index with them unchecked
+    (a host read of the extremes, one synchronization)."""
+    if ids.numel() and (int(ids.min()) < 0 or int(ids.max()) >= limit):
+        raise ValueError(message)
+
+
 def _ws(nbytes: int, device) -> Tensor:
     return torch.empty(max(int(nbytes), 1), dtype=torch.uint8, device=device)
 
@@ -113,8 +120,7 @@ def native_affine_gather_qmm(x: Tensor, q: Tensor, scales: Tensor, biases: Tenso
     x_index = torch.arange(xb.shape[0], device=x.device, dtype=torch.int32).reshape(x.shape[:-2])
     x_index = x_index.expand(batch).reshape(-1).contiguous()
     idx = indices.to(torch.int32).expand(batch).reshape(-1).contiguous()
-    if idx.numel() and (int(idx.min()) < 0 or int(idx.max()) >= w.experts):
-        raise ValueError("expert index out of range")
+    _check_range(idx, w.experts, "expert index out of range")
     y = torch.empty((*batch, 1, w.out_features), dtype=x.dtype, device=x.device)
     check(lib().tf_affine_gather_qmm(_ptr(xb), xb.shape[0], 1, _ptr(x_index), _ptr(idx), idx.numel(),
                                      C.byref(w), int(sorted_indices), _act(x), _ptr(y), _stream()))
@@ -239,6 +245,7 @@ def moe_route_sort(indices: Tensor, experts: int):
     666-684): (order, inverse, offsets[E+1]), int32."""
     _cuda(indices)
     idx = indices.to(torch.int32).contiguous()
+    _check_range(idx, experts, "expert index out of range")
     T = idx.shape[0] if idx.ndim > 1 else idx.numel()
     K = idx.shape[-1] if idx.ndim > 1 else 1
     n = idx.numel()
@@ -322,6 +329,8 @@ def expert_gpu(x: Tensor, token_indices: Tensor, expert_ids: Tensor, experts_sor
     H = x.shape[-1]
     xc = x.contiguous().reshape(-1, H)
     g, u, d = affine_desc(*gate), affine_desc(*up), affine_desc(*down)
+    _check_range(expert_ids, g.experts, "expert index out of range")
+    _check_range(token_indices, xc.shape[0], "token index out of range")
     n = token_indices.numel()
     out = torch.empty((n, H), dtype=x.dtype, device=x.device)
     inverse = torch.empty(n, dtype=torch.int32, device=x.device)
