@@ -19,10 +19,11 @@
  *    cudaStream_t passed as void* (NULL = the legacy default stream).
  *  - Shape and argument checks happen before any launch; a failed check
  *    launches nothing and changes no output.  Index arrays that live on the
- *    device (expert ids, token indices, route indices) are read only by the
- *    kernels and are not range-checked on the host: ids outside [0, experts)
- *    or rows outside [0, x_rows) are undefined behaviour, as out-of-range
- *    indices are in MLX's gather_qmm.  Token ids of the embedding are the
+ *    device (expert ids, token and route indices, attention positions) are
+ *    read only by the kernels and are not range-checked on the host: ids
+ *    outside [0, experts), rows outside [0, x_rows) or positions outside
+ *    [0, max_length) are undefined behaviour, as out-of-range indices are in
+ *    MLX's gather_qmm.  Route counts (tokens * k) are limited to 2^31 - 1.  Token ids of the embedding are the
  *    exception: an id past the table reads row 0 and records device error 6
  *    (tf_device_error).  The Python mirror (trifuse_b200.ops) checks ids on
  *    the host before calling in.

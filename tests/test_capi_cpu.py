@@ -87,6 +87,29 @@ def test_moe_geometry_validation():
     assert b"packed parameter geometry differs" in L.tf_last_error()
 
 
+def test_route_count_and_workspace_limits():
+    """order / inverse are int32: more than 2^31 - 1 routes is refused, and
+    the expert hook refuses a NULL workspace even when its size is claimed."""
+    L = lib()
+    nb = C.c_size_t(1 << 40)
+    p = C.c_void_p(0x100)
+    assert L.tf_moe_route_sort(p, 1 << 28, 8, 64, p, p, p, p, nb.value, None) == 2
+    assert b"bad geometry" in L.tf_last_error()
+    a = MoeArgs()
+    a.x = a.residual = a.out = 0x100
+    a.tokens, a.hidden, a.intermediate, a.experts, a.top_k, a.act = 1 << 28, 256, 128, 8, 8, 1
+    a.router.dense = 0x100
+    a.gate_proj = w(experts=8, out=128, inn=256)
+    a.up_proj = w(experts=8, out=128, inn=256)
+    a.down_proj = w(experts=8, out=256, inn=128)
+    assert L.tf_moe_workspace_size(C.byref(a), C.byref(nb)) == 2
+    assert b"2^31 - 1 routes" in L.tf_last_error()
+    g, u, d = w(experts=8, out=128, inn=256), w(experts=8, out=128, inn=256), w(experts=8, out=256, inn=128)
+    assert L.tf_moe_expert_gpu(p, 4, 256, p, p, 2, 0, 128, 8, C.byref(g), C.byref(u), C.byref(d), 1, p, p,
+                               None, 1 << 40, None) == 1
+    assert b"NULL or unaligned" in L.tf_last_error()
+
+
 def test_model_config_admission():
     L = lib()
     h = C.c_void_p()

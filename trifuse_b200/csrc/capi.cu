@@ -307,7 +307,7 @@ int tf_moe_route_sort_workspace_size(int64_t tokens, int32_t k, int32_t experts,
 int tf_moe_route_sort(const int32_t* indices, int64_t tokens, int32_t k, int32_t experts,
                       int32_t* order, int32_t* inverse, int32_t* offsets, void* workspace,
                       size_t workspace_bytes, void* stream) {
-  if (tokens < 0 || k <= 0 || experts <= 0 || experts > 256)
+  if (tokens < 0 || k <= 0 || experts <= 0 || experts > 256 || tokens > INT32_MAX / k)
     return set_error(TF_ERR_SHAPE, "route sort: bad geometry");
   const int64_t n = tokens * k;
   if (!offsets || (n && (!indices || !order || !inverse)))
@@ -369,6 +369,7 @@ static tf_status check_moe(const tf_moe_args* a) {
   if (!a) return set_error(TF_ERR_INVALID_ARGUMENT, "moe: args is NULL");
   TF_TRY(check_act(a->act));
   TF_TRY(check_route(a->tokens, a->experts, a->top_k));
+  if (a->tokens > INT32_MAX / a->top_k) return set_error(TF_ERR_SHAPE, "moe: more than 2^31 - 1 routes");
   if (a->hidden % 256 || a->hidden > 2048 || a->intermediate % 64 || a->intermediate <= 0)
     return set_error(TF_ERR_SHAPE, "moe: unsupported hidden/intermediate geometry");
   TF_TRY(check_router(&a->router, a->hidden, a->experts));
@@ -529,7 +530,7 @@ int tf_moe_expert_gpu(const void* x, int64_t x_rows, int32_t hidden, const int32
                       void* workspace, size_t workspace_bytes, void* stream) {
   (void)experts_sorted;  // the stable sort of sorted ids is the identity
   TF_TRY(check_act(act));
-  if (n < 0 || x_rows < 0 || hidden <= 0 || hidden % 64 || experts <= 0 || experts > 256)
+  if (n < 0 || n > INT32_MAX || x_rows < 0 || hidden <= 0 || hidden % 64 || experts <= 0 || experts > 256)
     return set_error(TF_ERR_SHAPE, "expert hook route arrays must be parallel integer vectors");
   TF_TRY(check_affine(gate, "gate_proj", true));
   TF_TRY(check_affine(up, "up_proj", true));
@@ -542,7 +543,7 @@ int tf_moe_expert_gpu(const void* x, int64_t x_rows, int32_t hidden, const int32
   if (workspace_bytes < plan_expert(nullptr, 0, n, x_rows, hidden, intermediate, experts, act).used)
     return set_error(TF_ERR_INVALID_ARGUMENT, "expert hook: workspace too small");
   if (n == 0) return TF_OK;
-  if (!x || !token_indices || !expert_ids || !out_sorted || !inverse || !aligned16(x))
+  if (!x || !token_indices || !expert_ids || !out_sorted || !inverse || !workspace || !aligned16(x))
     return set_error(TF_ERR_INVALID_ARGUMENT, "expert hook: NULL or unaligned pointer");
   cudaStream_t s = st(stream);
   const ExpertPlan w = plan_expert(workspace, workspace_bytes, n, x_rows, hidden, intermediate, experts, act);
