@@ -18,15 +18,18 @@
  *    and contiguous, unless a parameter says "host".  `stream` is a
  *    cudaStream_t passed as void* (NULL = the legacy default stream).
  *  - Shape and argument checks happen before any launch; a failed check
- *    launches nothing and changes no output.  Index arrays that live on the
- *    device (expert ids, token and route indices, attention positions) are
- *    read only by the kernels and are not range-checked on the host: ids
- *    outside [0, experts), rows outside [0, x_rows) or positions outside
- *    [0, max_length) are undefined behaviour, as out-of-range indices are in
- *    MLX's gather_qmm.  Route counts (tokens * k) are limited to 2^31 - 1.  Token ids of the embedding are the
- *    exception: an id past the table reads row 0 and records device error 6
- *    (tf_device_error).  The Python mirror (trifuse_b200.ops) checks ids on
- *    the host before calling in.
+ *    launches nothing and changes no output.  Route counts (tokens * k) are
+ *    limited to 2^31 - 1.
+ *  - Index arrays that live on the device (expert ids, token and route
+ *    indices, attention positions) are read only by the kernels and are not
+ *    range-checked on the host: ids outside [0, experts), rows outside
+ *    [0, x_rows) or positions outside [0, max_length) are undefined
+ *    behaviour, as out-of-range indices are in MLX's gather_qmm.  Token ids
+ *    of the embedding are the exception: a negative id reads row 0 (the
+ *    reference's maximum(token, 0)), and an id past the table reads row 0
+ *    and records device error 6 (tf_device_error).  Host-resident ids
+ *    (session calls with TF_HOST_INPUTS) are checked before any launch, and
+ *    the Python mirror (trifuse_b200.ops) checks device ids on the host.
  *  - Activation tensors ("act") are float16 or bfloat16 (tf_dtype).  Packed
  *    weights are uint32 words holding eight 4-bit codes, code j at bits 4j;
  *    scales and biases are float16, one per group of 64 inputs

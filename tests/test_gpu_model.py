@@ -96,6 +96,9 @@ def test_session_admission_rules(tiny):
     assert sess.lengths(2) == [3, 3]
     sess.reset()
     assert sess.lengths(2) == [0, 0]
+    with pytest.raises(ValueError, match="outside the vocabulary"):
+        sess.prefill([0, 1], [[1, 2], [3, cfg.vocab]])
+    assert sess.lengths(2) == [0, 0]
     out = sess.decode(ids)
     assert torch.isfinite(out).all()
 

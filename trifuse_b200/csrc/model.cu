@@ -755,6 +755,11 @@ int tf_session_prefill(tf_session* s, const int32_t* requests, const int32_t* to
   const int64_t rows = (int64_t)pos.size();
   if (rows > s->max_rows)
     return set_error(TF_ERR_CAPACITY, "prefill: %lld rows exceed the session's %d", (long long)rows, s->max_rows);
+  if (flags & TF_HOST_INPUTS)
+    for (int64_t i = 0; i < rows; ++i)
+      if (token_ids[i] < 0 || token_ids[i] >= c.vocab)
+        return set_error(TF_ERR_INVALID_ARGUMENT, "prefill: token id %lld at row %lld outside the vocabulary",
+                         (long long)token_ids[i], (long long)i);
   DeviceGuard g(s->m->device);
   TraceScope ts(s->tracing ? &s->tracer : nullptr);
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
