@@ -474,11 +474,12 @@ static tf_status attention_impl(const AttnProblem& a, cudaStream_t s) {
   TF_TRY(check_launch("attn_append"));
   if (a.qblocks && a.nqblocks > 0) {
     // Prefill rows grouped per request: tiled tensor-core attention.
-    static bool attr = false;
-    if (!attr) {
+    static PerDeviceOnce attr;
+    int dev = 0;
+    if (attr.needed(&dev)) {
       TF_CUDA(cudaFuncSetAttribute(attn_prefill_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                    kPrefillSmem));
-      attr = true;
+      attr.mark(dev);
     }
     dim3 pgrid((unsigned)a.nqblocks, a.heads);
     attn_prefill_kernel<T><<<pgrid, kPrefillThreads, kPrefillSmem, s>>>(

@@ -6,6 +6,7 @@
 #include <stddef.h>
 #include <stdint.h>
 
+#include <atomic>
 #include <string>
 
 #include "../../include/trifuse_b200.h"
@@ -35,6 +36,23 @@ void add_launches(int64_t n);
   } while (0)
 
 inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+// Kernel attributes (cudaFuncSetAttribute) belong to the kernel's image on
+// the current device, so a launcher sets them once per device: one bit per
+// device ordinal below 64 (higher ordinals set them on every launch).
+struct PerDeviceOnce {
+  std::atomic<uint64_t> bits{0};
+  // True when the current device (written to *dev) still needs the setup.
+  bool needed(int* dev) {
+    int d = 0;
+    cudaGetDevice(&d);
+    *dev = d;
+    return d >= 64 || !((bits.load(std::memory_order_acquire) >> d) & 1u);
+  }
+  void mark(int dev) {
+    if (dev < 64) bits.fetch_or(uint64_t(1) << dev, std::memory_order_release);
+  }
+};
 
 // ---------------------------------------------------------------- tracing
 // Phases of one forward; a session with profiling on records a CUDA event

@@ -765,13 +765,14 @@ tf_status launch_cfg(tc::Params& p, const QmmProblem& q, cudaStream_t s) {
                   CU_TENSOR_MAP_SWIZZLE_128B));
   constexpr size_t smem = L::kBytes;
   static_assert(smem * R::kBlocksPerSM <= 226 * 1024, "qmm_tc: shared memory budget per SM");
-  static bool attr = false;
-  if (!attr) {
+  static PerDeviceOnce attr;
+  int dev = 0;
+  if (attr.needed(&dev)) {
     TF_CUDA(cudaFuncSetAttribute(tc::qmm_tc_kernel<T, EPI, PERM, NT, KS, PK, SA, SB, G>,
                                  cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     TF_CUDA(cudaFuncSetAttribute(tc::qmm_tc_kernel<T, EPI, PERM, NT, KS, PK, SA, SB, G>,
                                  cudaFuncAttributePreferredSharedMemoryCarveout, 100));
-    attr = true;
+    attr.mark(dev);
   }
   const int64_t slots = (int64_t)num_sms() * R::kBlocksPerSM;
   int64_t grid = p.tiles_bound < slots ? p.tiles_bound : slots;
