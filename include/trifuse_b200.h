@@ -311,7 +311,8 @@ typedef struct tf_session tf_session;
  * (MLXNativeGraniteMoEPrefill.h:157-304). */
 int tf_model_create(const tf_olmoe_config* config, int device, tf_model** model);
 /* Copy `bytes` from `data` (host memory unless data_on_device) into the role
- * `name`.  Unknown names, wrong sizes and rebinding are errors. */
+ * `name`; the copy has completed when the call returns, so the source may be
+ * reused at once.  Unknown names, wrong sizes and rebinding are errors. */
 int tf_model_bind(tf_model* model, const char* name, const void* data, size_t bytes,
                   int data_on_device);
 /* All roles bound?  TF_ERR_STATE names the first missing role. */

@@ -323,6 +323,9 @@ int tf_model_bind(tf_model* model, const char* name, const void* data, size_t by
                      bytes, r.bytes);
   DeviceGuard g(model->device);
   TF_CUDA(cudaMemcpy(r.ptr, data, bytes, data_on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice));
+  // A device-to-device cudaMemcpy may return before the copy ran; the caller
+  // may reuse the source as soon as this returns.
+  if (data_on_device) TF_CUDA(cudaDeviceSynchronize());
   r.bound = true;
   return TF_OK;
 }
