@@ -110,6 +110,46 @@ def test_route_count_and_workspace_limits():
     assert b"NULL or unaligned" in L.tf_last_error()
 
 
+C_HOST = r"""
+#include <stdio.h>
+#include <string.h>
+#include "trifuse_b200.h"
+int main(void) {
+  if (tf_abi_version() != TF_ABI_VERSION) return 1;
+  if (strcmp(tf_status_name(TF_ERR_CANCELLED), "TF_ERR_CANCELLED") != 0) return 2;
+  tf_affine_weight w;
+  memset(&w, 0, sizeof w);
+  w.bits = 3; w.group_size = 64; w.out_features = 64; w.in_features = 256;
+  if (tf_affine_qmm((void*)0x100, 1, &w, TF_DTYPE_F16, (void*)0x200, NULL) != TF_ERR_INVALID_ARGUMENT ||
+      !strstr(tf_last_error(), "bits4/8")) return 3;
+  size_t bytes = 0;
+  if (tf_moe_route_sort_workspace_size(16, 8, 64, &bytes) != TF_OK || bytes == 0) return 4;
+  puts("ok");
+  return 0;
+}
+"""
+
+
+def test_header_serves_a_plain_c_host(tmp_path):
+    """A C99 host (what a cgo / FFI binding compiles against) builds with
+    -pedantic -Werror against the header, links the library and gets the
+    status codes and messages back without a GPU."""
+    import shutil
+    import subprocess
+    gcc = shutil.which("gcc")
+    if gcc is None:
+        pytest.skip("gcc not available")
+    src = tmp_path / "host.c"
+    src.write_text(C_HOST)
+    libdir = Path(_lib.LIB_PATH).resolve().parent
+    exe = tmp_path / "host"
+    subprocess.run([gcc, "-std=c99", "-Wall", "-Wextra", "-Werror", "-pedantic", f"-I{ROOT / 'include'}",
+                    str(src), f"-L{libdir}", "-ltrifuse_b200", f"-Wl,-rpath,{libdir}", "-o", str(exe)],
+                   check=True, capture_output=True)
+    out = subprocess.run([str(exe)], capture_output=True, text=True, timeout=120)
+    assert out.returncode == 0 and out.stdout.strip() == "ok", (out.returncode, out.stdout, out.stderr)
+
+
 def test_model_config_admission():
     L = lib()
     h = C.c_void_p()
