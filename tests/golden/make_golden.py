@@ -1,8 +1,9 @@
 #!/usr/bin/env python3
 """Generate the golden fixtures under tests/golden/ from the reference itself.
 
-Run in a container that has the TriFuse reference checkout (default
-``/root/reference``, override with ``TRIFUSE_REFERENCE``)::
+Run where the TriFuse reference checkout is available (by default the
+``reference`` directory beside this repository's directory; override with
+``TRIFUSE_REFERENCE``)::
 
     python tests/golden/make_golden.py
 
@@ -44,7 +45,7 @@ sys.path.insert(0, str(ROOT))
 
 import oracle  # noqa: E402
 
-REF = Path(os.environ.get("TRIFUSE_REFERENCE", "/root/reference"))
+REF = Path(os.environ.get("TRIFUSE_REFERENCE", str(ROOT.parent / "reference")))
 OPS_FILE = REF / "overlays/executorch/backends/mlx/native_affine_ops.py"
 PREP_FILE = REF / "tools/export/prepare_model.py"
 
