@@ -133,26 +133,35 @@ class ClockSampler:
                 "samples": len(sm)}
 
 
-def build_model(B, L, cap, device, layers=16):
+def build_model(cap, device, layers=16):
     import torch
 
-    from trifuse_b200.model import Config, Model, Session
+    from trifuse_b200.model import Config, Model
     from trifuse_b200.quant import synthetic_olmoe
     cfg = Config(capacity=cap, layers=layers)
     w = synthetic_olmoe(cfg, seed=20260102, device=f"cuda:{device}")
     model = Model(cfg, w, device=device)
     del w
     torch.cuda.empty_cache()
+    return cfg, model
+
+
+def decode_session(model, B, L, cap, device, seed=20260103):
+    """A session of B requests whose caches hold N(0, 1) f16 keys and values
+    in slots [0, L) of every layer."""
+    import torch
+
+    from trifuse_b200.model import Session
     sess = Session(model, max_batch=B, capacity=cap)
     g = torch.Generator(device=f"cuda:{device}")
-    g.manual_seed(20260103)
-    for layer in range(cfg.layers):
+    g.manual_seed(seed)
+    for layer in range(model.cfg.layers):
         k, v = sess.kv_tensors(layer)
         for t in (k, v):
             for b0 in range(0, B, 16):
                 t[b0:b0 + 16, :, :L].normal_(generator=g)
     torch.cuda.synchronize()
-    return cfg, model, sess
+    return sess
 
 
 def time_steps(sess, ids, logits, steps, warmup, L, B, stream, barrier):
@@ -171,6 +180,122 @@ def time_steps(sess, ids, logits, steps, warmup, L, B, stream, barrier):
     torch.cuda.synchronize()
     barrier()
     return e0.elapsed_time(e1) / steps
+
+
+def prefill_flops(seqs, T):
+    """Algorithmic flops of a prefill of `seqs` sequences of T tokens with the
+    reference's semantics (MLXNativeGraniteMoEPrefill.h:440-442, 471): layers
+    0-14 run every row; the last layer projects K and V of every row but
+    runs Q, attention, o-proj and the MoE block for the last row only; the
+    lm_head runs on the last row.  Causal attention counts 4 D flops per
+    (query, key) pair at or before the query."""
+    D = 16 * 128
+    rows = seqs * T
+    per_row = K_TOP * 3 * 2 * H * I + 2 * H * E + 4 * 2 * H * W
+    attn_seq = 4 * D * (T * (T + 1) // 2)
+    full = 15 * (rows * per_row + seqs * attn_seq)
+    last = rows * 2 * 2 * H * W + seqs * (per_row - 2 * 2 * H * W + 4 * D * T)
+    return full + last + seqs * 2 * H * V
+
+
+class PhaseRoof:
+    """Roofline entries of traced phases from their algorithmic bytes."""
+
+    def __init__(self, peak, peak_kind):
+        self.peak, self.peak_kind = peak, peak_kind
+
+    def entry(self, phases, name, nbytes):
+        tot, cnt = phases.get(name, (0.0, 0))
+        if not (nbytes and cnt):
+            return None
+        avg_ms = tot / cnt
+        achieved = nbytes / (avg_ms / 1000.0) / 1e9
+        return {"bound": "hbm", "kernel": name, "achieved": achieved, "peak": self.peak, "unit": "GB/s",
+                "frac": achieved / self.peak, "peak_source": self.peak_kind,
+                "algorithmic_bytes_per_launch": nbytes, "avg_launch_ms": avg_ms}
+
+
+def run_prefill(model, cfg, rank, world, device, warmup, iters, barrier, max_over_ranks, bf16_peak, peak_kind):
+    """8 sequences of 2048 uniform token ids, data parallel
+    over the ranks (sequence i on rank i % world), one session call per rank
+    and iteration; tok/s = 16384 / the slowest rank's time."""
+    import torch
+
+    from trifuse_b200.model import Session
+    seqs_total, T = 8, 2048
+    mine = [i for i in range(seqs_total) if i % world == rank]
+    g = torch.Generator()
+    g.manual_seed(20260103)
+    prompts = [torch.randint(0, cfg.vocab, (T,), generator=g) for _ in range(seqs_total)]
+    n = len(mine)
+    if n == 0:
+        # more ranks than sequences: this rank only takes part in the timing barriers
+        for _ in range(warmup + iters):
+            barrier()
+        return None
+    sess = Session(model, max_batch=n, capacity=T + 64, max_prefill_tokens=n * T)
+    ids_dev = torch.cat([prompts[i] for i in mine]).cuda(device)
+    logits_dev = torch.empty((n, cfg.vocab), dtype=torch.float32, device=f"cuda:{device}")
+    stream = torch.cuda.current_stream()
+
+    def timed(fn, k):
+        for _ in range(warmup):
+            sess.reset()
+            fn()
+        torch.cuda.synchronize()
+        barrier()
+        total = 0.0
+        for _ in range(k):
+            sess.reset()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            fn()
+            b.record(stream)
+            b.synchronize()
+            total += a.elapsed_time(b)
+        barrier()
+        return max_over_ranks(total / k)
+
+    reqs = list(range(n))
+    ms = timed(lambda: sess.prefill_device(reqs, [T] * n, ids_dev, logits_dev), iters)
+    e2e_ms = timed(lambda: sess.prefill(reqs, [prompts[i] for i in mine]), iters)
+    sess.reset()
+    sess.trace(True)
+    sess.prefill_device(reqs, [T] * n, ids_dev, logits_dev)
+    sess.trace(False)
+    phases = {p: round(v[0], 3) for p, v in sess.trace_read().items() if v[1]}
+    sess.close()
+    flops = prefill_flops(seqs_total, T)
+    tflops = flops / (ms / 1000.0) / 1e12
+    return {"workload": "prefill 8 x 2048 uniform token ids (config 3), sequence i on rank i % n_gpus",
+            "value": seqs_total * T / (ms / 1000.0), "unit": "tok/s", "ms_per_call": ms,
+            "scaling": "strong", "sequences_per_gpu": n,
+            "roofline": {"bound": "tensor", "achieved": tflops, "peak": bf16_peak, "unit": "TFLOP/s",
+                         "frac": tflops / bf16_peak, "peak_source": peak_kind,
+                         "algorithmic_tflop": flops / 1e12,
+                         "flops": "reference semantics: last layer last-row-only, lm_head on last rows"},
+            "e2e": {"value": seqs_total * T / (e2e_ms / 1000.0), "unit": "tok/s", "ms_per_call": e2e_ms,
+                    "h2d_bytes_per_step": seqs_total * T * 8, "d2h_bytes_per_step": seqs_total * cfg.vocab * 4},
+            "phase_ms_rank0": phases if rank == 0 else None}
+
+
+def run_sweep(model, cfg, batches, L, rank, world, device, warmup, steps, barrier, max_over_ranks):
+    """Decode tok/s at other batch sizes (config 2 sweep), same model and L."""
+    import torch
+    out = {}
+    for B in batches:
+        cap = L + 2 * (warmup + steps) + 8
+        sess = decode_session(model, B, L, cap, device, seed=20260110 + B)
+        g = torch.Generator(device="cuda")
+        g.manual_seed(20260104 + rank + B)
+        ids = torch.randint(0, cfg.vocab, (warmup + steps, B), device="cuda", generator=g, dtype=torch.int64)
+        logits = torch.empty((B, cfg.vocab), dtype=torch.float32, device="cuda")
+        ms = max_over_ranks(time_steps(sess, ids, logits, steps, warmup, L, B, torch.cuda.current_stream(), barrier))
+        out[f"B={B}"] = {"value": B * world / (ms / 1000.0), "unit": "tok/s", "ms_per_step": ms}
+        sess.close()
+        del sess
+        torch.cuda.empty_cache()
+    return out
 
 
 class CpuWorkload:
@@ -259,10 +384,10 @@ def run_reference(args, rank, world):
     cores = cpu_threads()
     line = {"metric": METRIC, "impl": "reference", "value": value, "unit": "tok/s", "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": step_s * 1000,
+            "ms_per_step_kind": "extrapolated: 16 x the mean of the sampled layers + the lm_head",
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
             "data": "synthetic",
-            "config": {"workload": f"decode B={args.batch}/GPU L={args.kv_len} OLMoE-1B-7B 4-bit (config 2)",
-                       "batch_per_gpu": args.batch, "kv_len": args.kv_len, "layers": 16},
+            "config": config_keys(args.batch, args.kv_len, world),
             "cpu_baseline": {"value": value, "unit": "tok/s", "cores": cores, "kind": "port",
                              "sample": f"per step one of 16 decode layers for {args.batch} requests at "
                                        f"L={args.kv_len} (numpy oracle, weights built once); lm_head timed "
@@ -280,6 +405,8 @@ def main():
     ap.add_argument("--batch", type=int, default=64)
     ap.add_argument("--kv-len", type=int, default=4096)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-prefill", action="store_true", help="skip the config-3 prefill measurement")
+    ap.add_argument("--sweep", default="1,16,256", help="decode batch sizes of the sweep ('' = none)")
     ap.add_argument("--layers", type=int, default=16, help="model depth (profiling small cases)")
     ap.add_argument("--ncu", action="store_true",
                     help="profiling run: warm up, then one decode step between cudaProfilerStart/Stop")
@@ -304,9 +431,17 @@ def main():
         if world > 1:
             dist.barrier()
 
+    def max_over_ranks(ms):
+        if world > 1:
+            t = torch.tensor([ms], device="cuda")
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            return float(t.item())
+        return ms
+
     B, L = args.batch, args.kv_len
-    cap = L + 2 * (args.warmup + args.steps) + 8
-    cfg, model, sess = build_model(B, L, cap, local_rank, args.layers)
+    cap = max(L + 2 * (args.warmup + args.steps) + 8, 2048 + 64)
+    cfg, model = build_model(cap, local_rank, args.layers)
+    sess = decode_session(model, B, L, cap, local_rank)
     stream = torch.cuda.current_stream()
     g = torch.Generator(device="cuda")
     g.manual_seed(20260104 + rank)
@@ -335,75 +470,94 @@ def main():
     except Exception:
         pass
     clocks = ClockSampler(uuid)
+    hbm_peak, peak_kind = measured_peaks()
+    bf16_peak = bf16_peak_tflops()
 
-    # 1) device-resident throughput
+    # 1) decode, device-resident throughput (the headline value)
     launches0 = lib().tf_launch_count()
     clocks.start()
     w0 = time.time()
-    ms = time_steps(sess, ids, logits, args.steps, args.warmup, L, B, stream, barrier)
+    ms = max_over_ranks(time_steps(sess, ids, logits, args.steps, args.warmup, L, B, stream, barrier))
     clk = clocks.stop(w0, time.time())
     launches = (lib().tf_launch_count() - launches0) // (args.steps + args.warmup)
-    if world > 1:
-        t = torch.tensor([ms], device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
     value = B * world / (ms / 1000.0)
 
-    # 2) phase trace of the same workload (roofline of the dominant kernel)
+    # 2) phase trace of the same workload: the dominant phase's roofline and
+    # the MoE gate/up and down HBM fractions
     n_trace = min(args.steps, 4)
     sess.trace(True)
     time_steps(sess, ids, logits, n_trace, 1, L, B, stream, barrier)  # traces the warm-up step too
     sess.trace(False)
     phases = sess.trace_read()
-    sess.trace_read()
     dom = max(phases, key=lambda p: phases[p][0])
-    peak, peak_kind = measured_peaks()
-    tot, cnt = phases[dom]
-    roof = None
-    nbytes = phase_bytes(dom, B, L)
-    if nbytes and cnt:
-        avg_ms = tot / cnt
-        achieved = nbytes / (avg_ms / 1000.0) / 1e9
-        traffic = nbytes * ATTN_TRAFFIC_PER_ALGO_BYTE if dom == "attention" else None
-        roof = {"bound": "hbm", "kernel": dom, "achieved": achieved, "peak": peak, "unit": "GB/s",
-                "frac": achieved / peak, "peak_source": peak_kind, "traffic": traffic,
-                "traffic_source": "ncu dram bytes of attn_split at B=64 L=512, scaled by KV length"
-                if traffic else None,
-                "algorithmic_bytes_per_launch": nbytes, "avg_launch_ms": avg_ms}
+    pr = PhaseRoof(hbm_peak, peak_kind)
+    roof = pr.entry(phases, dom, phase_bytes(dom, B, L))
+    if roof is not None:
+        if dom == "attention":
+            roof["traffic"] = roof["algorithmic_bytes_per_launch"] * ATTN_TRAFFIC_PER_ALGO_BYTE
+            roof["traffic_source"] = "ncu dram bytes of attn_split at B=64 L=512, scaled by KV length"
+        else:
+            roof["traffic"] = None
+        for ph in ("moe_gate_up", "moe_down"):
+            roof[ph] = pr.entry(phases, ph, phase_bytes(ph, B, L))
     step_phase_ms = {p: round(v[0] / (n_trace + 1), 4) for p, v in phases.items() if v[1]}
 
     # 3) end to end through the C-ABI call with host buffers
     ids_host = ids.cpu().pin_memory()
     logits_host = torch.empty((B, cfg.vocab), dtype=torch.float32, pin_memory=True)
-    e2e_ms = time_steps(sess, ids_host, logits_host, args.steps, args.warmup, L, B, stream, barrier)
-    if world > 1:
-        t = torch.tensor([e2e_ms], device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_ms = float(t.item())
+    e2e_ms = max_over_ranks(time_steps(sess, ids_host, logits_host, args.steps, args.warmup, L, B, stream, barrier))
     e2e = {"value": B * world / (e2e_ms / 1000.0), "unit": "tok/s", "h2d_bytes_per_step": B * (8 + 4),
            "d2h_bytes_per_step": B * cfg.vocab * 4, "ms_per_step": e2e_ms}
+    sess.close()
+    del sess
+    torch.cuda.empty_cache()
+
+    # 4) prefill (config 3) and 5) the decode batch sweep (config 2)
+    prefill = None
+    if not args.no_prefill and args.layers == 16:
+        prefill = run_prefill(model, cfg, rank, world, local_rank, args.warmup, max(3, min(args.steps, 5)),
+                              barrier, max_over_ranks, bf16_peak, peak_kind)
+    sweep = None
+    batches = [int(b) for b in args.sweep.split(",") if b.strip()]
+    if batches:
+        sweep = run_sweep(model, cfg, batches, L, rank, world, local_rank, args.warmup,
+                          max(3, min(args.steps, 10)), barrier, max_over_ranks)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         step_s, det = cpu_sample(B, L)
         cpu = {"value": B / step_s, "unit": "tok/s", "cores": cpu_threads(), "kind": "port",
                "sample": f"one of 16 decode layers + lm_head for {B} requests at L={L} (numpy oracle, "
-                         f"layer {det['layer_s']:.2f}s, head {det['head_s']:.2f}s), step = 16 x layer + head"}
+                         f"layer {det['layer_s']:.2f}s, head {det['head_s']:.2f}s), step = 16 x layer + head "
+                         f"(extrapolated)"}
 
     if rank == 0:
         line = {"metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
                 "vs_baseline": None, "dtype": "f16", "data": "synthetic (random-init weights, N(0,1) KV)",
-                "config": {"workload": f"decode B={B}/GPU L={L} OLMoE-1B-7B 4-bit (config 2)",
-                           "batch_per_gpu": B, "global_batch": B * world, "kv_len": L, "layers": 16,
-                           "parallelism": f"dp{world} replicas", "l2": "inputs larger than L2 (KV cache)"},
+                "config": config_keys(B, L, world),
                 "e2e": e2e, "gpu_launches": int(launches), "roofline": roof, "cpu_baseline": cpu,
-                "clocks": clk, "phase_ms_per_step": step_phase_ms}
+                "clocks": clk, "phase_ms_per_step": step_phase_ms, "prefill": prefill, "sweep": sweep}
         print(json.dumps(line), flush=True)
-    sess.close()
     model.close()
     if world > 1:
         dist.destroy_process_group()
+
+
+def config_keys(B, L, world):
+    return {"workload": f"decode B={B}/GPU L={L} OLMoE-1B-7B 4-bit (config 2)",
+            "batch_per_gpu": B, "global_batch": B * world, "kv_len": L, "layers": 16,
+            "parallelism": f"dp{world} replicas", "l2": "inputs larger than L2 (KV cache)"}
+
+
+def bf16_peak_tflops():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            return float(json.loads(p.read_text())["bf16_tflops"])
+        except Exception:
+            pass
+    return 1590.0
 
 
 if __name__ == "__main__":

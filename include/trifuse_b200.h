@@ -229,14 +229,22 @@ int tf_moe_forward(const tf_moe_args* args, void* workspace, size_t workspace_by
  * (a host framework's execute callback with a pre-planned memory arena, or a
  * serving loop where cudaMalloc/cudaFree would synchronize the device):
  * same computation and arguments as tf_moe_forward, but no workspace
- * argument and no allocation of any kind.  Its scratch is one fixed
+ * argument and no allocation by this library.  Its scratch is one fixed
  * TF_MOE_NOALLOC_SCRATCH_BYTES buffer built into this library, held on every
  * GPU that loads it.  Calls with more than TF_MOE_NOALLOC_MAX_TOKENS tokens,
  * or whose scratch would exceed the buffer (it fits 64 tokens at
- * OLMoE-1B-7B geometry), return TF_ERR_CAPACITY.  The first call on a device looks up the
- * buffer's device address, so make it before any stream capture.  All calls
- * share the buffer: calls that overlap on the GPU race and must be
- * serialized.  No counterpart in the reference. */
+ * OLMoE-1B-7B geometry), return TF_ERR_CAPACITY.  Without the workspace this
+ * entry runs every tensor-core tile on one block (no split schedule).
+ * The first call on a device looks up the buffer's device address, so make
+ * it before any stream capture; the address is kept for the process, so do
+ * not use this entry across a reset of the device (cudaDeviceReset).  With
+ * CUDA's lazy module loading (the default) the first call on a device, and
+ * the first call of each batch shape, may still load kernel modules, which
+ * allocates device memory and synchronizes inside the driver: callers that
+ * must never see that make one warm-up call per device and shape, or run
+ * with CUDA_MODULE_LOADING=EAGER.  All calls share the buffer: calls that
+ * overlap on the GPU race and must be serialized.  No counterpart in the
+ * reference. */
 #define TF_MOE_NOALLOC_SCRATCH_BYTES ((size_t)6 << 20)
 #define TF_MOE_NOALLOC_MAX_TOKENS 64
 int tf_moe_forward_noalloc(const tf_moe_args* args, void* stream);
@@ -418,11 +426,52 @@ const char* tf_trace_phase_name(int phase);
 int tf_session_trace(tf_session* session, int enable);
 int tf_session_trace_read(tf_session* session, float* total_ms, int32_t* counts);
 
+/* Diagnostic routing capture: while `indices` is non-NULL, every forward of
+ * at most max_rows rows writes each layer's top-k expert ids into it, int32
+ * [layers][rows][top_k] with the rows of that call in order (for the last
+ * layer of a prefill, the rows whose MoE block runs: each request's last
+ * row); decode steps then run without graph replay.  NULL turns it off.
+ * The counterpart of the reference's inspect / receipt diagnostics
+ * (src/apple/TFETResidentSession.mm:1816-1967); tests use it to follow the
+ * device's routing layer by layer. */
+int tf_session_capture_routing(tf_session* session, int32_t* indices, int64_t max_rows);
+
 /* Cooperative cancellation: the next layer boundary of a running or future
- * call returns TF_ERR_CANCELLED (TFETResidentSession.h:5-11). */
+ * call returns TF_ERR_CANCELLED (TFETResidentSession.h:5-11).  A call
+ * cancelled before it dispatched anything leaves the session as it was; one
+ * cancelled between layers invalidates it (below). */
 int tf_session_cancel(tf_session* session);
-/* Clear the cancellation flag and every request's length (beginRequest). */
+
+/* Dispatched failures.  Any failure after a session call has submitted work
+ * (a launch or CUDA error, a cancellation between layers, or a device-side
+ * failure found at a completion point) invalidates the session: the call
+ * waits for the submitted work, returns the error, and every later call but
+ * tf_session_kv / tf_session_get_lengths / tf_session_reset returns
+ * TF_ERR_STATE.  Failures found by the checks before dispatch change nothing.
+ * (TFETResidentSession.mm:388-392 quarantine and :667 failDispatched;
+ * patches/executorch.patch:1486-1499 maps the failure to Error::Internal.)
+ * Device-side failures are: a tensor-core pipeline wait that expired
+ * (TF_ERR_TIMEOUT; the kernel gave up and its outputs are incomplete), an
+ * activation beyond the f16 range reaching a tensor-core operand, and a
+ * token id past the embedding table (both TF_ERR_STATE).  Calls with host
+ * outputs and every prefill check for them before returning; calls with
+ * device outputs do not wait for the device, so their failures surface at
+ * the next such completion point or at tf_session_check. */
+/* Completion point for device-output calls: waits for `stream`, then
+ * reports (and invalidates the session on) a device-side failure since the
+ * last check.  The reference's counterpart is its synchronize_storage +
+ * finite check after submission (TFETResidentSession.mm:1612-1626). */
+int tf_session_check(tf_session* session, void* stream);
+/* Clear the cancellation flag and every request's length (beginRequest),
+ * and re-admit an invalidated session (after waiting for the device and
+ * clearing its device-side error flags). */
 int tf_session_reset(tf_session* session);
+
+/* Test hook: the number of SM clock cycles a tensor-core pipeline wait may
+ * take before the kernel records TF_ERR_TIMEOUT and returns (cycles <= 0
+ * restores the default, about one second), on the calling thread's current
+ * device.  For failure-path tests; no reference counterpart. */
+int tf_set_wait_limit(int64_t cycles);
 
 #ifdef __cplusplus
 }

@@ -415,7 +415,7 @@ def combine(expert_out, gates, residual, act):
     return to_act((f32(residual) + red).astype(np.float32), act)
 
 
-def moe_block(x, residual, router, experts, top_k, act):
+def moe_block(x, residual, router, experts, top_k, act, forced_indices=None):
     """One OLMoE sparse-MoE block; returns (out, aux).
 
     Restates ``NativeGraniteMoEPrefill::moe`` (``MLXNativeGraniteMoEPrefill.h:
@@ -432,6 +432,12 @@ def moe_block(x, residual, router, experts, top_k, act):
     else:
         logits = router_logits_affine(x, *router[1:], act)
     idx, gates = olmoe_route(logits, top_k, act)
+    own = idx
+    if forced_indices is not None:
+        # Follow a given routing (test harness: the device's choices); the
+        # gates are this block's own probabilities at those experts.
+        idx = np.asarray(forced_indices, np.int64).reshape(T, top_k)
+        gates = np.take_along_axis(olmoe_softmax(logits, act), idx, -1)
     E = experts["gate"][0].shape[0]
     order, inverse, offsets = route_sort(idx, E)
     flat = idx.reshape(-1)
@@ -447,7 +453,7 @@ def moe_block(x, residual, router, experts, top_k, act):
     y = y_sorted[inverse].reshape(T, top_k, -1)
     out = combine(y, gates, residual, act)
     aux = dict(logits=logits, indices=idx, gates=gates, order=order,
-               inverse=inverse, offsets=offsets, h_sorted=h, y_sorted=y_sorted)
+               inverse=inverse, offsets=offsets, h_sorted=h, y_sorted=y_sorted, own_indices=own)
     return out, aux
 
 
@@ -546,7 +552,7 @@ class OLMoEConfig:
         return np.float32(self.head_dim ** -0.5)
 
 
-def attention_block(h, layer, cfg, k_cache, v_cache, positions):
+def attention_block(h, layer, cfg, k_cache, v_cache, positions, fast=False):
     """Attention half of one layer for one request (decode or prefill chunk).
 
     h: act [T, H]; k_cache/v_cache: float32 holding f16 values [Hh, cap, D],
@@ -572,12 +578,12 @@ def attention_block(h, layer, cfg, k_cache, v_cache, positions):
     v_cache[:, start:start + T] = round_f16(v.reshape(T, Hh, D).transpose(1, 0, 2))
     L = start + T
     o = sdpa(q, k_cache[:, :L], v_cache[:, :L], cfg.attn_scale, act,
-             causal_offset=start if T > 1 else None)
+             causal_offset=start if T > 1 else None, fast=fast)
     proj = affine_qmm(o.reshape(T, Hh * D), *layer["o"], act)
     return to_act(f32(h) + proj, act)
 
 
-def decode_layer_batched(h, layer, cfg, k_caches, v_caches, positions, fast=False):
+def decode_layer_batched(h, layer, cfg, k_caches, v_caches, positions, fast=False, forced=None, aux_out=None):
     """One layer of batched decode: request b has one new token at absolute
     position positions[b] and its own cache k_caches[b] / v_caches[b]
     ([Hh, cap, D], f16 values, updated in place).  Projections and the MoE
@@ -605,33 +611,52 @@ def decode_layer_batched(h, layer, cfg, k_caches, v_caches, positions, fast=Fals
                     fast=fast).reshape(-1)
     h = to_act(f32(h) + affine_qmm(o, *layer["o"], act), act)
     post = rms_norm(h, layer["post_norm"], cfg.rms_eps, act)
-    out, _ = moe_block(post, h, ("affine",) + tuple(layer["router"]), layer["experts"], cfg.top_k, act)
+    out, aux = moe_block(post, h, ("affine",) + tuple(layer["router"]), layer["experts"], cfg.top_k, act,
+                         forced_indices=forced)
+    if aux_out is not None:
+        aux_out.append(aux)
     return out
 
 
-def layer_forward(h, layer, cfg, k_cache, v_cache, positions):
+def layer_forward(h, layer, cfg, k_cache, v_cache, positions, fast=False, forced=None, aux_out=None,
+                  last_row_only=False):
     """One decoder layer: attention block, post-attention RMSNorm, MoE block.
 
     Restates ``MLXNativeGraniteMoEPrefill.h:433-487`` / ``Layer.forward``
-    (``export_native_olmoe_target.py:225-227``)."""
-    h = attention_block(h, layer, cfg, k_cache, v_cache, positions)
+    (``export_native_olmoe_target.py:225-227``).  ``last_row_only`` keeps
+    the MoE half for the last row (the reference's last layer with T > 1,
+    ``MLXNativeGraniteMoEPrefill.h:440-442, 471``; every row still writes
+    its K/V).  ``forced`` routes the MoE block's rows to given experts."""
+    h = attention_block(h, layer, cfg, k_cache, v_cache, positions, fast=fast)
+    if last_row_only:
+        h = h[-1:]
     post = rms_norm(h, layer["post_norm"], cfg.rms_eps, cfg.act)
-    out, _ = moe_block(post, h, ("affine",) + tuple(layer["router"]), layer["experts"],
-                       cfg.top_k, cfg.act)
+    out, aux = moe_block(post, h, ("affine",) + tuple(layer["router"]), layer["experts"],
+                         cfg.top_k, cfg.act, forced_indices=forced)
+    if aux_out is not None:
+        aux_out.append(aux)
     return out
 
 
-def model_forward(ids, weights, cfg, k_caches, v_caches, start):
+def model_forward(ids, weights, cfg, k_caches, v_caches, start, fast=False, forced=None, aux_out=None):
     """Embedding -> layers -> final RMSNorm on the last row -> lm_head (fp32).
 
     Restates ``NativeGraniteMoEPrefill::run`` (``MLXNativeGraniteMoEPrefill.h:
     347-493``) for one request, without the last-query-only shortcut (which
-    changes no returned value).  Returns fp32 logits [V] (act-rounded)."""
+    changes no returned value).  Returns fp32 logits [V] (act-rounded).
+    ``fast`` selects the float32-BLAS attention (see ``sdpa``) for long
+    sequences.  ``forced`` (a list per layer) routes each layer's MoE rows to
+    given experts; the last layer's entry then holds the last row's experts
+    only and that layer runs its MoE half for the last row, as the reference
+    does.  ``aux_out`` collects each layer's MoE aux (own routing included)."""
     ids = np.asarray(ids).reshape(-1)
     T = ids.size
     positions = np.arange(start, start + T)
     h = affine_embedding(ids, *weights["embed"], cfg.act)
+    n = len(weights["layers"])
     for i, layer in enumerate(weights["layers"]):
-        h = layer_forward(h, layer, cfg, k_caches[i], v_caches[i], positions)
+        h = layer_forward(h, layer, cfg, k_caches[i], v_caches[i], positions, fast=fast,
+                          forced=None if forced is None else forced[i], aux_out=aux_out,
+                          last_row_only=forced is not None and i == n - 1 and T > 1)
     last = rms_norm(h[-1:], weights["final_norm"], cfg.rms_eps, cfg.act)
     return affine_qmm(last, *weights["lm_head"], cfg.act)[0]

@@ -159,6 +159,29 @@ def make_moe(ops, name, seed, T, H, I, E, K, act, dense_router=True):
     return arrays
 
 
+def make_config1(ops):
+    """BASELINE config 1 at full geometry (T=32, H=2048, E=64, K=8, I=1024,
+    bf16, dense bf16 router), composed from the reference's operators as
+    ``MoE.forward`` does.  The inputs are regenerated from a seed at test time
+    (``config1_inputs.py``); the fixture keeps the reference's outputs and a
+    digest of the inputs."""
+    sys.path.insert(0, str(HERE))
+    import config1_inputs as c1
+    x, residual, ex, wr = c1.generate()
+    act = c1.ACT
+    logits_t = (t_act(x, act).float() @ t_act(wr, act).float().T).to(TORCH_ACT[act])
+    logits = oracle.bits_to_act(n_act(logits_t, act), act)
+    ref = reference_moe(ops, x, logits, ex, c1.K, act)
+    layer_out = (t_act(residual, act) + t_act(oracle.bits_to_act(ref["moe"], act), act)).float()
+    arrays = dict(
+        logits=n_act(logits_t, act), probabilities=ref["probabilities"], ids=ref["ids"], scores=ref["scores"],
+        moe=ref["moe"], layer_out=oracle.act_to_bits(layer_out.numpy(), act),
+        digest=np.array(c1.digest(x, residual, ex, wr)),
+        meta=np.array(json.dumps(dict(T=c1.T, H=c1.H, I=c1.I, E=c1.E, K=c1.K, act=act, seed=c1.SEED,
+                                      dense_router=True, sorted=bool(ref["sorted"])))))
+    np.savez_compressed(HERE / "config1_full.npz", **arrays)
+
+
 def make_ops(ops):
     """Single-operator fixtures: dequantize, qmm, gather_qmm (both call forms),
     embedding, softmax/top-k on crafted rows with ties, NaN and +-inf."""
@@ -277,6 +300,8 @@ def main():
     make_moe(ops, "moe_small_sorted_f16", 103, T=40, H=256, I=128, E=16, K=8, act="f16",
              dense_router=False)
     make_attention()
+    # BASELINE config 1 at its full geometry (inputs regenerated from a seed).
+    make_config1(ops)
     stack = prep.self_test()
     (HERE / "prepare_model_selftest.json").write_text(json.dumps(stack, indent=1) + "\n")
     print("golden fixtures written to", HERE)

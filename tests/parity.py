@@ -49,7 +49,7 @@ def assert_close(got, ref, act=None, max_abs=MAX_ABS, mean_rel=MEAN_REL, ulp_act
     return mx, rel
 
 
-def assert_logits_close(got, ref, act, max_abs=MAX_ABS, mean_rel=MEAN_REL):
+def assert_logits_close(got, ref, act, max_abs=MAX_ABS, mean_rel=MEAN_REL, ulps=1):
     """End-to-end logits: max-abs within max(2e-2, 1 act ulp), normalized L1
     error mean|d| / mean|ref| within 5e-3, and identical top-1 token per row.
 
@@ -57,14 +57,19 @@ def assert_logits_close(got, ref, act, max_abs=MAX_ABS, mean_rel=MEAN_REL):
     sides, so small-magnitude logits carry percent-level relative noise that
     the per-element mean-relative bar (meant for one layer's output) would
     over-weight; the normalized L1 error measures the same 5e-3 bar on the
-    vector as a whole."""
+    vector as a whole.
+
+    ``ulps`` widens the per-element bound to that many act ulps for deep
+    models: after 16 layers each side's final fp32 logit carries the
+    accumulated act-dtype roundings of the whole stack, so the single
+    rounding to the act dtype can land one more ulp apart."""
     got = np.asarray(got, np.float64)
     ref = np.asarray(ref, np.float64)
     assert got.shape == ref.shape
     d = np.abs(got - ref)
-    bound = np.maximum(max_abs, act_ulp(ref, act))
-    assert not (d > bound).any(), f"max_abs={d.max():.3e}"
+    bound = np.maximum(max_abs, ulps * act_ulp(ref, act))
     l1 = float(d.mean() / max(np.abs(ref).mean(), 1e-30))
+    assert not (d > bound).any(), f"max_abs={d.max():.3e} normalized_l1={l1:.3e}"
     assert l1 <= mean_rel, f"normalized L1 {l1:.3e}"
     g2 = got.reshape(-1, got.shape[-1])
     r2 = ref.reshape(-1, ref.shape[-1])

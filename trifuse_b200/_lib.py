@@ -102,6 +102,9 @@ SIGNATURES = {
     "tf_session_trace": [P, C.c_int],
     "tf_session_trace_read": [P, C.POINTER(C.c_float), C.POINTER(C.c_int32)],
     "tf_session_reset": [P],
+    "tf_session_check": [P, P],
+    "tf_session_capture_routing": [P, P, C.c_int64],
+    "tf_set_wait_limit": [C.c_int64],
 }
 
 _lib = None

@@ -15,8 +15,11 @@
 //
 //   append  (one block per row)   : norms, ropes, writes q (act) to scratch
 //                                   and k/v (f16) into the cache slot pos[r];
-//   split   (split, head, row)    : kSplit keys -> unnormalised (max, sum, o);
-//   merge   (head, row)           : combines the splits in order.
+//   split   (split, head, query)  : kSplit keys -> unnormalised (max, sum, o);
+//   merge   (head, query)         : combines the splits in order.
+// The queries are every row, or a listed subset (the last row of each
+// request in the last layer of a prefill, MLXNativeGraniteMoEPrefill.h:
+// 440-442, 471), or none (a cache-only chunk's last layer, :470).
 // K/V rows stream with 128-bit loads, a half-warp per 256-byte key row.
 #include <math.h>
 
@@ -102,18 +105,20 @@ __global__ void __launch_bounds__(kAttnThreads)
 template <typename T>
 __global__ void __launch_bounds__(kAttnThreads)
     attn_split_kernel(const T* __restrict__ q, int heads, const int32_t* __restrict__ pos,
-                      const int32_t* __restrict__ req, const __half* __restrict__ k_cache,
-                      const __half* __restrict__ v_cache, int cap, float scale, int nsplit,
-                      float* __restrict__ pm, float* __restrict__ pl, float* __restrict__ po) {
+                      const int32_t* __restrict__ req, const int32_t* __restrict__ qrows,
+                      const __half* __restrict__ k_cache, const __half* __restrict__ v_cache, int cap,
+                      float scale, int nsplit, float* __restrict__ pm, float* __restrict__ pl,
+                      float* __restrict__ po) {
   __shared__ float sc[kSplit];
   __shared__ float red[kAttnThreads / 32];
   __shared__ float opart[kKeyGroups][kHeadDim];
   const int s = blockIdx.x, h = blockIdx.y;
-  const int64_t r = blockIdx.z;
+  const int64_t z = blockIdx.z;                  // output (query) index
+  const int64_t r = qrows ? qrows[z] : z;        // its row among the appended rows
   const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
   const int L = pos[r] + 1;
   const int k0 = s * kSplit;
-  const int64_t part = (r * heads + h) * nsplit + s;
+  const int64_t part = (z * heads + h) * nsplit + s;
   if (k0 >= L) {
     if (t == 0) {
       pm[part] = -INFINITY;
@@ -221,14 +226,15 @@ __global__ void __launch_bounds__(kAttnThreads)
 
 template <typename T>
 __global__ void __launch_bounds__(kHeadDim)
-    attn_merge_kernel(const int32_t* __restrict__ pos, int heads, int nsplit,
+    attn_merge_kernel(const int32_t* __restrict__ pos, const int32_t* __restrict__ qrows, int heads, int nsplit,
                       const float* __restrict__ pm, const float* __restrict__ pl,
                       const float* __restrict__ po, T* __restrict__ out) {
   const int h = blockIdx.x, d = threadIdx.x;
-  const int64_t r = blockIdx.y;
+  const int64_t z = blockIdx.y;
+  const int64_t r = qrows ? qrows[z] : z;
   const int L = pos[r] + 1;
   const int ns = (L + kSplit - 1) / kSplit;
-  const int64_t base = (r * heads + h) * nsplit;
+  const int64_t base = (z * heads + h) * nsplit;
   float M = -INFINITY;
   for (int s = 0; s < ns; ++s) M = fmaxf(M, pm[base + s]);
   float acc = 0.f, l = 0.f;
@@ -237,7 +243,7 @@ __global__ void __launch_bounds__(kHeadDim)
     acc = fmaf(w, po[(base + s) * kHeadDim + d], acc);
     l = fmaf(w, pl[base + s], l);
   }
-  out[r * heads * kHeadDim + h * kHeadDim + d] = from_f<T>(acc / l);
+  out[z * heads * kHeadDim + h * kHeadDim + d] = from_f<T>(acc / l);
 }
 
 // ---------------------------------------------------------------------------
@@ -472,7 +478,11 @@ static tf_status attention_impl(const AttnProblem& a, cudaStream_t s) {
       (const T*)a.qkv, a.heads, (const __half*)a.q_norm, (const __half*)a.k_norm, a.eps, a.theta,
       a.pos, a.req, (__half*)a.k_cache, (__half*)a.v_cache, a.capacity, qr);
   TF_TRY(check_launch("attn_append"));
-  if (a.qblocks && a.nqblocks > 0) {
+  // Queries: every row, or only the rows a.qrows lists (output row i for
+  // a.qrows[i]); none when a.nq == 0 (the rows only extend the cache).
+  const int64_t nq = a.qrows ? a.nq : a.rows;
+  if (nq == 0) return TF_OK;
+  if (a.qblocks && a.nqblocks > 0 && !a.qrows) {
     // Prefill rows grouped per request: tiled tensor-core attention.
     static PerDeviceOnce attr;
     int dev = 0;
@@ -487,14 +497,14 @@ static tf_status attention_impl(const AttnProblem& a, cudaStream_t s) {
         (T*)a.out);
     return check_launch("attn_prefill");
   }
-  dim3 grid(grid_splits, a.heads, (unsigned)a.rows);
-  attn_split_kernel<T><<<grid, kAttnThreads, 0, s>>>(qr, a.heads, a.pos, a.req,
+  dim3 grid(grid_splits, a.heads, (unsigned)nq);
+  attn_split_kernel<T><<<grid, kAttnThreads, 0, s>>>(qr, a.heads, a.pos, a.req, a.qrows,
                                                      (const __half*)a.k_cache,
                                                      (const __half*)a.v_cache, a.capacity, a.scale,
                                                      nsplit, pm, pl, po);
   TF_TRY(check_launch("attn_split"));
-  dim3 mgrid(a.heads, (unsigned)a.rows);
-  attn_merge_kernel<T><<<mgrid, kHeadDim, 0, s>>>(a.pos, a.heads, nsplit, pm, pl, po, (T*)a.out);
+  dim3 mgrid(a.heads, (unsigned)nq);
+  attn_merge_kernel<T><<<mgrid, kHeadDim, 0, s>>>(a.pos, a.qrows, a.heads, nsplit, pm, pl, po, (T*)a.out);
   return check_launch("attn_merge");
 }
 

@@ -94,6 +94,8 @@ int tf_set_qmm_path(int path) {
   return TF_OK;
 }
 
+int tf_set_wait_limit(int64_t cycles) { return set_wait_limit(cycles); }
+
 int tf_device_error(int clear) {
   TF_CUDA(cudaDeviceSynchronize());
   const int tc = read_tc_error(clear != 0);
@@ -340,10 +342,16 @@ struct MoePlan {
   // f16 tensor-core operand: x rows in slot order when gate/up runs on tensor cores, else the
   // f16 copy of h when only the down projection does (never both in one call).
   void* op16;
+  // Split-schedule buffers of the tensor-core QMMs (NULL in the plan without them).
+  float* partials;
+  size_t partial_bytes;
+  int* counters;
   size_t used;
 };
 
-static MoePlan plan_moe(const tf_moe_args* a, void* ws, size_t ws_bytes) {
+// with_split: also carve the tensor-core split buffers (fp32 partials and
+// tile counters) that spread decode-sized expert tiles over every SM.
+static MoePlan plan_moe(const tf_moe_args* a, void* ws, size_t ws_bytes, bool with_split = true) {
   const int64_t T = a->tokens, N = a->tokens * a->top_k;
   const int ab = act_bytes(a->act);
   Carve c(ws, ws_bytes);
@@ -361,6 +369,14 @@ static MoePlan plan_moe(const tf_moe_args* a, void* ws, size_t ws_bytes) {
   p.h = c.take<char>((size_t)N * a->intermediate * ab);
   p.y = c.take<char>((size_t)N * a->hidden * ab);
   p.op16 = c.take<char>((size_t)N * (a->hidden > a->intermediate ? a->hidden : a->intermediate) * 2);
+  p.partials = nullptr;
+  p.partial_bytes = 0;
+  p.counters = nullptr;
+  if (with_split) {
+    p.partial_bytes = qmm_split_partial_bytes();
+    p.partials = c.take<float>(p.partial_bytes);
+    p.counters = c.take<int>((size_t)kQmmSplitCounters * sizeof(int));
+  }
   p.used = c.used;
   return p;
 }
@@ -390,8 +406,13 @@ static tf_status check_moe(const tf_moe_args* a) {
   return TF_OK;
 }
 
-static tf_status run_moe(const tf_moe_args* a, const MoePlan& p, cudaStream_t s) {
+// counters_zero: the caller guarantees the split counters are zero (a
+// session's scratch, zeroed once and left zero by every completed launch);
+// otherwise they are cleared first.
+static tf_status run_moe(const tf_moe_args* a, const MoePlan& p, cudaStream_t s, bool counters_zero = false) {
   const int64_t N = a->tokens * a->top_k;
+  if (p.counters && !counters_zero)
+    TF_CUDA(cudaMemsetAsync(p.counters, 0, (size_t)kQmmSplitCounters * sizeof(int), s));
   trace(PH_ROUTER, true, s);
   TF_TRY(launch_router(a->x, a->tokens, a->hidden, a->router, a->experts, a->top_k, a->act,
                        p.logits, p.idx, p.gates, s));
@@ -416,6 +437,10 @@ static tf_status run_moe(const tf_moe_args* a, const MoePlan& p, cudaStream_t s)
   up.w1 = a->up_proj;
   up.y = p.h;
   up.y_stride = a->intermediate;
+  up.partials = p.partials;
+  up.partial_bytes = p.partial_bytes;
+  up.counters = p.counters;
+  up.counter_cap = p.counters ? kQmmSplitCounters : 0;
   QmmProblem dn = up;
   dn.epilogue = EPI_PLAIN;
   dn.x = p.h;
@@ -459,12 +484,13 @@ static tf_status run_moe(const tf_moe_args* a, const MoePlan& p, cudaStream_t s)
 }  // extern "C"
 
 namespace tf {
-size_t moe_workspace_bytes(const tf_moe_args* a) { return plan_moe(a, nullptr, 0).used; }
-tf_status moe_run(const tf_moe_args* a, void* ws, size_t ws_bytes, cudaStream_t s) {
+size_t moe_workspace_bytes(const tf_moe_args* a, bool with_split) { return plan_moe(a, nullptr, 0, with_split).used; }
+tf_status moe_run(const tf_moe_args* a, void* ws, size_t ws_bytes, cudaStream_t s, bool counters_zero) {
   if (a->tokens == 0) return TF_OK;
-  const MoePlan p = plan_moe(a, ws, ws_bytes);
+  const bool split = plan_moe(a, nullptr, 0, true).used <= ws_bytes;
+  const MoePlan p = plan_moe(a, ws, ws_bytes, split);
   if (p.used > ws_bytes) return set_error(TF_ERR_INVALID_ARGUMENT, "moe: workspace too small");
-  return run_moe(a, p, s);
+  return run_moe(a, p, s, counters_zero);
 }
 }  // namespace tf
 
@@ -479,12 +505,15 @@ int tf_moe_workspace_size(const tf_moe_args* args, size_t* bytes) {
 
 int tf_moe_forward(const tf_moe_args* args, void* workspace, size_t workspace_bytes, void* stream) {
   TF_TRY(check_moe(args));
-  const MoePlan need = plan_moe(args, nullptr, 0);
+  // The reported size includes the split buffers; a workspace of at least the
+  // size without them still runs (every tile then goes to one block).
+  const MoePlan full = plan_moe(args, nullptr, 0, true);
+  const MoePlan need = plan_moe(args, nullptr, 0, false);
   if (workspace_bytes < need.used || (need.used && !workspace))
     return set_error(TF_ERR_INVALID_ARGUMENT, "moe: workspace %zu bytes < required %zu", workspace_bytes,
-                     need.used);
+                     full.used);
   if (args->tokens == 0) return TF_OK;
-  const MoePlan p = plan_moe(args, workspace, workspace_bytes);
+  const MoePlan p = plan_moe(args, workspace, workspace_bytes, workspace_bytes >= full.used);
   return run_moe(args, p, st(stream));
 }
 

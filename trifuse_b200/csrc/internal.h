@@ -159,7 +159,20 @@ struct QmmProblem {
   // EPI_SWIGLU: y is written in f16 in the x16_perm order, as the operand of
   // a following tensor-core QMM.
   int y_f16 = 0;
+  // Optional buffers of the tensor-core split schedule (decode-sized tiles
+  // spread evenly over every SM): fp32 partials of at least
+  // qmm_split_partial_bytes() and counter_cap int counters that are zero when
+  // the launch starts (a completed launch leaves them zero again).  Without
+  // them each block takes whole tiles.
+  float* partials = nullptr;
+  size_t partial_bytes = 0;
+  int* counters = nullptr;
+  int64_t counter_cap = 0;
 };
+// Bytes of fp32 partials the tensor-core split schedule needs on this device.
+size_t qmm_split_partial_bytes();
+// Counters a split QMM over `routes` grouped routes or dense rows can use.
+constexpr int64_t kQmmSplitCounters = 8192;
 // Path launch_qmm would take for this problem (true = tensor cores).
 bool qmm_uses_tc(const QmmProblem& p);
 // f16 copy of n bf16 values (rows of 2048), optionally in the x16_perm order.
@@ -176,9 +189,15 @@ tf_status launch_qmm_tc(const QmmProblem& p, cudaStream_t s);
 // 0 = automatic, 1 = CUDA-core GEMV only, 2 = tensor cores whenever eligible.
 extern int g_qmm_path;
 int read_tc_error(bool clear);
+// Cycles a tensor-core pipeline wait may take (<= 0: the default), current device.
+tf_status set_wait_limit(long long cycles);
 int read_embed_error(bool clear);
 // tokens[r] = all(isfinite(logits[r])) ? argmax (lowest index on ties) : -1.
 tf_status launch_greedy(const float* logits, int64_t rows, int64_t vocab, int64_t* tokens, cudaStream_t s);
+
+// y[i][:] = x[idx[i]][:] for i < n (act rows of `width`, width % 8 == 0).
+tf_status launch_gather_rows(const void* x, int64_t x_stride, const int32_t* idx, int64_t n, int width, int act,
+                             void* y, cudaStream_t s);
 
 // ---------------------------------------------------------------- combine
 tf_status launch_combine(const void* y_sorted, const int32_t* inverse, const void* gates,
@@ -186,9 +205,12 @@ tf_status launch_combine(const void* y_sorted, const int32_t* inverse, const voi
                          void* out, cudaStream_t s);
 
 // ---------------------------------------------------------------- MoE block
-size_t moe_workspace_bytes(const tf_moe_args* a);
-// Runs the block on a workspace of at least moe_workspace_bytes(a).
-tf_status moe_run(const tf_moe_args* a, void* ws, size_t ws_bytes, cudaStream_t s);
+// with_split adds the tensor-core split buffers (about 10 MB).
+size_t moe_workspace_bytes(const tf_moe_args* a, bool with_split = true);
+// Runs the block on a workspace of at least moe_workspace_bytes(a, false),
+// with the split schedule when it holds moe_workspace_bytes(a, true).
+// counters_zero: the workspace's split counters are known to be zero.
+tf_status moe_run(const tf_moe_args* a, void* ws, size_t ws_bytes, cudaStream_t s, bool counters_zero = false);
 
 // ---------------------------------------------------------------- attention
 // Row r (one query token) of request req[r] (r when req == NULL) at absolute
@@ -219,6 +241,10 @@ struct AttnProblem {
   // tiled tensor-core kernel instead of the per-row split-K one.
   const int4* qblocks = nullptr;
   int nqblocks = 0;
+  // Optional: attend only the rows qrows[0..nq) (device), writing output row
+  // i for qrows[i]; every row is still appended.  nq == 0: append only.
+  const int32_t* qrows = nullptr;
+  int64_t nq = 0;
 };
 size_t attention_ws_bytes(int64_t rows, int heads, int capacity, int act);
 tf_status launch_attention(const AttnProblem& a, cudaStream_t s);

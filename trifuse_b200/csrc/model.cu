@@ -141,6 +141,7 @@ struct tf_session {
   void* qkv = nullptr;
   void* attn = nullptr;
   void* x16 = nullptr;  // f16 operand copy (bf16 models, tensor-core projections)
+  void* hc = nullptr;   // [max_batch][H] residual rows of the last layer's queries (prefill)
   int64_t* ids = nullptr;
   int32_t* pos = nullptr;
   int32_t* req = nullptr;
@@ -152,8 +153,21 @@ struct tf_session {
   size_t attn_ws_bytes = 0;
   void* moe_ws = nullptr;
   size_t moe_ws_bytes = 0;
+  // Split-schedule buffers of the dense tensor-core projections (the MoE
+  // block carries its own inside moe_ws); counters zeroed at creation and
+  // on reset, left zero by every completed launch.
+  float* split_partials = nullptr;
+  int* split_counters = nullptr;
   std::atomic<int> cancelled{0};
+  // Set by a failure after work was dispatched (a launch or CUDA error, a
+  // cancellation between layers, or a device-side error found at a
+  // completion point); every call but reset is refused while it is set.
+  bool invalid = false;
   bool tracing = false;
+  // Diagnostic routing capture (tf_session_capture_routing): each layer's
+  // top-k expert ids of a forward land at route_capture + layer * rows * k.
+  int32_t* route_capture = nullptr;
+  int64_t route_capture_rows = 0;
   SessionTracer tracer;
   // Decode steps as CUDA graphs, one per (batch, with logits, attention
   // splits of 256 keys, QMM path): the first step of a shape runs eagerly,
@@ -204,6 +218,36 @@ tf_status validate_config(const tf_olmoe_config* c) {
   if (c->experts > 64 || c->top_k > 32) return set_error(TF_ERR_UNSUPPORTED, "experts <= 64, top_k <= 32");
   if (!act_ok(c->act)) return set_error(TF_ERR_INVALID_ARGUMENT, "activation dtype must be f16 or bf16");
   return TF_OK;
+}
+
+// Device-side failures recorded since the last check, as a status: an
+// expired tensor-core pipeline wait (codes 11-51), an activation beyond the
+// f16 range reaching a tensor-core operand (5), a token id past the
+// embedding table (6).  Clears the flags.  The stream has been synchronized.
+tf_status device_status() {
+  const int tc = read_tc_error(true);
+  const int emb = read_embed_error(true);
+  if (tc >= 11)
+    return set_error(TF_ERR_TIMEOUT, "a tensor-core pipeline wait expired (device code %d); results are incomplete", tc);
+  if (tc == 5)
+    return set_error(TF_ERR_STATE, "an activation beyond the f16 range reached a tensor-core operand (device code 5)");
+  if (tc) return set_error(TF_ERR_STATE, "device error code %d", tc);
+  if (emb == 6) return set_error(TF_ERR_STATE, "a token id past the embedding table was read as row 0 (device code 6)");
+  return TF_OK;
+}
+
+// A failure after dispatch invalidates the session until tf_session_reset,
+// after the submitted work drained (TFETResidentSession.mm:388-392 quarantine,
+// failDispatched at :667; patches/executorch.patch:1486-1499 maps the error).
+tf_status invalidate(tf_session* s, tf_status rc, cudaStream_t st) {
+  s->invalid = true;
+  cudaStreamSynchronize(st);
+  if (s->gstream) cudaStreamSynchronize(s->gstream);
+  return rc;
+}
+
+tf_status refuse_invalid(const tf_session* s) {
+  return set_error(TF_ERR_STATE, "Resident session is invalid after a dispatched failure; tf_session_reset re-admits it");
 }
 
 }  // namespace
@@ -383,6 +427,7 @@ int tf_session_create(tf_model* model, int32_t max_batch, int32_t capacity, int3
     s->qkv = k.take<char>((size_t)R * (W + 2 * Wkv) * 2);
     s->attn = k.take<char>((size_t)R * W * 2);
     s->x16 = k.take<char>((size_t)R * (H > W ? H : W) * 2);
+    s->hc = k.take<char>((size_t)max_batch * H * 2);
     s->ids = k.take<int64_t>((size_t)R * 8);
     s->pos = k.take<int32_t>((size_t)R * 4);
     s->req = k.take<int32_t>((size_t)R * 4);
@@ -392,6 +437,8 @@ int tf_session_create(tf_model* model, int32_t max_batch, int32_t capacity, int3
     s->qblocks = k.take<int4>((size_t)(R / 64 + max_batch + 1) * sizeof(int4));
     s->attn_ws = k.take<char>(s->attn_ws_bytes);
     s->moe_ws = k.take<char>(s->moe_ws_bytes);
+    s->split_partials = k.take<float>(qmm_split_partial_bytes());
+    s->split_counters = k.take<int>((size_t)kQmmSplitCounters * sizeof(int));
   };
   plan(cv);
   DeviceGuard g(model->device);
@@ -409,6 +456,14 @@ int tf_session_create(tf_model* model, int32_t max_batch, int32_t capacity, int3
   }
   Carve real(s->scratch, cv.used);
   plan(real);
+  // The split counters (in moe_ws and split_counters) start at zero.
+  e = cudaMemset(s->scratch, 0, cv.used);
+  if (e != cudaSuccess) {
+    cudaFree(s->kv);
+    cudaFree(s->scratch);
+    delete s;
+    return set_error(TF_ERR_CUDA, "session scratch clear: %s", cudaGetErrorString(e));
+  }
   for (int l = 0; l < c.layers; ++l) {
     s->k.push_back(s->kv + per_cache * (2 * l));
     s->v.push_back(s->kv + per_cache * (2 * l + 1));
@@ -470,9 +525,31 @@ int tf_session_cancel(tf_session* s) {
 
 int tf_session_reset(tf_session* s) {
   if (!s) return set_error(TF_ERR_INVALID_ARGUMENT, "session is NULL");
+  DeviceGuard g(s->m->device);
+  if (s->invalid) {
+    // After a dispatched failure: wait for the device, clear its error flags
+    // and the split counters a stopped launch may have left behind.
+    TF_CUDA(cudaDeviceSynchronize());
+    read_tc_error(true);
+    read_embed_error(true);
+    TF_CUDA(cudaMemset(s->moe_ws, 0, s->moe_ws_bytes));
+    TF_CUDA(cudaMemset(s->split_counters, 0, (size_t)kQmmSplitCounters * sizeof(int)));
+    s->invalid = false;
+  }
   s->cancelled.store(0);
   for (auto& l : s->lengths) l = 0;
   return TF_OK;
+}
+
+int tf_session_check(tf_session* s, void* stream) {
+  if (!s) return set_error(TF_ERR_INVALID_ARGUMENT, "session is NULL");
+  if (s->invalid) return refuse_invalid(s);
+  DeviceGuard g(s->m->device);
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const cudaError_t e = cudaStreamSynchronize(st);
+  if (e != cudaSuccess) return invalidate(s, set_error(TF_ERR_CUDA, "session check: %s", cudaGetErrorString(e)), st);
+  const tf_status rc = device_status();
+  return rc == TF_OK ? TF_OK : invalidate(s, rc, st);
 }
 
 }  // extern "C"
@@ -483,6 +560,10 @@ namespace {
 // rows are first copied to f16 (the MMA operand dtype) in the tensor-core
 // operand order.  f16 activations are read in place.
 tf_status dense_qmm(tf_session* s, QmmProblem& q, int64_t x_rows, cudaStream_t st) {
+  q.partials = s->split_partials;
+  q.partial_bytes = qmm_split_partial_bytes();
+  q.counters = s->split_counters;
+  q.counter_cap = kQmmSplitCounters;
   if (q.act == TF_DTYPE_BF16 && qmm_uses_tc(q)) {
     TF_TRY(launch_bf16_to_f16(q.x, x_rows * q.x_stride, s->x16, 1, st));
     q.x16 = s->x16;
@@ -494,8 +575,15 @@ tf_status dense_qmm(tf_session* s, QmmProblem& q, int64_t x_rows, cudaStream_t s
 // Forward `rows` token rows through every layer.  Inputs already on device:
 // s->ids [rows], s->pos [rows], s->req [rows] (or identity when req_ident).
 // Leaves the final hidden states in s->h0.
+//
+// Prefill (`last` = the nlast device rows that end a request, fewer than
+// `rows`): as the reference, the last layer appends K/V of every row but
+// runs attention, o-proj and the MoE block only for those rows
+// (MLXNativeGraniteMoEPrefill.h:440-442, 471), leaving their hidden states
+// compact in s->h0 rows 0..nlast-1; a cache-only call (`cache_only`) stops
+// after that layer's K/V write (:470).
 tf_status forward_rows(tf_session* s, int64_t rows, bool req_ident, int max_len, cudaStream_t st,
-                       int nqblocks = 0) {
+                       int nqblocks = 0, const int32_t* last = nullptr, int nlast = 0, bool cache_only = false) {
   const tf_model* m = s->m;
   const tf_olmoe_config& c = m->c;
   const int H = c.hidden, W = c.heads * c.head_dim;
@@ -506,6 +594,8 @@ tf_status forward_rows(tf_session* s, int64_t rows, bool req_ident, int max_len,
   for (int l = 0; l < c.layers; ++l) {
     if (s->cancelled.load()) return set_error(TF_ERR_CANCELLED, "cancelled before layer %d", l);
     const LayerW& L = m->layers[l];
+    // Last layer of a prefill: queries of the requests' last rows only.
+    const bool lq = last && nlast < rows && l == c.layers - 1;
     trace(PH_INPUT_NORM, true, st);
     TF_TRY(launch_rms_norm(s->h0, rows, H, L.input_norm, c.rms_eps, c.act, s->xn, st));
     trace(PH_INPUT_NORM, false, st);
@@ -543,32 +633,44 @@ tf_status forward_rows(tf_session* s, int64_t rows, bool req_ident, int max_len,
     a.ws_bytes = s->attn_ws_bytes;
     a.qblocks = nqblocks ? s->qblocks : nullptr;
     a.nqblocks = nqblocks;
+    int64_t n = rows;  // rows past the attention
+    if (lq) {
+      a.qrows = last;
+      a.nq = cache_only ? 0 : nlast;
+      n = a.nq;
+    }
     trace(PH_ATTENTION, true, st);
     TF_TRY(launch_attention(a, st));
     trace(PH_ATTENTION, false, st);
+    if (lq && cache_only) break;
+    const void* resid = s->h0;
+    if (lq) {
+      TF_TRY(launch_gather_rows(s->h0, H, last, nlast, H, c.act, s->hc, st));
+      resid = s->hc;
+    }
     QmmProblem o;
     o.mode = QMM_DENSE;
     o.epilogue = EPI_RESIDUAL;
     o.act = c.act;
     o.x = s->attn;
     o.x_stride = W;
-    o.n = rows;
+    o.n = n;
     o.w0 = L.o;
     o.y = s->h1;
     o.y_stride = H;
-    o.residual = s->h0;
+    o.residual = resid;
     o.residual_stride = H;
     trace(PH_O_PROJ, true, st);
-    TF_TRY(dense_qmm(s, o, rows, st));
+    TF_TRY(dense_qmm(s, o, n, st));
     trace(PH_O_PROJ, false, st);
     trace(PH_POST_NORM, true, st);
-    TF_TRY(launch_rms_norm(s->h1, rows, H, L.post_norm, c.rms_eps, c.act, s->xn, st));
+    TF_TRY(launch_rms_norm(s->h1, n, H, L.post_norm, c.rms_eps, c.act, s->xn, st));
     trace(PH_POST_NORM, false, st);
     tf_moe_args ma{};
     ma.x = s->xn;
     ma.residual = s->h1;
     ma.out = s->h0;
-    ma.tokens = rows;
+    ma.tokens = n;
     ma.hidden = H;
     ma.intermediate = c.intermediate;
     ma.experts = c.experts;
@@ -579,7 +681,9 @@ tf_status forward_rows(tf_session* s, int64_t rows, bool req_ident, int max_len,
     ma.gate_proj = L.gate;
     ma.up_proj = L.up;
     ma.down_proj = L.down;
-    TF_TRY(moe_run(&ma, s->moe_ws, s->moe_ws_bytes, st));
+    if (s->route_capture && rows <= s->route_capture_rows)
+      ma.indices = s->route_capture + (size_t)l * rows * c.top_k;
+    TF_TRY(moe_run(&ma, s->moe_ws, s->moe_ws_bytes, st, /*counters_zero=*/true));
   }
   return TF_OK;
 }
@@ -618,8 +722,10 @@ namespace {
 // Shared body of the decode entry points: checks, input copies, the layer
 // stack and (when `head`) the final norm + lm_head into s->logits.
 tf_status decode_step(tf_session* s, const int64_t* token_ids, const int32_t* positions, int32_t batch, int flags,
-                      bool head, cudaStream_t st) {
+                      bool head, cudaStream_t st, bool* dispatched) {
+  *dispatched = false;
   if (!s || !token_ids) return set_error(TF_ERR_INVALID_ARGUMENT, "decode: NULL argument");
+  if (s->invalid) return refuse_invalid(s);
   if (batch <= 0 || batch > s->max_batch)
     return set_error(TF_ERR_INVALID_ARGUMENT, "decode: batch %d outside [1, %d]", batch, s->max_batch);
   if (s->cancelled.load()) return set_error(TF_ERR_CANCELLED, "session cancelled");
@@ -637,10 +743,11 @@ tf_status decode_step(tf_session* s, const int64_t* token_ids, const int32_t* po
       return set_error(TF_ERR_INVALID_ARGUMENT, "token id %lld of request %d outside the vocabulary",
                        (long long)token_ids[b], b);
   }
+  *dispatched = true;
   TF_CUDA(cudaMemcpyAsync(s->ids, token_ids, (size_t)batch * 8,
                           (flags & TF_HOST_INPUTS) ? cudaMemcpyHostToDevice : cudaMemcpyDeviceToDevice, st));
   TF_CUDA(cudaMemcpyAsync(s->pos, pos.data(), (size_t)batch * 4, cudaMemcpyHostToDevice, st));
-  if (s->graphs_on && !s->tracing) {
+  if (s->graphs_on && !s->tracing && !s->route_capture) {
     const int splits = (max_len + 255) / 256;
     tf_session::DecodeGraph& gr = s->graphs[std::make_tuple(batch, head ? 1 : 0, splits, g_qmm_path)];
     if (gr.exec || gr.eager_runs > 0) {
@@ -685,6 +792,36 @@ tf_status decode_step(tf_session* s, const int64_t* token_ids, const int32_t* po
   return TF_OK;
 }
 
+// The dispatched part of tf_session_prefill: input copies, the layer stack,
+// the head, and the final synchronization (the host vectors are pageable),
+// which is also the call's completion point for device-side failures.
+tf_status prefill_dispatch(tf_session* s, int64_t rows, const int64_t* token_ids, int flags,
+                           const std::vector<int32_t>& pos, const std::vector<int32_t>& req,
+                           const std::vector<int32_t>& last, const std::vector<int4>& qb, int max_len,
+                           int num_requests, float* last_logits, cudaStream_t st) {
+  const tf_olmoe_config& c = s->m->c;
+  TF_CUDA(cudaMemcpyAsync(s->ids, token_ids, (size_t)rows * 8,
+                          (flags & TF_HOST_INPUTS) ? cudaMemcpyHostToDevice : cudaMemcpyDeviceToDevice, st));
+  TF_CUDA(cudaMemcpyAsync(s->pos, pos.data(), (size_t)rows * 4, cudaMemcpyHostToDevice, st));
+  TF_CUDA(cudaMemcpyAsync(s->req, req.data(), (size_t)rows * 4, cudaMemcpyHostToDevice, st));
+  TF_CUDA(cudaMemcpyAsync(s->last_rows, last.data(), (size_t)num_requests * 4, cudaMemcpyHostToDevice, st));
+  TF_CUDA(cudaMemcpyAsync(s->qblocks, qb.data(), qb.size() * sizeof(int4), cudaMemcpyHostToDevice, st));
+  TF_TRY(forward_rows(s, rows, false, max_len, st, (int)qb.size(), s->last_rows, num_requests,
+                      last_logits == nullptr));
+  if (last_logits) {
+    // With fewer requests than rows the last layer left each request's final
+    // hidden state compact in rows 0..num_requests-1.
+    if (num_requests < rows)
+      TF_TRY(head_rows(s, num_requests, nullptr, num_requests, st));
+    else
+      TF_TRY(head_rows(s, rows, s->last_rows, num_requests, st));
+    TF_CUDA(cudaMemcpyAsync(last_logits, s->logits, (size_t)num_requests * c.vocab * 4,
+                            (flags & TF_HOST_OUTPUT) ? cudaMemcpyDeviceToHost : cudaMemcpyDeviceToDevice, st));
+  }
+  TF_CUDA(cudaStreamSynchronize(st));
+  return device_status();
+}
+
 }  // namespace
 
 extern "C" {
@@ -694,11 +831,21 @@ int tf_session_decode(tf_session* s, const int64_t* token_ids, const int32_t* po
   DeviceGuard g(s ? s->m->device : 0);
   TraceScope ts(s && s->tracing ? &s->tracer : nullptr);
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  TF_TRY(decode_step(s, token_ids, positions, batch, flags, logits != nullptr, st));
+  bool dispatched = false;
+  tf_status rc = decode_step(s, token_ids, positions, batch, flags, logits != nullptr, st, &dispatched);
+  if (rc != TF_OK) return dispatched ? invalidate(s, rc, st) : rc;
   if (logits) {
-    TF_CUDA(cudaMemcpyAsync(logits, s->logits, (size_t)batch * s->m->c.vocab * 4,
-                            (flags & TF_HOST_OUTPUT) ? cudaMemcpyDeviceToHost : cudaMemcpyDeviceToDevice, st));
-    if (flags & TF_HOST_OUTPUT) TF_CUDA(cudaStreamSynchronize(st));
+    const cudaError_t e = cudaMemcpyAsync(logits, s->logits, (size_t)batch * s->m->c.vocab * 4,
+                                          (flags & TF_HOST_OUTPUT) ? cudaMemcpyDeviceToHost : cudaMemcpyDeviceToDevice,
+                                          st);
+    if (e != cudaSuccess) return invalidate(s, set_error(TF_ERR_CUDA, "decode logits copy: %s", cudaGetErrorString(e)), st);
+    if (flags & TF_HOST_OUTPUT) {
+      // A host-visible completion point: device-side failures surface here.
+      const cudaError_t w = cudaStreamSynchronize(st);
+      if (w != cudaSuccess) return invalidate(s, set_error(TF_ERR_CUDA, "decode: %s", cudaGetErrorString(w)), st);
+      rc = device_status();
+      if (rc != TF_OK) return invalidate(s, rc, st);
+    }
   }
   for (int b = 0; b < batch; ++b) s->lengths[b] += 1;
   return TF_OK;
@@ -710,16 +857,25 @@ int tf_session_decode_greedy(tf_session* s, const int64_t* token_ids, const int3
   DeviceGuard g(s ? s->m->device : 0);
   TraceScope ts(s && s->tracing ? &s->tracer : nullptr);
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  TF_TRY(decode_step(s, token_ids, positions, batch, flags, true, st));
+  bool dispatched = false;
+  tf_status rc = decode_step(s, token_ids, positions, batch, flags, true, st, &dispatched);
+  if (rc != TF_OK) return dispatched ? invalidate(s, rc, st) : rc;
   const int64_t vocab = s->m->c.vocab;
   const bool host_out = (flags & TF_HOST_OUTPUT) != 0;
-  TF_TRY(launch_greedy(s->logits, batch, vocab, host_out ? s->greedy : tokens, st));
+  rc = launch_greedy(s->logits, batch, vocab, host_out ? s->greedy : tokens, st);
+  if (rc != TF_OK) return invalidate(s, rc, st);
+  cudaError_t e = cudaSuccess;
   if (logits)
-    TF_CUDA(cudaMemcpyAsync(logits, s->logits, (size_t)batch * vocab * 4,
-                            host_out ? cudaMemcpyDeviceToHost : cudaMemcpyDeviceToDevice, st));
+    e = cudaMemcpyAsync(logits, s->logits, (size_t)batch * vocab * 4,
+                        host_out ? cudaMemcpyDeviceToHost : cudaMemcpyDeviceToDevice, st);
+  if (e == cudaSuccess && host_out) {
+    e = cudaMemcpyAsync(tokens, s->greedy, (size_t)batch * 8, cudaMemcpyDeviceToHost, st);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  }
+  if (e != cudaSuccess) return invalidate(s, set_error(TF_ERR_CUDA, "greedy decode: %s", cudaGetErrorString(e)), st);
   if (host_out) {
-    TF_CUDA(cudaMemcpyAsync(tokens, s->greedy, (size_t)batch * 8, cudaMemcpyDeviceToHost, st));
-    TF_CUDA(cudaStreamSynchronize(st));
+    rc = device_status();
+    if (rc != TF_OK) return invalidate(s, rc, st);
   }
   for (int b = 0; b < batch; ++b) s->lengths[b] += 1;
   return TF_OK;
@@ -729,6 +885,7 @@ int tf_session_prefill(tf_session* s, const int32_t* requests, const int32_t* to
                        const int64_t* token_ids, float* last_logits, int flags, void* stream) {
   if (!s || !requests || !token_counts || !token_ids)
     return set_error(TF_ERR_INVALID_ARGUMENT, "prefill: NULL argument");
+  if (s->invalid) return refuse_invalid(s);
   if (num_requests <= 0 || num_requests > s->max_batch)
     return set_error(TF_ERR_INVALID_ARGUMENT, "prefill: %d requests outside [1, %d]", num_requests, s->max_batch);
   if (s->cancelled.load()) return set_error(TF_ERR_CANCELLED, "session cancelled");
@@ -766,20 +923,10 @@ int tf_session_prefill(tf_session* s, const int32_t* requests, const int32_t* to
   DeviceGuard g(s->m->device);
   TraceScope ts(s->tracing ? &s->tracer : nullptr);
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  TF_CUDA(cudaMemcpyAsync(s->ids, token_ids, (size_t)rows * 8,
-                          (flags & TF_HOST_INPUTS) ? cudaMemcpyHostToDevice : cudaMemcpyDeviceToDevice, st));
-  TF_CUDA(cudaMemcpyAsync(s->pos, pos.data(), (size_t)rows * 4, cudaMemcpyHostToDevice, st));
-  TF_CUDA(cudaMemcpyAsync(s->req, req.data(), (size_t)rows * 4, cudaMemcpyHostToDevice, st));
-  TF_CUDA(cudaMemcpyAsync(s->last_rows, last.data(), (size_t)num_requests * 4, cudaMemcpyHostToDevice, st));
-  TF_CUDA(cudaMemcpyAsync(s->qblocks, qb.data(), qb.size() * sizeof(int4), cudaMemcpyHostToDevice, st));
-  TF_TRY(forward_rows(s, rows, false, max_len, st, (int)qb.size()));
-  if (last_logits) {
-    TF_TRY(head_rows(s, rows, s->last_rows, num_requests, st));
-    TF_CUDA(cudaMemcpyAsync(last_logits, s->logits, (size_t)num_requests * c.vocab * 4,
-                            (flags & TF_HOST_OUTPUT) ? cudaMemcpyDeviceToHost : cudaMemcpyDeviceToDevice, st));
-  }
-  // The host vectors above are pageable; make sure the copies finished.
-  TF_CUDA(cudaStreamSynchronize(st));
+  const tf_status rc = prefill_dispatch(s, rows, token_ids, flags, pos, req, last, qb, max_len, num_requests,
+                                        last_logits, st);
+  // Everything after the first copy counts as dispatched.
+  if (rc != TF_OK) return invalidate(s, rc, st);
   for (int i = 0; i < num_requests; ++i) s->lengths[requests[i]] += token_counts[i];
   return TF_OK;
 }
@@ -827,6 +974,14 @@ int tf_session_graphs(tf_session* s, int enable) {
   if (enable && (!s->gstream || !s->ev_in || !s->ev_out))
     return set_error(TF_ERR_UNSUPPORTED, "graph stream/events could not be created");
   s->graphs_on = enable != 0;
+  return TF_OK;
+}
+
+int tf_session_capture_routing(tf_session* s, int32_t* indices, int64_t max_rows) {
+  if (!s) return set_error(TF_ERR_INVALID_ARGUMENT, "session is NULL");
+  if (indices && max_rows <= 0) return set_error(TF_ERR_INVALID_ARGUMENT, "capture: max_rows must be positive");
+  s->route_capture = indices;
+  s->route_capture_rows = indices ? max_rows : 0;
   return TF_OK;
 }
 

@@ -14,7 +14,12 @@
 // the array's name is only a host-side stand-in, so its device address is
 // looked up once per device (cudaGetSymbolAddress with that device current)
 // on the first call made on that device, and passed to the kernels.  Make
-// that first call before any stream capture.
+// that first call before any stream capture.  The address is kept for the
+// life of the process: after a device reset the module (and the array) may
+// load elsewhere, so this entry must not be used across one.  With lazy
+// module loading the first call per device and batch shape may load kernel
+// modules (the driver allocates for them); a warm-up call, or
+// CUDA_MODULE_LOADING=EAGER, moves that out of the caller's critical path.
 //
 // Every call shares the one buffer and leaves its contents behind; nothing
 // in it has to start at zero, because each call writes every scratch byte
@@ -62,6 +67,9 @@ extern "C" int tf_moe_forward_noalloc(const tf_moe_args* args, void* stream) {
   size_t need = 0;
   // Same admission as tf_moe_forward (geometry, dtypes, pointers).
   TF_TRY((tf_status)tf_moe_workspace_size(args, &need));
+  // This entry runs without the tensor-core split buffers (each tile on one
+  // block), so it needs only the block's own scratch.
+  need = tf::moe_workspace_bytes(args, false);
   if (args->tokens > TF_MOE_NOALLOC_MAX_TOKENS)
     return tf::set_error(TF_ERR_CAPACITY,
                          "tf_moe_forward_noalloc: %lld tokens exceed the fixed buffer's limit of %d; "

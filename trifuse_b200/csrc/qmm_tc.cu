@@ -69,37 +69,51 @@
 namespace tf {
 
 __device__ int g_tc_error = 0;  // first error code recorded by a bounded wait
+// Cycles a pipeline wait may take before the kernel gives up (about one
+// second of SM clock; tf_set_wait_limit shortens it for failure tests).
+__device__ long long g_wait_cycles = 2000000000LL;
 
 namespace tc {
 
-// Warp roles of a block with G dequant groups.  G = 2 (prefill tiles): one
-// block per SM owning all of tensor memory.  G = 1 (decode tiles): two
-// blocks per SM, 256 TMEM columns each, so two MMA issuers run side by side
-// (a small-N MMA is issue-bound, about 50 cycles per instruction).
-template <int G>
+// Warp roles of a block with G dequant groups of 4 warps (one warp per TMEM
+// lane quarter; groups take alternate stages, so while one group waits on a
+// barrier or a shared load the others dequantize).  BPS blocks share an SM:
+// decode expert tiles run two blocks per SM with 256 TMEM columns each, so two
+// MMA issuers run side by side (a small-N MMA is issue-bound, about 50 cycles
+// per instruction); dense decode projections and prefill run one block per
+// SM owning all 512 columns.
+template <int G, int BPS>
 struct Roles {
-  static constexpr int kDeqGroups = G;                 // dequant groups take alternate stages
-  static constexpr int kDeqWarps = 8 * G;              // 8 warps cover one stage
+  static constexpr int kDeqGroups = G;
+  static constexpr int kDeqWarps = 4 * G;
   static constexpr int kEpiWarps = 4;
   static constexpr int kLoadWarp = kDeqWarps + kEpiWarps;  // packed codes + scales
   static constexpr int kMmaWarp = kLoadWarp + 1;
   static constexpr int kActWarp = kMmaWarp + 1;            // activation tiles
-  static constexpr int kThreads = (kActWarp + 1) * 32;     // 480 or 736
-  static constexpr int kBlocksPerSM = G == 1 ? 2 : 1;
-  static constexpr uint32_t kTmemCols = G == 1 ? 256 : 512;
+  static constexpr int kThreads = (kActWarp + 1) * 32;
+  static constexpr int kBlocksPerSM = BPS;
+  static constexpr uint32_t kTmemCols = BPS == 2 ? 256 : 512;
 };
 constexpr int kM = 128;
 constexpr int kKStep = 64;
-constexpr int kSK = 8;          // k-steps per scale slot (16 bytes of f16 per row)
-constexpr int kMaxTiles = 256;  // per-block tile table
+constexpr int kSK = 8;          // k-steps per scale slot (16 bytes of f16 per row) = one work chunk
+constexpr int kMaxSegs = 128;   // per-block segment table
+constexpr int kMaxExperts = 256;
 constexpr int kACols = kKStep / 2;   // TMEM columns of one k-step of A (two f16 per column)
-constexpr long long kWaitCycles = 2000000000LL;
+// Fixed limit of the waits that drain a block's own copies and MMAs before
+// it exits (not shortened by tf_set_wait_limit: copies in flight always land).
+constexpr long long kDrainCycles = 2000000000LL;
 // try_wait suspends the thread until the phase completes or this many ns
 // pass, so a waiting role takes no issue slots from the dequant warps.
 constexpr uint32_t kSuspendNs = 1000000;
 
-struct TileInfo {
+// A block's work item: chunks [kc0, kc1) (a chunk is kSK k-steps) of one
+// tile (expert e, token slots s0 .. s0 + cnt, row block rb).  `whole`
+// segments cover every chunk of the tile; the others are parts of a tile
+// split across consecutive blocks (split schedule) and meet in the fixup.
+struct Seg {
   int e, s0, cnt, rb;
+  int kc0, kc1, tile, whole;
 };
 
 struct Params {
@@ -115,12 +129,18 @@ struct Params {
   int out;  // rows per expert (per matrix)
   int in;
   int64_t n;  // slots (= activation rows)
-  int64_t tiles_bound;
   void* y;
   int64_t y_stride;
   int y_f16;
   const void* residual;
   int64_t residual_stride;
+  // Split schedule (stream-K over chunks): each block takes an equal run of
+  // the (tile, chunk) sequence; a tile split across blocks is finished by
+  // the last of them to arrive (counters[tile], zero at launch and left zero)
+  // from fp32 partials in `partials` (two slots of 128 x NT per block).
+  int split;
+  float* partials;
+  int* counters;
 };
 
 __device__ __forceinline__ uint32_t smem_addr(const void* p) {
@@ -136,35 +156,56 @@ __device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)), "r"(bytes)
                : "memory");
 }
-__device__ __forceinline__ bool mbar_try(uint64_t* bar, uint32_t parity) {
+__device__ __forceinline__ bool mbar_try(uint64_t* bar, uint32_t parity, uint32_t suspend_ns = kSuspendNs) {
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
       "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(ok)
-      : "r"(smem_addr(bar)), "r"(parity), "r"(kSuspendNs)
+      : "r"(smem_addr(bar)), "r"(parity), "r"(suspend_ns)
       : "memory");
   return ok != 0;
 }
+// Shared-memory wait control of a block: the abort flag every role polls,
+// and the limit and suspend hint of its bounded waits (a test limit below
+// the default polls without suspending, so it can expire).
+struct WaitCtl {
+  volatile int abort;
+  uint32_t suspend_ns;
+  long long limit;
+};
 // Bounded wait; false when the phase did not complete in time or another
-// role already gave up (*abort set).
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort, int code) {
-  if (mbar_try(bar, parity)) return true;
+// role already gave up (abort set).
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, WaitCtl* w, int code) {
+  const uint32_t susp = w->suspend_ns;
+  if (mbar_try(bar, parity, susp)) return true;
   const long long t0 = clock64();
-  while (!mbar_try(bar, parity)) {
-    if (*abort) return false;
-    if (clock64() - t0 > kWaitCycles) {
+  const long long limit = w->limit;
+  while (!mbar_try(bar, parity, susp)) {
+    if (w->abort) return false;
+    if (clock64() - t0 > limit) {
       atomicCAS(&g_tc_error, 0, code);
-      *abort = 1;
+      w->abort = 1;
       return false;
     }
   }
   return true;
 }
+// Wait for a phase that is known to complete (a block's own TMA copy or
+// MMA commit) before the block exits, ignoring the abort flag; fixed limit.
+__device__ __forceinline__ void mbar_drain(uint64_t* bar, uint32_t parity) {
+  if (mbar_try(bar, parity)) return;
+  const long long t0 = clock64();
+  while (!mbar_try(bar, parity))
+    if (clock64() - t0 > kDrainCycles) {
+      atomicCAS(&g_tc_error, 0, 51);
+      return;
+    }
+}
 // Warp-uniform bounded wait (every lane waits; all agree on the result).
-__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volatile int* abort, int code) {
-  return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort, code));
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, WaitCtl* w, int code) {
+  return __all_sync(0xffffffffu, mbar_wait(bar, parity, w, code));
 }
 __device__ __forceinline__ void tma_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
   asm volatile(
@@ -305,60 +346,24 @@ __host__ __device__ __forceinline__ int perm_col(int f) {
   return (f & ~7) | ((q & 3) << 1) | (q >> 2);
 }
 
-// Tile t -> (expert, first slot, token count, row block); e = -1 past the end.
-// Must be called by a full warp (grouped lookup scans 32 experts per round).
-__device__ TileInfo lookup_tile(const Params& p, int64_t t, int nt, int lane) {
-  TileInfo ti{-1, 0, 0, (int)(t % p.row_blocks)};
-  const int64_t tblock = t / p.row_blocks;
-  if (!p.grouped) {
-    const int64_t nblk = (p.n + nt - 1) / nt;
-    if (tblock < nblk) {
-      ti.e = 0;
-      ti.s0 = (int)(tblock * nt);
-      ti.cnt = (int)((p.n - ti.s0) < (int64_t)nt ? (p.n - ti.s0) : (int64_t)nt);
-    }
-    return ti;
-  }
-  const int na = *p.active_count;
-  int64_t base = 0;
-  for (int c0 = 0; c0 < na && ti.e < 0; c0 += 32) {
-    const int i = c0 + lane;
-    int ex = -1, lo = 0, hi = 0;
-    if (i < na) {
-      ex = p.active[i];
-      lo = p.offsets[ex];
-      hi = p.offsets[ex + 1];
-    }
-    const int nb = ex >= 0 ? (hi - lo + nt - 1) / nt : 0;
-    int incl = nb;
-#pragma unroll
-    for (int off = 1; off < 32; off <<= 1) {
-      const int v = __shfl_up_sync(0xffffffffu, incl, off);
-      if (lane >= off) incl += v;
-    }
-    const unsigned hit = __ballot_sync(0xffffffffu, ex >= 0 && base + incl > tblock);
-    if (hit) {
-      const int src = __ffs(hit) - 1;
-      const int ex_s = __shfl_sync(0xffffffffu, ex, src);
-      const int lo_s = __shfl_sync(0xffffffffu, lo, src);
-      const int hi_s = __shfl_sync(0xffffffffu, hi, src);
-      const int first = (int)(base + __shfl_sync(0xffffffffu, incl - nb, src));
-      ti.e = ex_s;
-      ti.s0 = lo_s + (int)(tblock - first) * nt;
-      ti.cnt = min(nt, hi_s - ti.s0);
-    }
-    base += __shfl_sync(0xffffffffu, incl, 31);
-  }
-  return ti;
+__device__ __forceinline__ uint32_t u4_word(const uint4& v, int i) {
+  return i == 0 ? v.x : i == 1 ? v.y : i == 2 ? v.z : v.w;
 }
 
-template <int NT, int KS, int PK, int SA, int SB, int G>
+// Block that owns unit u of U units split over `grid` blocks in equal runs
+// (block b owns [floor(b U / grid), floor((b + 1) U / grid))).
+// 32-bit: the launcher splits only problems with U * grid < 2^31.
+__device__ __forceinline__ int unit_owner(int u, int U, int grid) { return ((u + 1) * grid - 1) / U; }
+__device__ __forceinline__ int unit_start(int b, int U, int grid) { return b * U / grid; }
+
+template <int NT, int KS, int PK, int SA, int SB, int G, int H, int BPS>
 struct Layout {
   static constexpr int kP = kM * 32 * KS;     // packed codes of one stage
   static constexpr int kS = 2 * kM * kSK * 2;  // scales | biases of 8 k-steps
   static constexpr int kB = NT * 128 * KS;     // f16 activation stage
-  static constexpr int kHead = 1024 + kMaxTiles * 16;
-  static constexpr int kOffS = kHead;
+  static constexpr int kOffSeg = 1024;
+  static constexpr int kHead = kOffSeg + kMaxSegs * (int)sizeof(Seg);
+  static constexpr int kOffS = (kHead + 1023) / 1024 * 1024;
   static constexpr int kOffP = (kOffS + 2 * kS + 1023) / 1024 * 1024;
   static constexpr int kOffB = kOffP + PK * kP;
   static constexpr int kBytes = kOffB + SB * kB + 1024;  // + alignment slack
@@ -367,15 +372,92 @@ struct Layout {
   static constexpr int kACol0 = 2 * NT;
   static_assert(kP % 1024 == 0 && kB % 1024 == 0, "stage sizes keep 1024-byte alignment");
   static_assert(kSK % KS == 0, "a scale slot holds whole stages");
-  static_assert(kACol0 + SA * kAStage <= (int)Roles<G>::kTmemCols, "accumulators and A stages fit tensor memory");
+  static_assert(kACol0 + SA * kAStage <= (int)Roles<G * H, BPS>::kTmemCols, "accumulators and A stages fit tensor memory");
+  static_assert(4 * (kMaxExperts + 1) * 4 <= PK * kP, "setup expert table fits the code ring");
+  static_assert(H == 1 || H == 2, "one or two threads per weight row and k-step");
+  // mbarriers (then the TMEM slot and segment count) below the wait control at 448.
+  static_assert((2 * PK + 2 * SA + 2 * SB + 9) * 8 + 8 <= 448, "barrier block fits below the wait control");
 };
 
-template <typename T, int EPI, bool PERM, int NT, int KS, int PK, int SA, int SB, int G>
-__global__ void __launch_bounds__(Roles<G>::kThreads, Roles<G>::kBlocksPerSM)
+// Epilogue of 16 accumulator columns (tokens c0 .. c0 + 15 of the segment's
+// tile) held by TMEM lane q.
+template <typename T, int EPI>
+__device__ __forceinline__ void epi_apply(const Params& p, const Seg& sg, int q, int c0, const float* v) {
+  constexpr bool kSw = EPI == EPI_SWIGLU;
+  if (kSw) {
+    // Lanes 2j (gate row j) and 2j+1 (up row j) split the 16 tokens: the even
+    // lane finishes tokens 0-7, the odd one 8-15, each getting the partner's
+    // value with one shuffle.  SiLU uses the fast exponential and division;
+    // the result is rounded to the activation dtype like the reference's
+    // compiled silu * up.
+    const int f = sg.rb * (kM / 2) + (q >> 1);
+    const int fo = p.y_f16 ? perm_col(f) : f;  // an f16 operand for the next tensor-core QMM
+    const int odd = q & 1;
+    bool wide = false;  // a value beyond the f16 range went to the f16 operand
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float mine = odd ? v[8 + i] : v[i];
+      const float theirs = __shfl_xor_sync(0xffffffffu, odd ? v[i] : v[8 + i], 1);
+      const int tok = c0 + i + 8 * odd;
+      if (tok < sg.cnt && f < p.out) {
+        const float gg = round_act<T>(odd ? theirs : mine);
+        const float uu = round_act<T>(odd ? mine : theirs);
+        const float sl = round_act<T>(__fdividef(gg, 1.0f + __expf(-gg)));
+        const float hv = round_act<T>(sl * uu);
+        const int64_t row = (int64_t)(sg.s0 + tok) * p.y_stride;
+        if (p.y_f16) {
+          wide |= fabsf(hv) > 65504.f;
+          static_cast<__half*>(p.y)[row + fo] = __float2half_rn(hv);
+        } else {
+          static_cast<T*>(p.y)[row + f] = from_f<T>(hv);
+        }
+      }
+    }
+    // The f16 operand of the down projection: a bf16 value beyond the f16
+    // range became inf there, which records device error 5.
+    if (wide) atomicCAS(&g_tc_error, 0, 5);
+  } else {
+    const int f = sg.rb * kM + q;
+#pragma unroll
+    for (int i0 = 0; i0 < 16; i0 += 8) {
+      float res[8];
+      if (EPI == EPI_RESIDUAL) {
+        // All 8 residual loads before any store (y may alias residual).
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int tok = c0 + i0 + i;
+          res[i] = tok < sg.cnt && f < p.out
+                       ? to_f(static_cast<const T*>(p.residual)[(int64_t)(sg.s0 + tok) * p.residual_stride + f])
+                       : 0.f;
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int tok = c0 + i0 + i;
+        const float vi = v[i0 + i];
+        if (tok < sg.cnt && f < p.out) {
+          const int64_t slot = sg.s0 + tok;
+          if (EPI == EPI_F32) {
+            static_cast<float*>(p.y)[slot * p.y_stride + f] = round_act<T>(vi);
+          } else if (EPI == EPI_RESIDUAL) {
+            static_cast<T*>(p.y)[slot * p.y_stride + f] = from_f<T>(res[i] + round_act<T>(vi));
+          } else {
+            static_cast<T*>(p.y)[slot * p.y_stride + f] = from_f<T>(vi);
+          }
+        }
+      }
+    }
+  }
+}
+
+template <typename T, int EPI, bool PERM, int NT, int KS, int PK, int SA, int SB, int G, int H, int BPS>
+__global__ void __launch_bounds__(Roles<G * H, BPS>::kThreads, BPS)
     qmm_tc_kernel(const __grid_constant__ Params p) {
-  using L = Layout<NT, KS, PK, SA, SB, G>;
-  using R = Roles<G>;
-  constexpr int kDeqGroups = R::kDeqGroups, kDeqWarps = R::kDeqWarps, kEpiWarps = R::kEpiWarps;
+  using L = Layout<NT, KS, PK, SA, SB, G, H, BPS>;
+  // G groups of 4 H warps; Roles counts groups of 4 warps.
+  using R = Roles<G * H, BPS>;
+  constexpr int kDeqWarps = R::kDeqWarps, kEpiWarps = R::kEpiWarps;
+  constexpr int kGroupWarps = 4 * H;
   constexpr int kLoadWarp = R::kLoadWarp, kMmaWarp = R::kMmaWarp, kActWarp = R::kActWarp;
   constexpr uint32_t kTmemCols = R::kTmemCols;
   extern __shared__ uint8_t smem_raw[];
@@ -392,29 +474,31 @@ __global__ void __launch_bounds__(Roles<G>::kThreads, Roles<G>::kBlocksPerSM)
   uint64_t* acc_empty = acc_full + 2;
   uint64_t* drain = acc_empty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  int* ntiles_s = const_cast<int*>(abort_flag) + 1;
-  TileInfo* table = reinterpret_cast<TileInfo*>(base + 1024);
+  WaitCtl* wctl = reinterpret_cast<WaitCtl*>(base + 448);
+  int* nsegs_s = reinterpret_cast<int*>(tmem_slot + 1);
+  int* units_s = reinterpret_cast<int*>(base + 512);
+  Seg* segs = reinterpret_cast<Seg*>(base + L::kOffSeg);
   uint8_t* ring_s = base + L::kOffS;  // [2 slots][s | b][kM rows][8 k-steps] f16
   uint8_t* ring_p = base + L::kOffP;
   uint8_t* ring_b = base + L::kOffB;
   const int nk = p.in / kKStep;  // a multiple of 8
+  const int cpt = nk / kSK;      // chunks per tile
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
 
   // ---- setup
   if (tid == 0) {
     for (int i = 0; i < PK; ++i) {
       mbar_init(&p_full[i], 1);
-      mbar_init(&p_empty[i], kDeqWarps / kDeqGroups);
+      mbar_init(&p_empty[i], kGroupWarps);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
-      mbar_init(&s_empty[i], kDeqWarps);  // both groups use every scale block
+      mbar_init(&s_empty[i], kDeqWarps);  // every group uses every scale block
       mbar_init(&acc_full[i], 1);
       mbar_init(&acc_empty[i], kEpiWarps);
     }
     for (int i = 0; i < SA; ++i) {
-      mbar_init(&a_full[i], kDeqWarps / kDeqGroups);
+      mbar_init(&a_full[i], kGroupWarps);
       mbar_init(&a_empty[i], 1);
     }
     for (int i = 0; i < SB; ++i) {
@@ -422,7 +506,10 @@ __global__ void __launch_bounds__(Roles<G>::kThreads, Roles<G>::kBlocksPerSM)
       mbar_init(&b_empty[i], 1);
     }
     mbar_init(drain, 1);
-    *abort_flag = 0;
+    const long long lim = g_wait_cycles;
+    wctl->abort = 0;
+    wctl->limit = lim;
+    wctl->suspend_ns = lim < 2000000000LL ? 0u : kSuspendNs;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == kMmaWarp) {
@@ -431,37 +518,117 @@ __global__ void __launch_bounds__(Roles<G>::kThreads, Roles<G>::kBlocksPerSM)
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
   }
   if (warp == 0) {
-    // This block's tiles: t = blockIdx.x + i * gridDim.x while t < tiles_bound.
-    int n = 0;
-    for (int64_t t = blockIdx.x; t < p.tiles_bound && n < kMaxTiles; t += gridDim.x) {
-      const TileInfo ti = lookup_tile(p, t, NT, lane);
-      if (ti.e < 0) break;  // tiles are enumerated in order; later ones are past the end too
-      if (lane == 0) table[n] = ti;
-      ++n;
+    // Segment table.  Grouped problems: the active experts' token blocks
+    // (prefix sums in a table that lives in the code ring until the loaders
+    // start), then every tile found by binary search, one lane per segment.
+    int* ex_id = reinterpret_cast<int*>(ring_p);
+    int* ex_lo = ex_id + kMaxExperts;
+    int* ex_hi = ex_lo + kMaxExperts;
+    int* tb_end = ex_hi + kMaxExperts;
+    int na = 0;
+    int tblocks;
+    if (p.grouped) {
+      na = min(*p.active_count, kMaxExperts);
+      int run = 0;
+      for (int c0 = 0; c0 < na; c0 += 32) {
+        const int i = c0 + lane;
+        int nb = 0;
+        if (i < na) {
+          const int ex = p.active[i];
+          const int lo = p.offsets[ex], hi = p.offsets[ex + 1];
+          nb = (hi - lo + NT - 1) / NT;
+          ex_id[i] = ex;
+          ex_lo[i] = lo;
+          ex_hi[i] = hi;
+        }
+        int incl = nb;
+#pragma unroll
+        for (int off = 1; off < 32; off <<= 1) {
+          const int v = __shfl_up_sync(0xffffffffu, incl, off);
+          if (lane >= off) incl += v;
+        }
+        if (i < na) tb_end[i] = run + incl;
+        run += __shfl_sync(0xffffffffu, incl, 31);
+      }
+      tblocks = run;
+    } else {
+      tblocks = (int)((p.n + NT - 1) / NT);
     }
-    if (lane == 0) *ntiles_s = n;
+    __syncwarp();
+    const int tiles = tblocks * p.row_blocks;  // < 2^31 (launcher)
+    const int grid = (int)gridDim.x;
+    int U = 0, u0 = 0, u1 = 0, t_first = 0, t_last = -1;
+    int ns;
+    if (p.split) {
+      U = tiles * cpt;
+      u0 = unit_start(blockIdx.x, U, grid);
+      u1 = unit_start(blockIdx.x + 1, U, grid);
+      if (u1 > u0) {
+        t_first = u0 / cpt;
+        t_last = (u1 - 1) / cpt;
+      }
+      ns = t_last - t_first + 1;
+    } else {
+      ns = (int)blockIdx.x < tiles ? (tiles - 1 - (int)blockIdx.x) / grid + 1 : 0;
+    }
+    const int nsegs = (int)(ns < kMaxSegs ? ns : kMaxSegs);  // the launcher sizes the grid so ns fits
+    for (int j = lane; j < nsegs; j += 32) {
+      const int t = p.split ? t_first + j : (int)blockIdx.x + j * grid;
+      const int tblock = t / p.row_blocks;
+      Seg s;
+      s.tile = t;
+      s.rb = t - tblock * p.row_blocks;
+      if (p.grouped) {
+        int lo = 0, hi = na - 1;  // first i with tb_end[i] > tblock
+        while (lo < hi) {
+          const int mid = (lo + hi) >> 1;
+          if (tb_end[mid] > tblock)
+            hi = mid;
+          else
+            lo = mid + 1;
+        }
+        const int first = lo ? tb_end[lo - 1] : 0;
+        s.e = ex_id[lo];
+        s.s0 = ex_lo[lo] + (tblock - first) * NT;
+        s.cnt = min(NT, ex_hi[lo] - s.s0);
+      } else {
+        s.e = 0;
+        s.s0 = tblock * NT;
+        s.cnt = (int)((p.n - s.s0) < (int64_t)NT ? (p.n - s.s0) : (int64_t)NT);
+      }
+      s.kc0 = p.split && t == t_first ? u0 - t * cpt : 0;
+      s.kc1 = p.split && t == t_last ? u1 - t * cpt : cpt;
+      s.whole = s.kc0 == 0 && s.kc1 == cpt;
+      segs[j] = s;
+    }
+    if (lane == 0) {
+      *nsegs_s = nsegs;
+      *units_s = U;
+    }
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  const int ntiles = *ntiles_s;
+  const int nsegs = *nsegs_s;
   const uint32_t tmem = *tmem_slot;
   constexpr bool kSw = EPI == EPI_SWIGLU;
   constexpr int kTileRows = kSw ? kM / 2 : kM;  // rows of each weight matrix per tile
+  constexpr int kSpb = kSK / KS;                // stages per scale block
 
   if (warp == kLoadWarp) {
     // ---- code loader: lane 0 streams packed codes (PK stages ahead of the
-    // dequant warps) and the scales of every 8 k-steps.  Activation tiles
-    // have their own warp, so the weight stream never waits on the MMA.
+    // dequant warps) and the scales of every chunk.  Activation tiles have
+    // their own warp, so the weight stream never waits on the MMA.
     if (lane == 0) {
       int g = 0, gs = 0;  // stage and scale-block counters (< 2^31 per block)
       bool ok = true;
-      for (int li = 0; li < ntiles && ok; ++li) {
-        const TileInfo ti = table[li];
-        const int row0 = ti.e * p.out + ti.rb * kTileRows;
-        for (int k8 = 0; k8 < nk && ok; k8 += kSK, ++gs) {
-          const int ss = (int)(gs & 1);
-          if (gs >= 2 && !(ok = mbar_wait(&s_empty[ss], (uint32_t)(((gs >> 1) - 1) & 1), abort_flag, 11))) break;
+      for (int j = 0; j < nsegs && ok; ++j) {
+        const Seg sg = segs[j];
+        const int row0 = sg.e * p.out + sg.rb * kTileRows;
+        for (int c = sg.kc0; c < sg.kc1 && ok; ++c, ++gs) {
+          const int k8 = c * kSK;
+          const int ss = gs & 1;
+          if (gs >= 2 && !(ok = mbar_wait(&s_empty[ss], (uint32_t)(((gs >> 1) - 1) & 1), wctl, 11))) break;
           uint8_t* sdst = ring_s + (size_t)ss * L::kS;
           mbar_expect_tx(&s_full[ss], (uint32_t)L::kS);
           tma_2d(sdst, &p.tm_s0, k8, row0, &s_full[ss]);
@@ -471,8 +638,8 @@ __global__ void __launch_bounds__(Roles<G>::kThreads, Roles<G>::kBlocksPerSM)
             tma_2d(sdst + kM * kSK * 2 + 64 * kSK * 2, &p.tm_b1, k8, row0, &s_full[ss]);
           }
           for (int ks = 0; ks < kSK && ok; ks += KS, ++g) {
-            const int ps = (int)(g % PK);
-            if (g >= PK && !(ok = mbar_wait(&p_empty[ps], (uint32_t)(((g / PK) - 1) & 1), abort_flag, 12))) break;
+            const int ps = g % PK;
+            if (g >= PK && !(ok = mbar_wait(&p_empty[ps], (uint32_t)(((g / PK) - 1) & 1), wctl, 12))) break;
             uint8_t* pdst = ring_p + (size_t)ps * L::kP;
             mbar_expect_tx(&p_full[ps], (uint32_t)L::kP);
             tma_2d(pdst, &p.tm_q0, (k8 + ks) * 8, row0, &p_full[ps]);
@@ -480,6 +647,10 @@ __global__ void __launch_bounds__(Roles<G>::kThreads, Roles<G>::kBlocksPerSM)
           }
         }
       }
+      // Every copy issued into the rings lands before the block may exit
+      // (after an expired wait the consumers are gone but the copies are not).
+      for (int i = g - 1; i >= 0 && i >= g - PK; --i) mbar_drain(&p_full[i % PK], (uint32_t)((i / PK) & 1));
+      for (int i = gs - 1; i >= 0 && i >= gs - 2; --i) mbar_drain(&s_full[i & 1], (uint32_t)((i >> 1) & 1));
     }
   } else if (warp == kActWarp) {
     // ---- activation loader: lane 0 streams each stage's activation tiles
@@ -487,71 +658,82 @@ __global__ void __launch_bounds__(Roles<G>::kThreads, Roles<G>::kBlocksPerSM)
     if (lane == 0) {
       int g = 0;
       bool ok = true;
-      for (int li = 0; li < ntiles && ok; ++li) {
-        const int s0 = table[li].s0;
-        for (int k = 0; k < nk && ok; k += KS, ++g) {
-          const int bs = (int)(g % SB);
-          if (g >= SB && !(ok = mbar_wait(&b_empty[bs], (uint32_t)(((g / SB) - 1) & 1), abort_flag, 13))) break;
+      for (int j = 0; j < nsegs && ok; ++j) {
+        const Seg sg = segs[j];
+        for (int k = sg.kc0 * kSK; k < sg.kc1 * kSK && ok; k += KS, ++g) {
+          const int bs = g % SB;
+          if (g >= SB && !(ok = mbar_wait(&b_empty[bs], (uint32_t)(((g / SB) - 1) & 1), wctl, 13))) break;
           uint8_t* bdst = ring_b + (size_t)bs * L::kB;
           mbar_expect_tx(&b_full[bs], (uint32_t)L::kB);
 #pragma unroll
-          for (int kk = 0; kk < KS; ++kk) tma_2d(bdst + kk * NT * 128, &p.tm_x, (k + kk) * kKStep, s0, &b_full[bs]);
+          for (int kk = 0; kk < KS; ++kk)
+            tma_2d(bdst + kk * NT * 128, &p.tm_x, (k + kk) * kKStep, sg.s0, &b_full[bs]);
         }
       }
+      for (int i = g - 1; i >= 0 && i >= g - SB; --i) mbar_drain(&b_full[i % SB], (uint32_t)((i / SB) & 1));
     }
   } else if (warp < kDeqWarps) {
-    // ---- dequant: group grp takes stages g = grp, grp + 2, ...; in a group
-    // warp w owns TMEM lanes (A rows) 32(w%4).. and k half (w/4)%2 of every
-    // k-step: each thread turns 4 packed words (32 codes) per k-step into 16
-    // TMEM columns of its row.  Every lane waits on the full barriers
-    // (warp-uniform result); one lane per warp arrives on the release
-    // barriers after __syncwarp (the barriers count warps).
-    static_assert(KS == 2 && (kDeqGroups == 1 || kDeqGroups == 2) && kSK / KS == 4,
-                  "each group takes two stages (one scale pair each) of every scale block");
-    constexpr int kSpb = kSK / KS;  // stages per scale block
-    const int grp = warp >> 3, quarter = warp & 3, kh = (warp >> 2) & 1;
+    // ---- dequant: group grp (4 H warps) takes stages g = grp, grp + G, ...;
+    // in a group warp w owns TMEM lanes (A rows) 32 (w % 4).. and, with
+    // H = 2, half kh = w / 4 of every k-step: each thread turns 8 / H packed
+    // words per k-step into 32 / H TMEM columns of its row.  Every lane waits
+    // on the full barriers (warp-uniform result); one lane per warp arrives
+    // on the release barriers after __syncwarp (the barriers count warps).
+    static_assert(kSpb % G == 0, "each group takes the same stages of every scale block");
+    constexpr int kWords = 8 / H;  // packed words per thread and k-step
+    const int grp = warp / kGroupWarps, sub = warp % kGroupWarps;
+    const int quarter = sub & 3, kh = sub >> 2;
     const int r = quarter * 32 + lane;
     // A row r <- packed/scale row pr.  SwiGLU tiles interleave gate row j
     // (A row 2j) and up row j (A row 2j+1); the packed and scale slots hold
     // gate rows 0..63 then up rows 64..127.
     const int pr = kSw ? ((r & 1) * 64 + (r >> 1)) : r;
-    const uint32_t tlane = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(L::kACol0 + kh * (kACols / 2));
-    const int total = ntiles * (nk / KS);
+    const uint32_t tlane =
+        tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(L::kACol0 + kh * (kACols / H));
+    int total = 0;
+    for (int j = 0; j < nsegs; ++j) total += (segs[j].kc1 - segs[j].kc0) * kSpb;
     uint4 sv = make_uint4(0, 0, 0, 0), bv = sv;
     bool ok = true;
-    for (int g = grp; g < total && ok; g += kDeqGroups) {
-      const int sb = (int)(g % kSpb);
+    for (int g = grp; g < total && ok; g += G) {
+      const int sb = g % kSpb;
       const int blk = g / kSpb;
-      if (sb == grp) {  // this group's first stage of a scale block
-        if (!(ok = warp_wait(&s_full[blk & 1], (uint32_t)((blk >> 1) & 1), abort_flag, 21))) break;
+      if (sb == grp % kSpb) {  // this group's first stage of a scale block
+        if (!(ok = warp_wait(&s_full[blk & 1], (uint32_t)((blk >> 1) & 1), wctl, 21))) break;
         const uint8_t* sslot = ring_s + (size_t)(blk & 1) * L::kS;
         sv = *reinterpret_cast<const uint4*>(sslot + pr * 16);
         bv = *reinterpret_cast<const uint4*>(sslot + kM * kSK * 2 + pr * 16);
       }
-      const int ps = (int)(g % PK);
-      if (!(ok = warp_wait(&p_full[ps], (uint32_t)((g / PK) & 1), abort_flag, 22))) break;
-      const uint4 w0 = *reinterpret_cast<const uint4*>(ring_p + (size_t)ps * L::kP + pr * (32 * KS) + kh * 16);
-      const uint4 w1 = *reinterpret_cast<const uint4*>(ring_p + (size_t)ps * L::kP + pr * (32 * KS) + 32 + kh * 16);
-      const int as = (int)(g % SA);
-      if (g >= SA && !(ok = warp_wait(&a_empty[as], (uint32_t)(((g / SA) - 1) & 1), abort_flag, 23))) break;
+      const int ps = g % PK;
+      if (!(ok = warp_wait(&p_full[ps], (uint32_t)((g / PK) & 1), wctl, 22))) break;
+      uint4 w[KS][kWords / 4];
+      const uint8_t* src = ring_p + (size_t)ps * L::kP + pr * (32 * KS) + kh * (32 / H);
+#pragma unroll
+      for (int kk = 0; kk < KS; ++kk)
+#pragma unroll
+        for (int i = 0; i < kWords / 4; ++i) w[kk][i] = *reinterpret_cast<const uint4*>(src + kk * 32 + 16 * i);
+      const int as = g % SA;
+      if (g >= SA && !(ok = warp_wait(&a_empty[as], (uint32_t)(((g / SA) - 1) & 1), wctl, 23))) break;
       tc_fence_after();
-      // k-steps 2 sb and 2 sb + 1 of the scale block: one f16 pair of s and b.
-      const uint32_t spw = sb < 2 ? (sb ? sv.y : sv.x) : (sb == 3 ? sv.w : sv.z);
-      const uint32_t bpw = sb < 2 ? (sb ? bv.y : bv.x) : (sb == 3 ? bv.w : bv.z);
-      const __half2 sp = *reinterpret_cast<const __half2*>(&spw);
-      const __half2 bp = *reinterpret_cast<const __half2*>(&bpw);
-      const uint32_t wa[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
 #pragma unroll
-      for (int kk = 0; kk < 2; ++kk) {
-        const __half2 s2 = kk ? __high2half2(sp) : __low2half2(sp);
-        const __half2 b2 = kk ? __high2half2(bp) : __low2half2(bp);
-        uint32_t cols[16];
+      for (int kk = 0; kk < KS; ++kk) {
+        // k-step sb * KS + kk of the scale block: f16 scale and bias.
+        const int ki = sb * KS + kk;
+        const uint32_t spw = u4_word(sv, ki >> 1), bpw = u4_word(bv, ki >> 1);
+        const __half2 sp = *reinterpret_cast<const __half2*>(&spw);
+        const __half2 bp = *reinterpret_cast<const __half2*>(&bpw);
+        const __half2 s2 = (ki & 1) ? __high2half2(sp) : __low2half2(sp);
+        const __half2 b2 = (ki & 1) ? __high2half2(bp) : __low2half2(bp);
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const uint4 d = dequant8<PERM>(wa[4 * kk + i], s2, b2);
-          cols[4 * i] = d.x, cols[4 * i + 1] = d.y, cols[4 * i + 2] = d.z, cols[4 * i + 3] = d.w;
+        for (int h = 0; h < kWords / 4; ++h) {
+          const uint32_t wa[4] = {w[kk][h].x, w[kk][h].y, w[kk][h].z, w[kk][h].w};
+          uint32_t cols[16];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const uint4 d = dequant8<PERM>(wa[i], s2, b2);
+            cols[4 * i] = d.x, cols[4 * i + 1] = d.y, cols[4 * i + 2] = d.z, cols[4 * i + 3] = d.w;
+          }
+          tmem_st16(tlane + (uint32_t)(as * L::kAStage + kk * kACols + h * 16), cols);
         }
-        tmem_st16(tlane + (uint32_t)(as * L::kAStage + kk * kACols), cols);
       }
       tmem_st_wait();
       tc_fence_before();
@@ -564,7 +746,7 @@ __global__ void __launch_bounds__(Roles<G>::kThreads, Roles<G>::kBlocksPerSM)
       if (lane == 0) {
         mbar_arrive(&a_full[as]);
         mbar_arrive(&p_empty[ps]);
-        if (sb + kDeqGroups >= kSpb) mbar_arrive(&s_empty[blk & 1]);
+        if (sb + G >= kSpb) mbar_arrive(&s_empty[blk & 1]);
       }
     }
   } else if (warp == kMmaWarp) {
@@ -572,27 +754,28 @@ __global__ void __launch_bounds__(Roles<G>::kThreads, Roles<G>::kBlocksPerSM)
     const uint32_t leader = elect_one();
     int g = 0;
     bool ok = true;
-    for (int li = 0; li < ntiles && ok; ++li) {
-      const TileInfo ti = table[li];
-      const int buf = li & 1;
-      if (li >= 2 && !(ok = warp_wait(&acc_empty[buf], (uint32_t)(((li >> 1) - 1) & 1), abort_flag, 31))) break;
+    for (int j = 0; j < nsegs && ok; ++j) {
+      const Seg sg = segs[j];
+      const int buf = j & 1;
+      if (j >= 2 && !(ok = warp_wait(&acc_empty[buf], (uint32_t)(((j >> 1) - 1) & 1), wctl, 31))) break;
       tc_fence_after();
-      const int n_mma = (ti.cnt + 15) / 16 * 16;
+      const int n_mma = (sg.cnt + 15) / 16 * 16;
       const uint32_t idesc = idesc_f16(kM, n_mma);
       const uint32_t d = tmem + (uint32_t)(buf * NT);
-      for (int k = 0; k < nk; k += KS, ++g) {
-        const int as = (int)(g % SA);
-        const int bs = (int)(g % SB);
-        if (!(ok = warp_wait(&a_full[as], (uint32_t)((g / SA) & 1), abort_flag, 32))) break;
-        if (!(ok = warp_wait(&b_full[bs], (uint32_t)((g / SB) & 1), abort_flag, 33))) break;
+      const int k0 = sg.kc0 * kSK, k1 = sg.kc1 * kSK;
+      for (int k = k0; k < k1; k += KS, ++g) {
+        const int as = g % SA;
+        const int bs = g % SB;
+        if (!(ok = warp_wait(&a_full[as], (uint32_t)((g / SA) & 1), wctl, 32))) break;
+        if (!(ok = warp_wait(&b_full[bs], (uint32_t)((g / SB) & 1), wctl, 33))) break;
         tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < KS; ++kk) {
           const uint32_t ta = tmem + (uint32_t)(L::kACol0 + as * L::kAStage + kk * kACols);
           const uint64_t bd = sw128_desc(smem_addr(ring_b + (size_t)bs * L::kB + kk * (NT * 128)));
 #pragma unroll
-          for (int j = 0; j < kKStep / 16; ++j)  // K=16 slice: 8 TMEM columns of A, +32 B (+2) of B
-            mma_f16_ts(leader, d, ta + 8 * j, bd + 2 * j, idesc, (k + kk > 0 || j > 0) ? 1u : 0u);
+          for (int s = 0; s < kKStep / 16; ++s)  // K=16 slice: 8 TMEM columns of A, +32 B (+2) of B
+            mma_f16_ts(leader, d, ta + 8 * s, bd + 2 * s, idesc, (k + kk > k0 || s > 0) ? 1u : 0u);
         }
         mma_commit(leader, &a_empty[as]);
         mma_commit(leader, &b_empty[bs]);
@@ -601,84 +784,87 @@ __global__ void __launch_bounds__(Roles<G>::kThreads, Roles<G>::kBlocksPerSM)
     }
     // Every MMA issued by this warp completes before TMEM is released.
     mma_commit(leader, drain);
-    mbar_wait(drain, 0, abort_flag, 34);
+    mbar_drain(drain, 0);
   } else {
-    // ---- epilogue: warps 8-11 read TMEM lane quarters 0-3
+    // ---- epilogue: warps kDeqWarps .. + 3 read TMEM lane quarters 0-3
     const int q = tid - kDeqWarps * 32;  // TMEM lane 0..127
     const int wq = warp & 3;
+    const int grid = (int)gridDim.x;
+    const int U = *units_s;
     bool ok = true;
-    for (int li = 0; li < ntiles && ok; ++li) {
-      const TileInfo ti = table[li];
-      const int buf = li & 1;
-      if (!(ok = warp_wait(&acc_full[buf], (uint32_t)((li >> 1) & 1), abort_flag, 41))) break;
+    for (int j = 0; j < nsegs && ok; ++j) {
+      const Seg sg = segs[j];
+      const int buf = j & 1;
+      if (!(ok = warp_wait(&acc_full[buf], (uint32_t)((j >> 1) & 1), wctl, 41))) break;
       tc_fence_after();
-      const int n_mma = (ti.cnt + 15) / 16 * 16;
+      const int n_mma = (sg.cnt + 15) / 16 * 16;
       const uint32_t taddr = tmem + ((uint32_t)(wq * 32) << 16) + (uint32_t)(buf * NT);
+      if (sg.whole) {
+        for (int c0 = 0; c0 < n_mma; c0 += 16) {
+          float v[16];
+          tmem_ld16(taddr + c0, v);
+          epi_apply<T, EPI>(p, sg, q, c0, v);
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&acc_empty[buf]);
+        continue;
+      }
+      // Part of a split tile: store this block's fp32 partial (slot 0 for
+      // the block's first segment, 1 for its last), release the accumulator,
+      // then count this warp's arrival.  The warp that arrives last sums the
+      // parts of all 128 rows in k order (block order) from the partials and
+      // runs the epilogue; nobody waits for anybody.
+      float* mine = p.partials + ((size_t)(2 * blockIdx.x + (j == 0 ? 0 : 1)) * kM + q) * NT;
+#pragma unroll 1
       for (int c0 = 0; c0 < n_mma; c0 += 16) {
         float v[16];
         tmem_ld16(taddr + c0, v);
-        if (kSw) {
-          // Lanes 2j (gate row j) and 2j+1 (up row j) split the 16 tokens:
-          // the even lane finishes tokens 0-7, the odd one 8-15, each getting
-          // the partner's value with one shuffle.  SiLU uses the fast
-          // exponential and division; the result is rounded to the
-          // activation dtype like the reference's compiled silu * up.
-          const int f = ti.rb * (kM / 2) + (q >> 1);
-          const int fo = p.y_f16 ? perm_col(f) : f;  // an f16 operand for the next tensor-core QMM
-          const int odd = q & 1;
 #pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            const float mine = odd ? v[8 + i] : v[i];
-            const float theirs = __shfl_xor_sync(0xffffffffu, odd ? v[i] : v[8 + i], 1);
-            const int tok = c0 + i + 8 * odd;
-            if (tok < ti.cnt && f < p.out) {
-              const float gg = round_act<T>(odd ? theirs : mine);
-              const float uu = round_act<T>(odd ? mine : theirs);
-              const float sl = round_act<T>(__fdividef(gg, 1.0f + __expf(-gg)));
-              const float hv = round_act<T>(sl * uu);
-              const int64_t row = (int64_t)(ti.s0 + tok) * p.y_stride;
-              if (p.y_f16)
-                static_cast<__half*>(p.y)[row + fo] = __float2half_rn(hv);
-              else
-                static_cast<T*>(p.y)[row + f] = from_f<T>(hv);
-            }
-          }
-        } else {
-          const int f = ti.rb * kM + q;
-#pragma unroll
-          for (int i0 = 0; i0 < 16; i0 += 8) {
-            float res[8];
-            if (EPI == EPI_RESIDUAL) {
-              // All 8 residual loads before any store (y may alias residual).
-#pragma unroll
-              for (int i = 0; i < 8; ++i) {
-                const int tok = c0 + i0 + i;
-                res[i] = tok < ti.cnt && f < p.out
-                             ? to_f(static_cast<const T*>(p.residual)[(int64_t)(ti.s0 + tok) * p.residual_stride + f])
-                             : 0.f;
-              }
-            }
-#pragma unroll
-            for (int i = 0; i < 8; ++i) {
-              const int tok = c0 + i0 + i;
-              const float vi = v[i0 + i];
-              if (tok < ti.cnt && f < p.out) {
-                const int64_t slot = ti.s0 + tok;
-                if (EPI == EPI_F32) {
-                  static_cast<float*>(p.y)[slot * p.y_stride + f] = round_act<T>(vi);
-                } else if (EPI == EPI_RESIDUAL) {
-                  static_cast<T*>(p.y)[slot * p.y_stride + f] = from_f<T>(res[i] + round_act<T>(vi));
-                } else {
-                  static_cast<T*>(p.y)[slot * p.y_stride + f] = from_f<T>(vi);
-                }
-              }
-            }
-          }
-        }
+        for (int i = 0; i < 16; i += 4)
+          __stcg(reinterpret_cast<float4*>(mine + c0 + i), make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]));
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[buf]);
+      __threadfence();
+      __syncwarp();
+      const int b_lo = unit_owner(sg.tile * cpt, U, grid);
+      const int b_hi = unit_owner((sg.tile + 1) * cpt - 1, U, grid);
+      int parts = 0;  // blocks holding a part (with fewer units than blocks some runs are empty)
+      for (int b = b_lo; b <= b_hi; ++b) parts += unit_start(b + 1, U, grid) > unit_start(b, U, grid);
+      int seen = 0;
+      if (lane == 0) seen = atomicAdd(&p.counters[sg.tile], 1);
+      seen = __shfl_sync(0xffffffffu, seen, 0);
+      if (seen != kEpiWarps * parts - 1) continue;
+      __threadfence();
+#pragma unroll 1
+      for (int qq = 0; qq < 4; ++qq) {
+        const int qr = qq * 32 + lane;
+#pragma unroll 1
+        for (int c0 = 0; c0 < n_mma; c0 += 16) {
+          float v[16];
+          bool first = true;
+#pragma unroll 1
+          for (int b = b_lo; b <= b_hi; ++b) {
+            const int ub = unit_start(b, U, grid);
+            if (unit_start(b + 1, U, grid) == ub) continue;
+            const float* part = p.partials + ((size_t)(2 * b + (sg.tile == ub / cpt ? 0 : 1)) * kM + qr) * NT + c0;
+#pragma unroll
+            for (int i = 0; i < 16; i += 4) {
+              const float4 f = __ldcg(reinterpret_cast<const float4*>(part + i));
+              if (first) {
+                v[i] = f.x, v[i + 1] = f.y, v[i + 2] = f.z, v[i + 3] = f.w;
+              } else {
+                v[i] += f.x, v[i + 1] += f.y, v[i + 2] += f.z, v[i + 3] += f.w;
+              }
+            }
+            first = false;
+          }
+          epi_apply<T, EPI>(p, sg, qr, c0, v);
+        }
+      }
+      if (lane == 0) p.counters[sg.tile] = 0;  // left at zero for the next launch
     }
   }
   tc_fence_before();
@@ -739,10 +925,10 @@ int num_sms() {
 
 // Weight maps (codes box {8*KS words, rows}, scales/biases box {8, rows}) and
 // the launch of one configuration.
-template <typename T, int EPI, bool PERM, int NT, int KS, int PK, int SA, int SB, int G>
-tf_status launch_cfg(tc::Params& p, const QmmProblem& q, cudaStream_t s) {
-  using L = tc::Layout<NT, KS, PK, SA, SB, G>;
-  using R = tc::Roles<G>;
+template <typename T, int EPI, bool PERM, int NT, int KS, int PK, int SA, int SB, int G, int H, int BPS>
+tf_status launch_cfg(tc::Params& p, const QmmProblem& q, int64_t tiles_bound, cudaStream_t s) {
+  using L = tc::Layout<NT, KS, PK, SA, SB, G, H, BPS>;
+  using R = tc::Roles<G * H, BPS>;
   const bool sw = EPI == EPI_SWIGLU;
   const int in = p.in;
   const int64_t rows_total = (int64_t)(q.w0.experts > 0 ? q.w0.experts : 1) * p.out;
@@ -768,40 +954,63 @@ tf_status launch_cfg(tc::Params& p, const QmmProblem& q, cudaStream_t s) {
   static PerDeviceOnce attr;
   int dev = 0;
   if (attr.needed(&dev)) {
-    TF_CUDA(cudaFuncSetAttribute(tc::qmm_tc_kernel<T, EPI, PERM, NT, KS, PK, SA, SB, G>,
+    TF_CUDA(cudaFuncSetAttribute(tc::qmm_tc_kernel<T, EPI, PERM, NT, KS, PK, SA, SB, G, H, BPS>,
                                  cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    TF_CUDA(cudaFuncSetAttribute(tc::qmm_tc_kernel<T, EPI, PERM, NT, KS, PK, SA, SB, G>,
+    TF_CUDA(cudaFuncSetAttribute(tc::qmm_tc_kernel<T, EPI, PERM, NT, KS, PK, SA, SB, G, H, BPS>,
                                  cudaFuncAttributePreferredSharedMemoryCarveout, 100));
     attr.mark(dev);
   }
   const int64_t slots = (int64_t)num_sms() * R::kBlocksPerSM;
-  int64_t grid = p.tiles_bound < slots ? p.tiles_bound : slots;
-  const int64_t need = (p.tiles_bound + tc::kMaxTiles - 1) / tc::kMaxTiles;
-  if (grid < need) grid = need;
+  int64_t grid;
+  // Split schedule: every block slot takes an equal run of (tile, chunk)
+  // units.  It needs a partial slot pair per block, a counter per tile, and
+  // a segment table that holds a block's tiles.
+  p.split = q.partials && q.counters && tiles_bound <= q.counter_cap && tiles_bound * 16 * slots < 2147483647LL &&
+            (size_t)2 * slots * tc::kM * NT * sizeof(float) <= q.partial_bytes &&
+            tiles_bound <= (int64_t)(tc::kMaxSegs - 2) * slots;
+  if (p.split) {
+    grid = slots;
+    p.partials = q.partials;
+    p.counters = q.counters;
+  } else {
+    grid = tiles_bound < slots ? tiles_bound : slots;
+    const int64_t need = (tiles_bound + tc::kMaxSegs - 1) / tc::kMaxSegs;
+    if (grid < need) grid = need;
+  }
   if (grid <= 0) return TF_OK;
-  tc::qmm_tc_kernel<T, EPI, PERM, NT, KS, PK, SA, SB, G><<<(unsigned)grid, R::kThreads, smem, s>>>(p);
+  if (tiles_bound > 2147483647 / 2) return set_error(TF_ERR_UNSUPPORTED, "qmm_tc: %lld tiles", (long long)tiles_bound);
+  tc::qmm_tc_kernel<T, EPI, PERM, NT, KS, PK, SA, SB, G, H, BPS><<<(unsigned)grid, R::kThreads, smem, s>>>(p);
   return check_launch("qmm_tc");
 }
 
 template <typename T, int EPI, bool PERM>
-tf_status launch_nt(tc::Params& p, const QmmProblem& q, int nt, cudaStream_t s) {
+tf_status launch_nt(tc::Params& p, const QmmProblem& q, int nt, int64_t tiles_bound, cudaStream_t s) {
   switch (nt) {
-    // <NT, KS, PK, SA, SB, G>: expert tiles of a decode batch (many tiles,
-    // few tokens) run two blocks per SM (G = 1, 256 TMEM columns each); dense
-    // projections of a decode batch (few tiles) want one deep pipeline per
-    // block (G = 2, 4 A stages); prefill tiles one block with two groups.
-    case 32: return launch_cfg<T, EPI, PERM, 32, 2, 4, 3, 6, 1>(p, q, s);
-    case 64: return launch_cfg<T, EPI, PERM, 64, 2, 4, 4, 4, 2>(p, q, s);
-    default: return launch_cfg<T, EPI, PERM, 192, 2, 4, 2, 3, 2>(p, q, s);
+    // <NT, KS, PK, SA, SB, G, H, BPS>: expert tiles of a decode batch (many
+    // tiles, few tokens) run two blocks per SM (256 TMEM columns each) with
+    // two dequant groups of 4 warps; dense projections of a decode batch
+    // (few tiles) one block per SM with four groups and 4 A stages; prefill
+    // tiles one block with two groups of 8 warps (two threads per row and
+    // k-step).
+    case 32: return launch_cfg<T, EPI, PERM, 32, 2, 4, 3, 6, 2, 1, 2>(p, q, tiles_bound, s);
+    case 64: return launch_cfg<T, EPI, PERM, 64, 2, 4, 4, 4, 4, 1, 1>(p, q, tiles_bound, s);
+    default: return launch_cfg<T, EPI, PERM, 192, 2, 4, 2, 3, 2, 2, 1>(p, q, tiles_bound, s);
   }
 }
 
 template <typename T, int EPI>
-tf_status launch_perm(tc::Params& p, const QmmProblem& q, int nt, cudaStream_t s) {
-  return q.x16 && q.x16_perm ? launch_nt<T, EPI, true>(p, q, nt, s) : launch_nt<T, EPI, false>(p, q, nt, s);
+tf_status launch_perm(tc::Params& p, const QmmProblem& q, int nt, int64_t tiles_bound, cudaStream_t s) {
+  return q.x16 && q.x16_perm ? launch_nt<T, EPI, true>(p, q, nt, tiles_bound, s)
+                             : launch_nt<T, EPI, false>(p, q, nt, tiles_bound, s);
 }
 
 }  // namespace
+
+size_t qmm_split_partial_bytes() {
+  // The largest configuration that splits: 2 slots x 128 rows x NT fp32 per
+  // block, with (NT, blocks per SM) = (32, 2) or (64, 1).
+  return (size_t)2 * num_sms() * 2 * tc::kM * 32 * sizeof(float);
+}
 
 // Tensor-core QMM.  Activation rows must be contiguous in slot order: for
 // dense problems x itself (no x_index), for grouped problems the caller's
@@ -816,6 +1025,8 @@ tf_status launch_qmm_tc(const QmmProblem& q, cudaStream_t s) {
   if (in % 512 || in > 8192) return set_error(TF_ERR_UNSUPPORTED, "qmm_tc: in_features %d", in);
   const bool sw = q.epilogue == EPI_SWIGLU;
   const int experts = q.w0.experts > 0 ? q.w0.experts : 1;
+  if (q.mode == QMM_GROUPED && experts > tc::kMaxExperts)
+    return set_error(TF_ERR_UNSUPPORTED, "qmm_tc: %d experts (at most %d)", experts, tc::kMaxExperts);
   const int out = q.w0.out_features;
   const int tile_rows = sw ? 64 : 128;
   tc::Params p;
@@ -837,10 +1048,10 @@ tf_status launch_qmm_tc(const QmmProblem& q, cudaStream_t s) {
   const int64_t per_matrix = p.grouped ? (q.n + experts - 1) / experts : q.n;
   const int nt = per_matrix <= 24 ? 32 : per_matrix <= 64 ? 64 : 192;
   const int64_t token_tiles = p.grouped ? experts + q.n / nt + 1 : (q.n + nt - 1) / nt;
-  p.tiles_bound = token_tiles * p.row_blocks;
-#define TF_TC_EPI(E)                                                                \
-  return q.act == TF_DTYPE_F16 ? launch_perm<__half, E>(p, q, nt, s)                \
-                               : launch_perm<__nv_bfloat16, E>(p, q, nt, s);
+  const int64_t tiles_bound = token_tiles * p.row_blocks;
+#define TF_TC_EPI(E)                                                                         \
+  return q.act == TF_DTYPE_F16 ? launch_perm<__half, E>(p, q, nt, tiles_bound, s)            \
+                               : launch_perm<__nv_bfloat16, E>(p, q, nt, tiles_bound, s);
   switch (q.epilogue) {
     case EPI_PLAIN: TF_TC_EPI(EPI_PLAIN)
     case EPI_SWIGLU: TF_TC_EPI(EPI_SWIGLU)
@@ -900,6 +1111,12 @@ tf_status launch_bf16_to_f16(const void* x, int64_t n, void* y, int permute, cud
   if (n == 0) return TF_OK;
   if (n % 2048) return set_error(TF_ERR_SHAPE, "bf16_to_f16: count %lld not a multiple of 2048", (long long)n);
   return launch_gather_f16(x, 2048, TF_DTYPE_BF16, nullptr, 1, n / 2048, 2048, y, permute, s);
+}
+
+tf_status set_wait_limit(long long cycles) {
+  const long long v = cycles > 0 ? cycles : 2000000000LL;
+  TF_CUDA(cudaMemcpyToSymbol(g_wait_cycles, &v, sizeof(v)));
+  return TF_OK;
 }
 
 int read_tc_error(bool clear) {

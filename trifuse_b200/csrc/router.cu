@@ -14,6 +14,8 @@
 // rank compares the act-rounded probabilities (NaN last, ties to lower id).
 #include <math.h>
 
+#include <cooperative_groups.h>
+
 #include "common.cuh"
 #include "internal.h"
 
@@ -148,6 +150,64 @@ __global__ void __launch_bounds__(kRouterBlockWarps * 32)
   }
 }
 
+// Router for small batches (decode): a cluster of kRouterCluster CTAs per
+// token, each computing ceil(E / kRouterCluster) experts (one warp per
+// expert, the same fixed order as router_kernel), so the 64 dot products of
+// a token run on 8 SMs at once instead of one after another on one.  Every
+// CTA writes its act-rounded logits into CTA 0's shared memory (distributed
+// shared memory); after the cluster barrier CTA 0's first warp ranks them.
+constexpr int kRouterCluster = 8;
+
+template <typename T, bool DENSE, int J>
+__global__ void __cluster_dims__(kRouterCluster, 1, 1) __launch_bounds__(kRouterBlockWarps * 32)
+    router_cluster_kernel(const T* __restrict__ x, int64_t tokens, const T* __restrict__ wd,
+                          const uint32_t* __restrict__ wq, const __half* __restrict__ ws,
+                          const __half* __restrict__ wb, int E, int K, T* logits, int32_t* idx, T* gates) {
+  constexpr int H = J * 256;
+  __shared__ float ls[64];
+  namespace cg = cooperative_groups;
+  cg::cluster_group cluster = cg::this_cluster();
+  const int part = (int)cluster.block_rank();
+  const int64_t t = blockIdx.x / kRouterCluster;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int epc = (E + kRouterCluster - 1) / kRouterCluster;  // experts per CTA (<= 8)
+  const int e = part * epc + warp;
+  if (warp < epc && e < E && t < tokens) {
+    float acc = 0.f;
+#pragma unroll
+    for (int j = 0; j < J; ++j) {
+      const int c = lane + 32 * j;
+      float xf[8], wf[8];
+      unpack8<T>(ld_v4(x + t * H + 8 * c), xf);
+      if (DENSE) {
+        unpack8<T>(ld_v4(wd + (int64_t)e * H + 8 * c), wf);
+      } else {
+        const uint32_t word = wq[(int64_t)e * (H / 8) + c];
+        const float sc = __half2float(ws[(int64_t)e * (H / 64) + c / 8]);
+        const float bi = __half2float(wb[(int64_t)e * (H / 64) + c / 8]);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float code = (float)((word >> (4 * i)) & 0xFu);
+          wf[i] = __half2float(__float2half_rn(__fadd_rn(__fmul_rn(code, sc), bi)));
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < 8; ++i) acc = __fadd_rn(acc, __fmul_rn(xf[i], wf[i]));
+    }
+    const float la = round_act<T>(warp_sum_butterfly(acc));
+    if (lane == 0) {
+      *cluster.map_shared_rank(&ls[e], 0) = la;
+      if (logits) logits[t * E + e] = from_f<T>(la);
+    }
+  }
+  cluster.sync();
+  if (part == 0 && warp == 0 && idx && t < tokens) {
+    const float la0 = lane < E ? ls[lane] : 0.f;
+    const float la1 = lane + 32 < E ? ls[lane + 32] : 0.f;
+    route_token<T>(lane, la0, la1, E, K, t, (T*)nullptr, idx, gates);
+  }
+}
+
 template <typename T>
 __global__ void __launch_bounds__(kRouterWarps * 32)
     route_kernel(const T* __restrict__ logits, int64_t tokens, int E, int K, T* probs,
@@ -217,12 +277,39 @@ static tf_status router_dispatch_tpc(const void* x, int64_t tokens, int hidden,
   return check_launch("router");
 }
 
-// One token per block while that still fills the GPU; four (weights decoded
-// once per four tokens) for long prefill batches.
+template <typename T, bool DENSE>
+static tf_status router_dispatch_cluster(const void* x, int64_t tokens, int hidden, const tf_router_weight& r,
+                                         int E, int K, void* logits, int32_t* idx, void* gates, cudaStream_t s) {
+  const unsigned blocks = (unsigned)(tokens * kRouterCluster);
+  const T* wd = (const T*)r.dense;
+  const uint32_t* wq = r.affine.q;
+  const __half* wsc = (const __half*)r.affine.scales;
+  const __half* wbi = (const __half*)r.affine.biases;
+#define TF_ROUTER_CCASE(JJ)                                                                  \
+  case JJ:                                                                                   \
+    router_cluster_kernel<T, DENSE, JJ><<<blocks, kRouterBlockWarps * 32, 0, s>>>(            \
+        (const T*)x, tokens, wd, wq, wsc, wbi, E, K, (T*)logits, idx, (T*)gates);            \
+    break;
+  switch (hidden / 256) {
+    TF_ROUTER_CCASE(1)
+    TF_ROUTER_CCASE(2)
+    TF_ROUTER_CCASE(4)
+    TF_ROUTER_CCASE(8)
+    default:
+      return set_error(TF_ERR_UNSUPPORTED, "router: hidden %d not in {256,512,1024,2048}", hidden);
+  }
+#undef TF_ROUTER_CCASE
+  return check_launch("router_cluster");
+}
+
+// Decode-sized batches: a cluster of 8 CTAs per token.  Up to 2048 tokens:
+// one token per block; beyond, four (weights decoded once per four tokens).
 template <typename T, bool DENSE>
 static tf_status router_dispatch(const void* x, int64_t tokens, int hidden,
                                  const tf_router_weight& r, int E, int K, void* logits,
                                  int32_t* idx, void* gates, cudaStream_t s) {
+  if (tokens <= 256)
+    return router_dispatch_cluster<T, DENSE>(x, tokens, hidden, r, E, K, logits, idx, gates, s);
   if (tokens <= 2048)
     return router_dispatch_tpc<T, DENSE, 1>(x, tokens, hidden, r, E, K, logits, idx, gates, s);
   return router_dispatch_tpc<T, DENSE, 4>(x, tokens, hidden, r, E, K, logits, idx, gates, s);

@@ -191,6 +191,23 @@ class Session:
                 raise TriFuseError(9, "Greedy pipeline token outside vocabulary")
         return toks
 
+    def prefill_device(self, requests, counts, ids: torch.Tensor, logits: torch.Tensor | None = None):
+        """Prefill with device-resident inputs and outputs: ids int64 [sum(counts)]
+        on the device (concatenated per request, checked on the device by the
+        embedding), logits f32 [len(requests), vocab] on the device or None
+        (cache only).  The call synchronizes its stream before it returns
+        (its per-row bookkeeping is staged from host memory)."""
+        n = len(requests)
+        req = (C.c_int32 * n)(*requests)
+        cnt = (C.c_int32 * n)(*counts)
+        ids = ids.to(torch.int64).contiguous()
+        if not ids.is_cuda or (logits is not None and not logits.is_cuda):
+            raise ValueError("prefill_device: ids and logits must be device tensors")
+        check(lib().tf_session_prefill(self.handle, req, cnt, n, C.c_void_p(ids.data_ptr()),
+                                       C.c_void_p(logits.data_ptr()) if logits is not None else None, 0,
+                                       C.c_void_p(torch.cuda.current_stream().cuda_stream)))
+        return logits
+
     def prefill(self, requests, token_lists, want_logits=True):
         """Prefill several requests; token_lists: list of int64 tensors/lists."""
         counts = [len(t) for t in token_lists]
@@ -219,6 +236,17 @@ class Session:
                                                HOST_INPUTS | HOST_OUTPUT,
                                                C.c_void_p(torch.cuda.current_stream().cuda_stream)))
         return logits
+
+    def capture_routing(self, indices: torch.Tensor | None):
+        """Diagnostic: write every layer's top-k expert ids of the following
+        forwards into `indices` (int32 device tensor [layers, rows, top_k]);
+        None turns it off."""
+        if indices is None:
+            check(lib().tf_session_capture_routing(self.handle, None, 0))
+            return
+        if indices.dtype != torch.int32 or not indices.is_cuda or indices.dim() != 3:
+            raise ValueError("capture_routing: int32 device tensor [layers, rows, top_k]")
+        check(lib().tf_session_capture_routing(self.handle, C.c_void_p(indices.data_ptr()), indices.shape[1]))
 
     def graphs(self, enable: bool):
         """Turn CUDA-graph replay of decode steps on/off (default on)."""
