@@ -265,6 +265,25 @@ int tf_moe_expert_gpu(const void* x, int64_t x_rows, int32_t hidden, const int32
                       void* out_sorted, int32_t* inverse, void* workspace, size_t workspace_bytes,
                       void* stream);
 
+/* The expert hook's computation with the outputs in the routes' own order:
+ * out [n][hidden] row i belongs to route i (token_indices[i], expert_ids[i]).
+ * Same workspace as tf_moe_expert_gpu.  For the expert-parallel layer,
+ * whose received rows go back to their ranks in the order they came; no
+ * counterpart in the reference (its hook returns expert-sorted rows and the
+ * inverse permutation). */
+int tf_moe_expert_gpu_ordered(const void* x, int64_t x_rows, int32_t hidden, const int32_t* token_indices,
+                              const int32_t* expert_ids, int64_t n, int32_t intermediate, int32_t experts,
+                              const tf_affine_weight* gate_proj, const tf_affine_weight* up_proj,
+                              const tf_affine_weight* down_proj, int act, void* out, void* workspace,
+                              size_t workspace_bytes, void* stream);
+
+/* y[i] = x[index[i] / div] for i < n: act rows of `width` (% 8 == 0); x has
+ * x_rows rows.  The routed-row gather x[order // k] of the MoE dispatch
+ * (MLXNativeGraniteMoEPrefill.h:670-684), used by the expert-parallel layer
+ * to fill its send buffer. */
+int tf_gather_rows(const void* x, int64_t x_rows, int32_t width, const int32_t* index, int32_t div, int64_t n,
+                   int act, void* y, void* stream);
+
 /* ------------------------------------------------------------------------ */
 /* attention                                                                  */
 
@@ -426,15 +445,17 @@ const char* tf_trace_phase_name(int phase);
 int tf_session_trace(tf_session* session, int enable);
 int tf_session_trace_read(tf_session* session, float* total_ms, int32_t* counts);
 
-/* Diagnostic routing capture: while `indices` is non-NULL, every forward of
- * at most max_rows rows writes each layer's top-k expert ids into it, int32
- * [layers][rows][top_k] with the rows of that call in order (for the last
- * layer of a prefill, the rows whose MoE block runs: each request's last
- * row); decode steps then run without graph replay.  NULL turns it off.
- * The counterpart of the reference's inspect / receipt diagnostics
- * (src/apple/TFETResidentSession.mm:1816-1967); tests use it to follow the
- * device's routing layer by layer. */
-int tf_session_capture_routing(tf_session* session, int32_t* indices, int64_t max_rows);
+/* Diagnostic capture: while `indices` or `hidden` is non-NULL, every forward
+ * of at most max_rows rows writes each layer's top-k expert ids (int32
+ * [layers][rows][top_k]) and output hidden states (act [layers][rows]
+ * [hidden]) into them, with the rows of that call in order; in the last
+ * layer of a prefill only each request's last row runs the MoE block, so
+ * that layer's first rows hold them.  Decode steps then run without graph
+ * replay.  Both NULL turns it off.  The counterpart of the reference's
+ * inspect / receipt diagnostics (src/apple/TFETResidentSession.mm:1816-1967);
+ * tests use it to check every layer against a CPU re-computation that starts
+ * from the device's own state. */
+int tf_session_capture(tf_session* session, int32_t* indices, void* hidden, int64_t max_rows);
 
 /* Cooperative cancellation: the next layer boundary of a running or future
  * call returns TF_ERR_CANCELLED (TFETResidentSession.h:5-11).  A call

@@ -37,6 +37,9 @@ class OracleKernels:
         y = oracle.gather_qmm(h, *[_np(t) if t.is_floating_point() else t.numpy() for t in down], e, self.a)
         return torch.from_numpy(np.asarray(y, np.float32)).to(self.act)
 
+    def gather_rows(self, x, order, k):
+        return x.index_select(0, order.long() // k).contiguous()
+
     def combine(self, y_sorted, inverse, gates, residual):
         T, K = gates.shape
         y = _np(y_sorted)[_np(inverse).astype(np.int64)].reshape(T, K, -1)

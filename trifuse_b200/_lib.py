@@ -103,7 +103,11 @@ SIGNATURES = {
     "tf_session_trace_read": [P, C.POINTER(C.c_float), C.POINTER(C.c_int32)],
     "tf_session_reset": [P],
     "tf_session_check": [P, P],
-    "tf_session_capture_routing": [P, P, C.c_int64],
+    "tf_moe_expert_gpu_ordered": [P, C.c_int64, C.c_int32, P, P, C.c_int64, C.c_int32, C.c_int32,
+                                  C.POINTER(AffineWeight), C.POINTER(AffineWeight), C.POINTER(AffineWeight), C.c_int,
+                                  P, P, C.c_size_t, P],
+    "tf_gather_rows": [P, C.c_int64, C.c_int32, P, C.c_int32, C.c_int64, C.c_int, P, P],
+    "tf_session_capture": [P, P, P, C.c_int64],
     "tf_set_wait_limit": [C.c_int64],
 }
 

@@ -520,7 +520,7 @@ int tf_moe_forward(const tf_moe_args* args, void* workspace, size_t workspace_by
 // ---------------------------------------------------------------- expert hook
 
 struct ExpertPlan {
-  int32_t *order, *xrow, *offsets, *active, *active_count;
+  int32_t *order, *inverse, *xrow, *offsets, *active, *active_count;
   void *sws, *h, *x16, *h16;
   size_t sws_bytes, used;
 };
@@ -530,6 +530,7 @@ static ExpertPlan plan_expert(void* ws, size_t ws_bytes, int64_t n, int64_t x_ro
   Carve c(ws, ws_bytes);
   ExpertPlan p;
   p.order = c.take<int32_t>((size_t)n * 4);
+  p.inverse = c.take<int32_t>((size_t)n * 4);
   p.xrow = c.take<int32_t>((size_t)n * 4);
   p.offsets = c.take<int32_t>((size_t)(experts + 1) * 4);
   p.active = c.take<int32_t>((size_t)experts * 4);
@@ -552,12 +553,13 @@ int tf_moe_expert_workspace_size(int64_t n, int64_t x_rows, int32_t hidden, int3
   return TF_OK;
 }
 
-int tf_moe_expert_gpu(const void* x, int64_t x_rows, int32_t hidden, const int32_t* token_indices,
-                      const int32_t* expert_ids, int64_t n, int experts_sorted, int32_t intermediate,
-                      int32_t experts, const tf_affine_weight* gate, const tf_affine_weight* up,
-                      const tf_affine_weight* down, int act, void* out_sorted, int32_t* inverse,
-                      void* workspace, size_t workspace_bytes, void* stream) {
-  (void)experts_sorted;  // the stable sort of sorted ids is the identity
+// ordered: out rows in the routes' own order (the down projection writes
+// slot n's row to order[n]); inverse then lives in the workspace.
+static tf_status expert_gpu(const void* x, int64_t x_rows, int32_t hidden, const int32_t* token_indices,
+                            const int32_t* expert_ids, int64_t n, int32_t intermediate, int32_t experts,
+                            const tf_affine_weight* gate, const tf_affine_weight* up,
+                            const tf_affine_weight* down, int act, void* out, int32_t* inverse, bool ordered,
+                            void* workspace, size_t workspace_bytes, void* stream) {
   TF_TRY(check_act(act));
   if (n < 0 || n > INT32_MAX || x_rows < 0 || hidden <= 0 || hidden % 64 || experts <= 0 || experts > 256)
     return set_error(TF_ERR_SHAPE, "expert hook route arrays must be parallel integer vectors");
@@ -572,10 +574,11 @@ int tf_moe_expert_gpu(const void* x, int64_t x_rows, int32_t hidden, const int32
   if (workspace_bytes < plan_expert(nullptr, 0, n, x_rows, hidden, intermediate, experts, act).used)
     return set_error(TF_ERR_INVALID_ARGUMENT, "expert hook: workspace too small");
   if (n == 0) return TF_OK;
-  if (!x || !token_indices || !expert_ids || !out_sorted || !inverse || !workspace || !aligned16(x))
+  if (!x || !token_indices || !expert_ids || !out || (!inverse && !ordered) || !workspace || !aligned16(x))
     return set_error(TF_ERR_INVALID_ARGUMENT, "expert hook: NULL or unaligned pointer");
   cudaStream_t s = st(stream);
   const ExpertPlan w = plan_expert(workspace, workspace_bytes, n, x_rows, hidden, intermediate, experts, act);
+  if (ordered) inverse = w.inverse;
   int32_t* order = w.order;
   int32_t* xrow = w.xrow;
   int32_t* offsets = w.offsets;
@@ -606,8 +609,9 @@ int tf_moe_expert_gpu(const void* x, int64_t x_rows, int32_t hidden, const int32
   d.x_stride = intermediate;
   d.x_index = nullptr;
   d.w0 = *down;
-  d.y = out_sorted;
+  d.y = out;
   d.y_stride = hidden;
+  d.y_index = ordered ? order : nullptr;
   const bool tc_up = qmm_uses_tc(p), tc_dn = qmm_uses_tc(d);
   if (tc_up) {
     TF_TRY(launch_gather_f16(x, hidden, act, xrow, 1, n, hidden, w.x16, 1, s));
@@ -626,6 +630,36 @@ int tf_moe_expert_gpu(const void* x, int64_t x_rows, int32_t hidden, const int32
     d.x16_perm = 1;
   }
   return launch_qmm(d, s);
+}
+
+int tf_moe_expert_gpu(const void* x, int64_t x_rows, int32_t hidden, const int32_t* token_indices,
+                      const int32_t* expert_ids, int64_t n, int experts_sorted, int32_t intermediate,
+                      int32_t experts, const tf_affine_weight* gate, const tf_affine_weight* up,
+                      const tf_affine_weight* down, int act, void* out_sorted, int32_t* inverse,
+                      void* workspace, size_t workspace_bytes, void* stream) {
+  (void)experts_sorted;  // the stable sort of sorted ids is the identity
+  return expert_gpu(x, x_rows, hidden, token_indices, expert_ids, n, intermediate, experts, gate, up, down, act,
+                    out_sorted, inverse, false, workspace, workspace_bytes, stream);
+}
+
+int tf_moe_expert_gpu_ordered(const void* x, int64_t x_rows, int32_t hidden, const int32_t* token_indices,
+                              const int32_t* expert_ids, int64_t n, int32_t intermediate, int32_t experts,
+                              const tf_affine_weight* gate, const tf_affine_weight* up,
+                              const tf_affine_weight* down, int act, void* out, void* workspace,
+                              size_t workspace_bytes, void* stream) {
+  return expert_gpu(x, x_rows, hidden, token_indices, expert_ids, n, intermediate, experts, gate, up, down, act,
+                    out, nullptr, true, workspace, workspace_bytes, stream);
+}
+
+int tf_gather_rows(const void* x, int64_t x_rows, int32_t width, const int32_t* index, int32_t div, int64_t n,
+                   int act, void* y, void* stream) {
+  TF_TRY(check_act(act));
+  if (n < 0 || x_rows < 0 || width <= 0 || width % 8 || div <= 0)
+    return set_error(TF_ERR_SHAPE, "gather_rows: bad geometry");
+  if (n == 0) return TF_OK;
+  if (!x || !index || !y || !aligned16(x) || !aligned16(y))
+    return set_error(TF_ERR_INVALID_ARGUMENT, "gather_rows: NULL or unaligned pointer");
+  return launch_gather_rows(x, width, index, div, n, width, act, y, st(stream));
 }
 
 // ---------------------------------------------------------------- attention

@@ -55,24 +55,25 @@ tf_status launch_combine(const void* y_sorted, const int32_t* inverse, const voi
   return check_launch("combine");
 }
 
-// Row gather in the activation dtype (16-byte vectors): the last rows of a
-// prefill's requests as a compact batch for the last layer's queries.
+// Row gather in the activation dtype (16-byte vectors): y[i] = x[idx[i] / div]
+// (the last rows of a prefill's requests as a compact batch for the last
+// layer's queries; the routed rows of an expert-parallel dispatch).
 __global__ void gather_rows_kernel(const uint4* __restrict__ x, int64_t x_stride16, const int32_t* __restrict__ idx,
-                                   int64_t n, int width16, uint4* __restrict__ y) {
+                                   int div, int64_t n, int width16, uint4* __restrict__ y) {
   const int64_t i = blockIdx.x;
   if (i >= n) return;
-  const int64_t src = idx[i];
+  const int64_t src = idx[i] / div;
   for (int c = threadIdx.x; c < width16; c += blockDim.x) y[i * width16 + c] = x[src * x_stride16 + c];
 }
 
-tf_status launch_gather_rows(const void* x, int64_t x_stride, const int32_t* idx, int64_t n, int width, int act,
-                             void* y, cudaStream_t s) {
+tf_status launch_gather_rows(const void* x, int64_t x_stride, const int32_t* idx, int div, int64_t n, int width,
+                             int act, void* y, cudaStream_t s) {
   if (n == 0) return TF_OK;
   const int eb = act_bytes(act);
   if ((width * eb) % 16 || (x_stride * eb) % 16) return set_error(TF_ERR_SHAPE, "gather_rows: width %d", width);
   if (n > 2147483647) return set_error(TF_ERR_UNSUPPORTED, "gather_rows: too many rows");
-  gather_rows_kernel<<<(unsigned)n, 128, 0, s>>>((const uint4*)x, x_stride * eb / 16, idx, n, width * eb / 16,
-                                                 (uint4*)y);
+  gather_rows_kernel<<<(unsigned)n, 128, 0, s>>>((const uint4*)x, x_stride * eb / 16, idx, div, n,
+                                                 width * eb / 16, (uint4*)y);
   return check_launch("gather_rows");
 }
 

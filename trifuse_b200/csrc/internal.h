@@ -148,6 +148,9 @@ struct QmmProblem {
   // output
   void* y = nullptr;
   int64_t y_stride = 0;
+  // EPI_PLAIN: output row of slot n is y_index[n] (NULL: n), so a grouped
+  // problem can write its rows back in the caller's route order.
+  const int32_t* y_index = nullptr;
   const void* residual = nullptr;  // EPI_RESIDUAL, indexed like y
   int64_t residual_stride = 0;
   // Tensor-core operand: an f16 copy of the activations with contiguous rows
@@ -171,8 +174,8 @@ struct QmmProblem {
 };
 // Bytes of fp32 partials the tensor-core split schedule needs on this device.
 size_t qmm_split_partial_bytes();
-// Counters a split QMM over `routes` grouped routes or dense rows can use.
-constexpr int64_t kQmmSplitCounters = 8192;
+// Counters of the split schedule in a workspace (four per tile).
+constexpr int64_t kQmmSplitCounters = 16384;
 // Path launch_qmm would take for this problem (true = tensor cores).
 bool qmm_uses_tc(const QmmProblem& p);
 // f16 copy of n bf16 values (rows of 2048), optionally in the x16_perm order.
@@ -195,9 +198,9 @@ int read_embed_error(bool clear);
 // tokens[r] = all(isfinite(logits[r])) ? argmax (lowest index on ties) : -1.
 tf_status launch_greedy(const float* logits, int64_t rows, int64_t vocab, int64_t* tokens, cudaStream_t s);
 
-// y[i][:] = x[idx[i]][:] for i < n (act rows of `width`, width % 8 == 0).
-tf_status launch_gather_rows(const void* x, int64_t x_stride, const int32_t* idx, int64_t n, int width, int act,
-                             void* y, cudaStream_t s);
+// y[i][:] = x[idx[i] / div][:] for i < n (act rows of `width`, width % 8 == 0).
+tf_status launch_gather_rows(const void* x, int64_t x_stride, const int32_t* idx, int div, int64_t n, int width,
+                             int act, void* y, cudaStream_t s);
 
 // ---------------------------------------------------------------- combine
 tf_status launch_combine(const void* y_sorted, const int32_t* inverse, const void* gates,

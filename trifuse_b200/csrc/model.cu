@@ -164,10 +164,12 @@ struct tf_session {
   // completion point); every call but reset is refused while it is set.
   bool invalid = false;
   bool tracing = false;
-  // Diagnostic routing capture (tf_session_capture_routing): each layer's
-  // top-k expert ids of a forward land at route_capture + layer * rows * k.
+  // Diagnostic capture (tf_session_capture): each layer's top-k expert ids
+  // and output hidden states of a forward land at route_capture + layer *
+  // rows * k and hidden_capture + layer * rows * hidden.
   int32_t* route_capture = nullptr;
-  int64_t route_capture_rows = 0;
+  void* hidden_capture = nullptr;
+  int64_t capture_rows = 0;
   SessionTracer tracer;
   // Decode steps as CUDA graphs, one per (batch, with logits, attention
   // splits of 256 keys, QMM path): the first step of a shape runs eagerly,
@@ -645,7 +647,7 @@ tf_status forward_rows(tf_session* s, int64_t rows, bool req_ident, int max_len,
     if (lq && cache_only) break;
     const void* resid = s->h0;
     if (lq) {
-      TF_TRY(launch_gather_rows(s->h0, H, last, nlast, H, c.act, s->hc, st));
+      TF_TRY(launch_gather_rows(s->h0, H, last, 1, nlast, H, c.act, s->hc, st));
       resid = s->hc;
     }
     QmmProblem o;
@@ -681,9 +683,12 @@ tf_status forward_rows(tf_session* s, int64_t rows, bool req_ident, int max_len,
     ma.gate_proj = L.gate;
     ma.up_proj = L.up;
     ma.down_proj = L.down;
-    if (s->route_capture && rows <= s->route_capture_rows)
-      ma.indices = s->route_capture + (size_t)l * rows * c.top_k;
+    const bool capture = rows <= s->capture_rows;
+    if (capture && s->route_capture) ma.indices = s->route_capture + (size_t)l * rows * c.top_k;
     TF_TRY(moe_run(&ma, s->moe_ws, s->moe_ws_bytes, st, /*counters_zero=*/true));
+    if (capture && s->hidden_capture)
+      TF_CUDA(cudaMemcpyAsync(static_cast<char*>(s->hidden_capture) + (size_t)l * rows * H * act_bytes(c.act), s->h0,
+                              (size_t)n * H * act_bytes(c.act), cudaMemcpyDeviceToDevice, st));
   }
   return TF_OK;
 }
@@ -747,7 +752,7 @@ tf_status decode_step(tf_session* s, const int64_t* token_ids, const int32_t* po
   TF_CUDA(cudaMemcpyAsync(s->ids, token_ids, (size_t)batch * 8,
                           (flags & TF_HOST_INPUTS) ? cudaMemcpyHostToDevice : cudaMemcpyDeviceToDevice, st));
   TF_CUDA(cudaMemcpyAsync(s->pos, pos.data(), (size_t)batch * 4, cudaMemcpyHostToDevice, st));
-  if (s->graphs_on && !s->tracing && !s->route_capture) {
+  if (s->graphs_on && !s->tracing && !s->route_capture && !s->hidden_capture) {
     const int splits = (max_len + 255) / 256;
     tf_session::DecodeGraph& gr = s->graphs[std::make_tuple(batch, head ? 1 : 0, splits, g_qmm_path)];
     if (gr.exec || gr.eager_runs > 0) {
@@ -977,11 +982,12 @@ int tf_session_graphs(tf_session* s, int enable) {
   return TF_OK;
 }
 
-int tf_session_capture_routing(tf_session* s, int32_t* indices, int64_t max_rows) {
+int tf_session_capture(tf_session* s, int32_t* indices, void* hidden, int64_t max_rows) {
   if (!s) return set_error(TF_ERR_INVALID_ARGUMENT, "session is NULL");
-  if (indices && max_rows <= 0) return set_error(TF_ERR_INVALID_ARGUMENT, "capture: max_rows must be positive");
+  if ((indices || hidden) && max_rows <= 0) return set_error(TF_ERR_INVALID_ARGUMENT, "capture: max_rows must be positive");
   s->route_capture = indices;
-  s->route_capture_rows = indices ? max_rows : 0;
+  s->hidden_capture = hidden;
+  s->capture_rows = (indices || hidden) ? max_rows : 0;
   return TF_OK;
 }
 

@@ -19,6 +19,11 @@
 // load elsewhere, so this entry must not be used across one.  With lazy
 // module loading the first call per device and batch shape may load kernel
 // modules (the driver allocates for them); a warm-up call, or
+// CUDA_MODULE_LOADING=EAGER, moves that out of the caller's critical path.  The address is kept for the
+// life of the process: after a device reset the module (and the array) may
+// load elsewhere, so this entry must not be used across one.  With lazy
+// module loading the first call per device and batch shape may load kernel
+// modules (the driver allocates for them); a warm-up call, or
 // CUDA_MODULE_LOADING=EAGER, moves that out of the caller's critical path.
 //
 // Every call shares the one buffer and leaves its contents behind; nothing

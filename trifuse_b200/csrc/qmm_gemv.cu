@@ -52,6 +52,7 @@ struct GemvArgs {
   int experts;
   void* y;
   int64_t y_stride;
+  const int32_t* y_index;
   const void* residual;
   int64_t residual_stride;
 };
@@ -189,7 +190,8 @@ __global__ void __launch_bounds__(kGemvWarps * 32) qmm_gemv_kernel(GemvArgs a) {
               const float res = to_f(((const T*)a.residual)[slot * a.residual_stride + row]);
               *yp = from_f<T>(res + round_act<T>(acc[0][tt]));
             } else {
-              *yp = from_f<T>(acc[0][tt]);
+              const int64_t orow = a.y_index ? (int64_t)a.y_index[slot] : slot;
+              ((T*)a.y)[orow * a.y_stride + row] = from_f<T>(acc[0][tt]);
             }
           }
         }
@@ -283,6 +285,7 @@ tf_status launch_qmm_gemv(const QmmProblem& p, cudaStream_t s) {
   a.experts = p.w0.experts > 0 ? p.w0.experts : 1;
   a.y = p.y;
   a.y_stride = p.y_stride;
+  a.y_index = p.epilogue == EPI_PLAIN ? p.y_index : nullptr;
   a.residual = p.residual;
   a.residual_stride = p.residual_stride;
   if (p.act == TF_DTYPE_F16) return qmm_by_mode<__half>(a, p.mode, p.epilogue, s);

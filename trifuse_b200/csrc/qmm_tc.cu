@@ -108,12 +108,13 @@ constexpr long long kDrainCycles = 2000000000LL;
 constexpr uint32_t kSuspendNs = 1000000;
 
 // A block's work item: chunks [kc0, kc1) (a chunk is kSK k-steps) of one
-// tile (expert e, token slots s0 .. s0 + cnt, row block rb).  `whole`
-// segments cover every chunk of the tile; the others are parts of a tile
+// tile (expert e, token slots s0 .. s0 + cnt, row block rb).  Segments with
+// slot < 0 cover every chunk of the tile; the others are parts of a tile
 // split across consecutive blocks (split schedule) and meet in the fixup.
 struct Seg {
   int e, s0, cnt, rb;
-  int kc0, kc1, tile, whole;
+  int kc0, kc1, tile;
+  int slot;  // -1: whole tile; else this block's partial slot (2 block + 0 first tile / 1 last tile)
 };
 
 struct Params {
@@ -125,12 +126,14 @@ struct Params {
   const int32_t* active;
   const int32_t* active_count;
   int grouped;
+  int experts;  // grouped: experts of the stacked weight (offsets has experts + 1 entries)
   int row_blocks;
   int out;  // rows per expert (per matrix)
   int in;
   int64_t n;  // slots (= activation rows)
   void* y;
   int64_t y_stride;
+  const int32_t* y_index;  // EPI_PLAIN output row of each slot (NULL: the slot)
   int y_f16;
   const void* residual;
   int64_t residual_stride;
@@ -442,7 +445,8 @@ __device__ __forceinline__ void epi_apply(const Params& p, const Seg& sg, int q,
           } else if (EPI == EPI_RESIDUAL) {
             static_cast<T*>(p.y)[slot * p.y_stride + f] = from_f<T>(res[i] + round_act<T>(vi));
           } else {
-            static_cast<T*>(p.y)[slot * p.y_stride + f] = from_f<T>(vi);
+            const int64_t orow = p.y_index ? (int64_t)p.y_index[slot] : slot;
+            static_cast<T*>(p.y)[orow * p.y_stride + f] = from_f<T>(vi);
           }
         }
       }
@@ -517,10 +521,25 @@ __global__ void __launch_bounds__(Roles<G * H, BPS>::kThreads, BPS)
                  "r"(kTmemCols));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
   }
+  if (warp == kLoadWarp && lane == 0) {
+    // Fetch the tensor maps while the segment table is built.
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&p.tm_q0)) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&p.tm_s0)) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&p.tm_b0)) : "memory");
+    if (EPI == EPI_SWIGLU) {
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&p.tm_q1)) : "memory");
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&p.tm_s1)) : "memory");
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&p.tm_b1)) : "memory");
+    }
+  }
+  if (warp == kActWarp && lane == 0)
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&p.tm_x)) : "memory");
   if (warp == 0) {
-    // Segment table.  Grouped problems: the active experts' token blocks
-    // (prefix sums in a table that lives in the code ring until the loaders
-    // start), then every tile found by binary search, one lane per segment.
+    // Segment table.  Grouped problems: every expert's token blocks from one
+    // round of independent offset loads (prefix sums in a table that lives
+    // in the code ring until the loaders start; experts without routes get
+    // no blocks), then every tile found by binary search, one lane per
+    // segment.
     int* ex_id = reinterpret_cast<int*>(ring_p);
     int* ex_lo = ex_id + kMaxExperts;
     int* ex_hi = ex_lo + kMaxExperts;
@@ -528,16 +547,25 @@ __global__ void __launch_bounds__(Roles<G * H, BPS>::kThreads, BPS)
     int na = 0;
     int tblocks;
     if (p.grouped) {
-      na = min(*p.active_count, kMaxExperts);
+      na = p.experts;
+      int lo_r[kMaxExperts / 32], hi_r[kMaxExperts / 32];
+#pragma unroll
+      for (int r = 0; r < kMaxExperts / 32; ++r) {
+        const int i = r * 32 + lane;
+        lo_r[r] = i < na ? p.offsets[i] : 0;
+        hi_r[r] = i < na ? p.offsets[i + 1] : 0;
+      }
       int run = 0;
-      for (int c0 = 0; c0 < na; c0 += 32) {
+#pragma unroll
+      for (int r = 0; r < kMaxExperts / 32; ++r) {
+        const int c0 = r * 32;
+        if (c0 >= na) break;
         const int i = c0 + lane;
         int nb = 0;
         if (i < na) {
-          const int ex = p.active[i];
-          const int lo = p.offsets[ex], hi = p.offsets[ex + 1];
+          const int lo = lo_r[r], hi = hi_r[r];
           nb = (hi - lo + NT - 1) / NT;
-          ex_id[i] = ex;
+          ex_id[i] = i;
           ex_lo[i] = lo;
           ex_hi[i] = hi;
         }
@@ -598,10 +626,19 @@ __global__ void __launch_bounds__(Roles<G * H, BPS>::kThreads, BPS)
       }
       s.kc0 = p.split && t == t_first ? u0 - t * cpt : 0;
       s.kc1 = p.split && t == t_last ? u1 - t * cpt : cpt;
-      s.whole = s.kc0 == 0 && s.kc1 == cpt;
+      s.slot = (s.kc0 == 0 && s.kc1 == cpt) ? -1 : 2 * (int)blockIdx.x + (t == t_first ? 0 : 1);
       segs[j] = s;
     }
+    __syncwarp();
     if (lane == 0) {
+      // A block's split tiles are its first and last; run the last one
+      // first too, so that their fixups happen early and the block ends on
+      // whole tiles.
+      if (nsegs >= 2 && segs[nsegs - 1].slot >= 0) {
+        const Seg last = segs[nsegs - 1];
+        for (int j = nsegs - 1; j > 0; --j) segs[j] = segs[j - 1];
+        segs[0] = last;
+      }
       *nsegs_s = nsegs;
       *units_s = U;
     }
@@ -799,7 +836,7 @@ __global__ void __launch_bounds__(Roles<G * H, BPS>::kThreads, BPS)
       tc_fence_after();
       const int n_mma = (sg.cnt + 15) / 16 * 16;
       const uint32_t taddr = tmem + ((uint32_t)(wq * 32) << 16) + (uint32_t)(buf * NT);
-      if (sg.whole) {
+      if (sg.slot < 0) {
         for (int c0 = 0; c0 < n_mma; c0 += 16) {
           float v[16];
           tmem_ld16(taddr + c0, v);
@@ -810,12 +847,12 @@ __global__ void __launch_bounds__(Roles<G * H, BPS>::kThreads, BPS)
         if (lane == 0) mbar_arrive(&acc_empty[buf]);
         continue;
       }
-      // Part of a split tile: store this block's fp32 partial (slot 0 for
-      // the block's first segment, 1 for its last), release the accumulator,
-      // then count this warp's arrival.  The warp that arrives last sums the
-      // parts of all 128 rows in k order (block order) from the partials and
-      // runs the epilogue; nobody waits for anybody.
-      float* mine = p.partials + ((size_t)(2 * blockIdx.x + (j == 0 ? 0 : 1)) * kM + q) * NT;
+      // Part of a split tile: store this block's fp32 partial of the warp's
+      // 32 rows, release the accumulator, then count the arrival on this
+      // row quarter's counter.  The warp that arrives last for a quarter sums
+      // that quarter's parts in k order (block order) from the partials and
+      // runs its epilogue; nobody waits for anybody.
+      float* mine = p.partials + ((size_t)sg.slot * kM + q) * NT;
 #pragma unroll 1
       for (int c0 = 0; c0 < n_mma; c0 += 16) {
         float v[16];
@@ -833,14 +870,14 @@ __global__ void __launch_bounds__(Roles<G * H, BPS>::kThreads, BPS)
       const int b_hi = unit_owner((sg.tile + 1) * cpt - 1, U, grid);
       int parts = 0;  // blocks holding a part (with fewer units than blocks some runs are empty)
       for (int b = b_lo; b <= b_hi; ++b) parts += unit_start(b + 1, U, grid) > unit_start(b, U, grid);
+      int* counter = &p.counters[4 * sg.tile + wq];
       int seen = 0;
-      if (lane == 0) seen = atomicAdd(&p.counters[sg.tile], 1);
+      if (lane == 0) seen = atomicAdd(counter, 1);
       seen = __shfl_sync(0xffffffffu, seen, 0);
-      if (seen != kEpiWarps * parts - 1) continue;
+      if (seen != parts - 1) continue;
       __threadfence();
-#pragma unroll 1
-      for (int qq = 0; qq < 4; ++qq) {
-        const int qr = qq * 32 + lane;
+      {
+        const int qr = q;
 #pragma unroll 1
         for (int c0 = 0; c0 < n_mma; c0 += 16) {
           float v[16];
@@ -864,7 +901,7 @@ __global__ void __launch_bounds__(Roles<G * H, BPS>::kThreads, BPS)
           epi_apply<T, EPI>(p, sg, qr, c0, v);
         }
       }
-      if (lane == 0) p.counters[sg.tile] = 0;  // left at zero for the next launch
+      if (lane == 0) *counter = 0;  // left at zero for the next launch
     }
   }
   tc_fence_before();
@@ -965,7 +1002,10 @@ tf_status launch_cfg(tc::Params& p, const QmmProblem& q, int64_t tiles_bound, cu
   // Split schedule: every block slot takes an equal run of (tile, chunk)
   // units.  It needs a partial slot pair per block, a counter per tile, and
   // a segment table that holds a block's tiles.
-  p.split = q.partials && q.counters && tiles_bound <= q.counter_cap && tiles_bound * 16 * slots < 2147483647LL &&
+  // Only grouped (expert) problems split: a dense problem has too few tiles
+  // for the units of a block to keep its tiles in one or two parts.
+  p.split = p.grouped && q.partials && q.counters && 4 * tiles_bound <= q.counter_cap &&
+            tiles_bound * 16 * slots < 2147483647LL &&
             (size_t)2 * slots * tc::kM * NT * sizeof(float) <= q.partial_bytes &&
             tiles_bound <= (int64_t)(tc::kMaxSegs - 2) * slots;
   if (p.split) {
@@ -989,11 +1029,10 @@ tf_status launch_nt(tc::Params& p, const QmmProblem& q, int nt, int64_t tiles_bo
     // <NT, KS, PK, SA, SB, G, H, BPS>: expert tiles of a decode batch (many
     // tiles, few tokens) run two blocks per SM (256 TMEM columns each) with
     // two dequant groups of 4 warps; dense projections of a decode batch
-    // (few tiles) one block per SM with four groups and 4 A stages; prefill
-    // tiles one block with two groups of 8 warps (two threads per row and
-    // k-step).
+    // (few tiles) and prefill tiles one block per SM with two groups of 8
+    // warps (two threads per row and k-step), 4 and 2 A stages.
     case 32: return launch_cfg<T, EPI, PERM, 32, 2, 4, 3, 6, 2, 1, 2>(p, q, tiles_bound, s);
-    case 64: return launch_cfg<T, EPI, PERM, 64, 2, 4, 4, 4, 4, 1, 1>(p, q, tiles_bound, s);
+    case 64: return launch_cfg<T, EPI, PERM, 64, 2, 4, 4, 4, 2, 2, 1>(p, q, tiles_bound, s);
     default: return launch_cfg<T, EPI, PERM, 192, 2, 4, 2, 3, 2, 2, 1>(p, q, tiles_bound, s);
   }
 }
@@ -1035,12 +1074,14 @@ tf_status launch_qmm_tc(const QmmProblem& q, cudaStream_t s) {
   p.active = q.active;
   p.active_count = q.active_count;
   p.grouped = q.mode == QMM_GROUPED;
+  p.experts = experts;
   p.row_blocks = (out + tile_rows - 1) / tile_rows;
   p.out = out;
   p.in = in;
   p.n = q.n;
   p.y = q.y;
   p.y_stride = q.y_stride;
+  p.y_index = q.epilogue == EPI_PLAIN ? q.y_index : nullptr;
   p.y_f16 = q.y_f16;
   p.residual = q.residual;
   p.residual_stride = q.residual_stride;

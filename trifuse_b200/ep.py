@@ -46,13 +46,19 @@ class CudaKernels:
         return ops.moe_route_sort(idx, experts)
 
     def experts(self, rows, expert_ids, gate, up, down):
+        """Expert outputs in the received order (the down projection writes
+        each row back to its route's position; no un-permute)."""
         from . import ops
         n = rows.shape[0]
         if n == 0:
             return torch.empty_like(rows)
         tok = torch.arange(n, dtype=torch.int32, device=rows.device)
-        out, inverse = ops.expert_gpu(rows, tok, expert_ids.to(torch.int32), False, gate, up, down)
-        return out.index_select(0, inverse.long())
+        return ops.expert_gpu_ordered(rows, tok, expert_ids.to(torch.int32), gate, up, down, check_ranges=False)
+
+    def gather_rows(self, x, order, k):
+        """Rows x[order // k] in route-sort order (the dispatch send buffer)."""
+        from . import ops
+        return ops.gather_rows(x, order.to(torch.int32), k)
 
     def combine(self, y_sorted, inverse, gates, residual):
         from . import ops
@@ -85,16 +91,18 @@ class ExpertParallelMoE:
         dev = x.device
         idx, gates = self.k.route(x, self.router, K, E)
         order, inverse, offsets = self.k.route_sort(idx, E)
-        order = order.long()
         # rows bound for each rank: routes of experts [r*L, (r+1)*L)
         bounds = offsets.long()[torch.arange(0, E + 1, L, device=offsets.device)]
         send_counts = (bounds[1:] - bounds[:-1]).to(torch.int64)
         recv_counts = torch.empty_like(send_counts)
         dist.all_to_all_single(recv_counts, send_counts, group=self.group)
-        send_sizes, recv_sizes = send_counts.tolist(), recv_counts.tolist()
-        # dispatch token rows and their destination-local expert ids
-        sel = idx.reshape(-1).long().index_select(0, order)
-        send_rows = x.index_select(0, order // K).contiguous()
+        # the one host synchronization of the layer: NCCL takes host split sizes
+        sizes = torch.stack([send_counts, recv_counts]).cpu()
+        send_sizes, recv_sizes = sizes[0].tolist(), sizes[1].tolist()
+        # dispatch token rows (gathered straight into the send buffer) and
+        # their destination-local expert ids
+        sel = idx.reshape(-1).index_select(0, order.long())
+        send_rows = self.k.gather_rows(x, order, K)
         send_eid = (sel % L).to(torch.int32)
         recv_rows = torch.empty((sum(recv_sizes), H), dtype=x.dtype, device=dev)
         recv_eid = torch.empty(sum(recv_sizes), dtype=torch.int32, device=dev)

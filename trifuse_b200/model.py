@@ -237,16 +237,23 @@ class Session:
                                                C.c_void_p(torch.cuda.current_stream().cuda_stream)))
         return logits
 
-    def capture_routing(self, indices: torch.Tensor | None):
-        """Diagnostic: write every layer's top-k expert ids of the following
-        forwards into `indices` (int32 device tensor [layers, rows, top_k]);
-        None turns it off."""
-        if indices is None:
-            check(lib().tf_session_capture_routing(self.handle, None, 0))
-            return
-        if indices.dtype != torch.int32 or not indices.is_cuda or indices.dim() != 3:
-            raise ValueError("capture_routing: int32 device tensor [layers, rows, top_k]")
-        check(lib().tf_session_capture_routing(self.handle, C.c_void_p(indices.data_ptr()), indices.shape[1]))
+    def capture(self, indices: torch.Tensor | None, hidden: torch.Tensor | None = None):
+        """Diagnostic: write every layer's top-k expert ids (int32 device
+        tensor [layers, rows, top_k]) and output hidden states (act device
+        tensor [layers, rows, hidden]) of the following forwards; both None
+        turns it off."""
+        rows = None
+        for t, dt in ((indices, torch.int32), (hidden, None)):
+            if t is None:
+                continue
+            if not t.is_cuda or t.dim() != 3 or (dt is not None and t.dtype != dt):
+                raise ValueError("capture: device tensors [layers, rows, ...] (int32 indices)")
+            if rows is not None and t.shape[1] != rows:
+                raise ValueError("capture: indices and hidden disagree on rows")
+            rows = t.shape[1]
+        check(lib().tf_session_capture(self.handle, C.c_void_p(indices.data_ptr()) if indices is not None else None,
+                                       C.c_void_p(hidden.data_ptr()) if hidden is not None else None,
+                                       rows or 0))
 
     def graphs(self, enable: bool):
         """Turn CUDA-graph replay of decode steps on/off (default on)."""

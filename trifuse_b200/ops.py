@@ -345,6 +345,48 @@ def expert_gpu(x: Tensor, token_indices: Tensor, expert_ids: Tensor, experts_sor
     return out, inverse
 
 
+def expert_gpu_ordered(x: Tensor, token_indices: Tensor, expert_ids: Tensor, gate, up, down,
+                       check_ranges: bool = True) -> Tensor:
+    """The expert hook's computation with the output rows in the routes' own
+    order (row i for route i); no inverse permutation.  check_ranges=False
+    skips the host-side index checks (one device-to-host read each) for
+    callers whose indices are valid by construction."""
+    if (token_indices.ndim != 1 or expert_ids.ndim != 1 or token_indices.shape != expert_ids.shape
+            or token_indices.dtype != torch.int32 or expert_ids.dtype != torch.int32):
+        raise ValueError("expert hook route arrays must be parallel integer vectors")
+    _cuda(x, token_indices, expert_ids)
+    H = x.shape[-1]
+    xc = x.contiguous().reshape(-1, H)
+    g, u, d = affine_desc(*gate), affine_desc(*up), affine_desc(*down)
+    if check_ranges:
+        _check_range(expert_ids, g.experts, "expert index out of range")
+        _check_range(token_indices, xc.shape[0], "token index out of range")
+    n = token_indices.numel()
+    out = torch.empty((n, H), dtype=x.dtype, device=x.device)
+    nb = C.c_size_t()
+    check(lib().tf_moe_expert_workspace_size(n, xc.shape[0], H, g.out_features, g.experts, _act(x),
+                                             C.byref(nb)))
+    ws = _ws(nb.value, x.device)
+    check(lib().tf_moe_expert_gpu_ordered(_ptr(xc), xc.shape[0], H, _ptr(token_indices), _ptr(expert_ids), n,
+                                          g.out_features, g.experts, C.byref(g), C.byref(u), C.byref(d),
+                                          _act(x), _ptr(out), _ptr(ws), nb.value, _stream()))
+    return out
+
+
+def gather_rows(x: Tensor, index: Tensor, div: int = 1) -> Tensor:
+    """y[i] = x[index[i] // div] (rows of the activation dtype); index int32
+    on the device, in range by the caller's construction."""
+    _cuda(x, index)
+    if index.dtype != torch.int32 or index.ndim != 1:
+        raise ValueError("gather_rows: int32 index vector")
+    H = x.shape[-1]
+    xc = x.contiguous().reshape(-1, H)
+    n = index.numel()
+    y = torch.empty((n, H), dtype=x.dtype, device=x.device)
+    check(lib().tf_gather_rows(_ptr(xc), xc.shape[0], H, _ptr(index), int(div), n, _act(x), _ptr(y), _stream()))
+    return y
+
+
 def rms_norm(x: Tensor, weight: Tensor, eps: float) -> Tensor:
     """``fast::rms_norm`` as used by the adapter (MLXNativeGraniteMoEPrefill.h:434)."""
     _cuda(x, weight)
