@@ -325,6 +325,71 @@ def test_long_prefill_tiled_attention_matches_oracle():
         model.close()
 
 
+def test_prefill_attention_blocks_layer_by_layer():
+    """Two requests in one prefill call: request 0 continues at position 100
+    (its 128-row query blocks straddle the 128-key tiles) with 300 rows,
+    request 1 starts fresh with 77 rows (one partial block).  Every layer's
+    output rows are recomputed by the oracle from the device's own input to
+    that layer and its routing (teacher forcing), with the caches rebuilt the
+    same way from the first call, and must agree within the layer tolerance;
+    this isolates the prefill attention from routing flips."""
+    import dataclasses
+
+    from trifuse_b200.model import Model, Session
+    from trifuse_b200.quant import synthetic_olmoe
+    cap = 512
+    cfg = dataclasses.replace(tiny_cfg(), capacity=cap)
+    w = synthetic_olmoe(cfg, seed=23, device="cuda")
+    ow = oracle_weights(w, cfg)
+    ocfg = oracle.OLMoEConfig(layers=cfg.layers, hidden=cfg.hidden, heads=cfg.heads, head_dim=cfg.head_dim,
+                              intermediate=cfg.intermediate, vocab=cfg.vocab, experts=cfg.experts,
+                              top_k=cfg.top_k, capacity=cap, act="f16")
+    model = Model(cfg, w)
+    sess = Session(model, max_batch=2, capacity=cap, max_prefill_tokens=cap)
+    rng = np.random.default_rng(71)
+    first = rng.integers(0, cfg.vocab, size=100)
+    prompts = [rng.integers(0, cfg.vocab, size=300), rng.integers(0, cfg.vocab, size=77)]
+    L, H, K = cfg.layers, cfg.hidden, cfg.top_k
+
+    def captured(ids_list, reqs):
+        rows = sum(len(x) for x in ids_list)
+        routes = torch.full((L, rows, K), -1, dtype=torch.int32, device="cuda")
+        hidden = torch.zeros((L, rows, H), dtype=torch.float16, device="cuda")
+        sess.capture(routes, hidden)
+        sess.prefill(reqs, [torch.from_numpy(x) for x in ids_list])
+        sess.capture(None)
+        torch.cuda.synchronize()
+        return host(routes), host(hidden)
+
+    try:
+        r1, h1 = captured([first], [0])
+        r2, h2 = captured(prompts, [0, 1])
+    finally:
+        sess.close()
+        model.close()
+    caches = [([np.zeros((cfg.heads, cap, cfg.head_dim), np.float32) for _ in range(L)],
+               [np.zeros((cfg.heads, cap, cfg.head_dim), np.float32) for _ in range(L)]) for _ in range(2)]
+
+    def run(ids, routes, hidden, req, start, row0):
+        """Teacher-forced layers of one request's rows [row0, row0 + n) of a
+        captured call; checks them when `hidden` rows are compared."""
+        n = len(ids)
+        pos = np.arange(start, start + n)
+        h = oracle.affine_embedding(ids, *ow["embed"], "f16")
+        for l in range(L):
+            last = l == L - 1
+            forced = routes[l][row0:row0 + n] if not last else None
+            out = oracle.layer_forward(h, ow["layers"][l], ocfg, caches[req][0][l], caches[req][1][l], pos,
+                                       forced=forced, last_row_only=last)
+            if not last:
+                assert_close(out, hidden[l][row0:row0 + n], ulp_act="f16")
+                h = hidden[l][row0:row0 + n]
+
+    run(first, r1, h1, 0, 0, 0)
+    run(prompts[0], r2, h2, 0, 100, 0)
+    run(prompts[1], r2, h2, 1, 0, 300)
+
+
 def test_decode_graph_replay_matches_eager():
     """Decode steps replayed from CUDA graphs give the logits of eager steps
     bit for bit, across a KV length of 256 (a new attention split, so a new

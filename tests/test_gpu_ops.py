@@ -33,8 +33,13 @@ def test_rms_norm_bit_exact(ops, act, width):
 
 
 @pytest.mark.parametrize("act,dense,H,T", [("bf16", True, 2048, 32), ("f16", False, 2048, 64),
-                                             ("bf16", False, 256, 9), ("f16", True, 512, 5)])
+                                             ("bf16", False, 256, 9), ("f16", True, 512, 5),
+                                             ("bf16", False, 2048, 300), ("f16", False, 2048, 2051),
+                                             ("bf16", True, 1024, 4099), ("bf16", False, 256, 2500)])
 def test_router_bit_exact(ops, act, dense, H, T):
+    """Every router launch shape (cluster per token up to 256 tokens, one
+    token per block up to 2048, sixteen per block on packed fp32 pairs
+    beyond, ragged last block) gives the oracle's logits bit for bit."""
     rng = np.random.default_rng(2)
     E, K = 64, 8
     x = oracle.to_act(rng.standard_normal((T, H)).astype(np.float32), act)

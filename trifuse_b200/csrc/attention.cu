@@ -247,212 +247,6 @@ __global__ void __launch_bounds__(kHeadDim)
 }
 
 // ---------------------------------------------------------------------------
-// Prefill: a block of up to 64 consecutive query rows of one request at
-// positions pos0.. attends keys 0..pos of its own request (causal), tiled
-// FlashAttention-style: K/V tiles of 64 keys stream through shared memory
-// (cp.async, double-buffered), S = Q K^T and O += P V run on the tensor
-// cores (mma.sync m16n8k16, f16 operands, f32 accumulation) with an online
-// softmax in f32; P is rounded to f16 for the second product.  4 warps x 16
-// query rows; tiles are [rows][256 B] with 16-byte chunks XOR-swizzled so
-// ldmatrix reads are conflict-free.  Key rows past the block's last query
-// position are zero-filled (never read from the cache).
-
-namespace {
-
-constexpr int kQB = 64, kKB = 64, kPrefillThreads = 128;
-constexpr int kTile = kKB * kHeadDim * 2;  // 16 KB
-constexpr int kPrefillSmem = 5 * kTile;    // Q, K x 2, V x 2
-
-__device__ __forceinline__ uint32_t sm_u32(const void* p) {
-  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-__device__ __forceinline__ int swz(int r, int c) { return r * 256 + (((c & 8) | ((c ^ r) & 7)) << 4); }
-__device__ __forceinline__ void ldsm4(uint32_t a, uint32_t* r) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
-               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
-               : "r"(a));
-}
-__device__ __forceinline__ void ldsm4_t(uint32_t a, uint32_t* r) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
-               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
-               : "r"(a));
-}
-__device__ __forceinline__ void mma16816(float* c, const uint32_t* a, uint32_t b0, uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-      "{%0,%1,%2,%3};"
-      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
-      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-}
-// 16-byte async copy; src_bytes 0 zero-fills the destination.
-__device__ __forceinline__ void cp16(uint32_t dst, const void* src, int src_bytes) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
-}
-__device__ __forceinline__ uint32_t pack_h2(float lo, float hi) {
-  const __half2 h = __floats2half2_rn(lo, hi);
-  return *reinterpret_cast<const uint32_t*>(&h);
-}
-
-}  // namespace
-
-template <typename T>
-__global__ void __launch_bounds__(kPrefillThreads)
-    attn_prefill_kernel(const T* __restrict__ q, int heads, const int4* __restrict__ blocks,
-                        const __half* __restrict__ k_cache, const __half* __restrict__ v_cache, int cap,
-                        float scale, T* __restrict__ out) {
-  extern __shared__ __align__(128) uint8_t smp[];
-  uint8_t* sq = smp;
-  uint8_t* sk = smp + kTile;
-  uint8_t* sv = smp + 3 * kTile;
-  const int4 blk = blocks[blockIdx.x];
-  const int row0 = blk.x, nrows = blk.y, rq = blk.z, pos0 = blk.w;
-  const int h = blockIdx.y;
-  const int W = heads * kHeadDim;
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int kend = pos0 + nrows;  // keys [0, kend) are attended by some row of the block
-  const int ntiles = (kend + kKB - 1) / kKB;
-  const int64_t head_base = ((int64_t)rq * heads + h) * cap * kHeadDim;
-  const __half* kb = k_cache + head_base;
-  const __half* vb = v_cache + head_base;
-
-  auto load_tile = [&](int t, int buf) {
-    for (int i = tid; i < kKB * 16; i += kPrefillThreads) {
-      const int r = i >> 4, c = i & 15, key = t * kKB + r;
-      const bool valid = key < kend;
-      const int64_t off = (int64_t)(valid ? key : 0) * kHeadDim + 8 * c;
-      cp16(sm_u32(sk + buf * kTile + swz(r, c)), kb + off, valid ? 16 : 0);
-      cp16(sm_u32(sv + buf * kTile + swz(r, c)), vb + off, valid ? 16 : 0);
-    }
-    asm volatile("cp.async.commit_group;" ::: "memory");
-  };
-  load_tile(0, 0);
-  // Q tile -> f16 in shared memory (rows past the block are zero)
-  for (int i = tid; i < kQB * 16; i += kPrefillThreads) {
-    const int r = i >> 4, c = i & 15;
-    uint4 v = make_uint4(0, 0, 0, 0);
-    if (r < nrows) {
-      float f[8];
-      unpack8<T>(ld_v4(q + (int64_t)(row0 + r) * W + h * kHeadDim + 8 * c), f);
-      v = pack8<__half>(f);
-    }
-    *reinterpret_cast<uint4*>(sq + swz(r, c)) = v;
-  }
-  __syncthreads();
-  uint32_t qa[8][4];
-#pragma unroll
-  for (int kd = 0; kd < 8; ++kd)
-    ldsm4(sm_u32(sq + swz(warp * 16 + (lane & 7) + ((lane >> 3) & 1) * 8, 2 * kd + (lane >> 4))), qa[kd]);
-
-  const int ra = warp * 16 + (lane >> 2), rb = ra + 8;  // block rows of accumulator halves
-  const int pa = pos0 + ra, pb = pos0 + rb;
-  float o[16][4];
-#pragma unroll
-  for (int i = 0; i < 16; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
-  float ma = -INFINITY, mb = -INFINITY, la = 0.f, lb = 0.f;
-
-  for (int t = 0; t < ntiles; ++t) {
-    const int buf = t & 1;
-    if (t + 1 < ntiles) {
-      load_tile(t + 1, buf ^ 1);
-      asm volatile("cp.async.wait_group 1;" ::: "memory");
-    } else {
-      asm volatile("cp.async.wait_group 0;" ::: "memory");
-    }
-    __syncthreads();
-    const uint8_t* skb = sk + buf * kTile;
-    const uint8_t* svb = sv + buf * kTile;
-    float sacc[8][4];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) sacc[i][0] = sacc[i][1] = sacc[i][2] = sacc[i][3] = 0.f;
-#pragma unroll
-    for (int kd = 0; kd < 8; ++kd) {
-#pragma unroll
-      for (int np = 0; np < 4; ++np) {
-        uint32_t b[4];
-        const int mi = lane >> 3;
-        ldsm4(sm_u32(skb + swz((2 * np + (mi >> 1)) * 8 + (lane & 7), 2 * kd + (mi & 1))), b);
-        mma16816(sacc[2 * np], qa[kd], b[0], b[1]);
-        mma16816(sacc[2 * np + 1], qa[kd], b[2], b[3]);
-      }
-    }
-    // scale, causal mask, online softmax (rows a = c0/c1, b = c2/c3)
-    float mxa = -INFINITY, mxb = -INFINITY;
-#pragma unroll
-    for (int nt = 0; nt < 8; ++nt) {
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int key = t * kKB + nt * 8 + 2 * (lane & 3) + (e & 1);
-        const float sv_ = sacc[nt][e] * scale;
-        const bool masked = key > (e < 2 ? pa : pb);
-        sacc[nt][e] = masked ? -INFINITY : sv_;
-      }
-      mxa = fmaxf(mxa, fmaxf(sacc[nt][0], sacc[nt][1]));
-      mxb = fmaxf(mxb, fmaxf(sacc[nt][2], sacc[nt][3]));
-    }
-    mxa = fmaxf(mxa, __shfl_xor_sync(0xffffffffu, mxa, 1));
-    mxa = fmaxf(mxa, __shfl_xor_sync(0xffffffffu, mxa, 2));
-    mxb = fmaxf(mxb, __shfl_xor_sync(0xffffffffu, mxb, 1));
-    mxb = fmaxf(mxb, __shfl_xor_sync(0xffffffffu, mxb, 2));
-    const float na = fmaxf(ma, mxa), nb = fmaxf(mb, mxb);
-    // A row with every key of this tile masked keeps its running max (finite
-    // from tile 0, whose key 0 every row attends).
-    const float ca = na == -INFINITY ? 1.f : expf(ma - na);
-    const float cb = nb == -INFINITY ? 1.f : expf(mb - nb);
-    ma = na;
-    mb = nb;
-    la *= ca;
-    lb *= cb;
-#pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      o[i][0] *= ca;
-      o[i][1] *= ca;
-      o[i][2] *= cb;
-      o[i][3] *= cb;
-    }
-    uint32_t pf[4][4];
-#pragma unroll
-    for (int nt = 0; nt < 8; ++nt) {
-      const float p0 = expf(sacc[nt][0] - na), p1 = expf(sacc[nt][1] - na);
-      const float p2 = expf(sacc[nt][2] - nb), p3 = expf(sacc[nt][3] - nb);
-      la += p0 + p1;
-      lb += p2 + p3;
-      pf[nt >> 1][(nt & 1) * 2] = pack_h2(p0, p1);
-      pf[nt >> 1][(nt & 1) * 2 + 1] = pack_h2(p2, p3);
-    }
-#pragma unroll
-    for (int kc = 0; kc < 4; ++kc) {
-#pragma unroll
-      for (int dp = 0; dp < 8; ++dp) {
-        uint32_t b[4];
-        const int mi = lane >> 3;
-        ldsm4_t(sm_u32(svb + swz(kc * 16 + (mi & 1) * 8 + (lane & 7), 2 * dp + (mi >> 1))), b);
-        mma16816(o[2 * dp], pf[kc], b[0], b[1]);
-        mma16816(o[2 * dp + 1], pf[kc], b[2], b[3]);
-      }
-    }
-    __syncthreads();  // every warp is done with this buffer before it is refilled
-  }
-  la += __shfl_xor_sync(0xffffffffu, la, 1);
-  la += __shfl_xor_sync(0xffffffffu, la, 2);
-  lb += __shfl_xor_sync(0xffffffffu, lb, 1);
-  lb += __shfl_xor_sync(0xffffffffu, lb, 2);
-  const float ia = 1.f / la, ib = 1.f / lb;
-#pragma unroll
-  for (int dn = 0; dn < 16; ++dn) {
-    const int d = h * kHeadDim + dn * 8 + 2 * (lane & 3);
-    if (ra < nrows) {
-      T* y = out + (int64_t)(row0 + ra) * W + d;
-      y[0] = from_f<T>(o[dn][0] * ia);
-      y[1] = from_f<T>(o[dn][1] * ia);
-    }
-    if (rb < nrows) {
-      T* y = out + (int64_t)(row0 + rb) * W + d;
-      y[0] = from_f<T>(o[dn][2] * ib);
-      y[1] = from_f<T>(o[dn][3] * ib);
-    }
-  }
-}
-
 size_t attention_ws_bytes(int64_t rows, int heads, int capacity, int act) {
   const int64_t nsplit = (capacity + kSplit - 1) / kSplit;
   const int64_t parts = rows * heads * nsplit;
@@ -484,18 +278,7 @@ static tf_status attention_impl(const AttnProblem& a, cudaStream_t s) {
   if (nq == 0) return TF_OK;
   if (a.qblocks && a.nqblocks > 0 && !a.qrows) {
     // Prefill rows grouped per request: tiled tensor-core attention.
-    static PerDeviceOnce attr;
-    int dev = 0;
-    if (attr.needed(&dev)) {
-      TF_CUDA(cudaFuncSetAttribute(attn_prefill_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                   kPrefillSmem));
-      attr.mark(dev);
-    }
-    dim3 pgrid((unsigned)a.nqblocks, a.heads);
-    attn_prefill_kernel<T><<<pgrid, kPrefillThreads, kPrefillSmem, s>>>(
-        qr, a.heads, a.qblocks, (const __half*)a.k_cache, (const __half*)a.v_cache, a.capacity, a.scale,
-        (T*)a.out);
-    return check_launch("attn_prefill");
+    return launch_attn_prefill_tc(a, qr, s);
   }
   dim3 grid(grid_splits, a.heads, (unsigned)nq);
   attn_split_kernel<T><<<grid, kAttnThreads, 0, s>>>(qr, a.heads, a.pos, a.req, a.qrows,

@@ -194,6 +194,9 @@ extern int g_qmm_path;
 int read_tc_error(bool clear);
 // Cycles a tensor-core pipeline wait may take (<= 0: the default), current device.
 tf_status set_wait_limit(long long cycles);
+// Device addresses of the tensor-core error code and wait limit, for
+// kernels in other translation units that record into the same flag.
+tf_status tc_flags(int** error, long long** wait_cycles);
 int read_embed_error(bool clear);
 // tokens[r] = all(isfinite(logits[r])) ? argmax (lowest index on ties) : -1.
 tf_status launch_greedy(const float* logits, int64_t rows, int64_t vocab, int64_t* tokens, cudaStream_t s);
@@ -238,18 +241,23 @@ struct AttnProblem {
   void* out = nullptr;  // act [rows][heads * head_dim]
   void* ws = nullptr;
   size_t ws_bytes = 0;
-  // Optional (prefill): device int4 {first row, rows <= 64, request, first
-  // position} per query block; every row of a block belongs to one request
-  // and the rows' positions are consecutive.  With it the attention runs the
-  // tiled tensor-core kernel instead of the per-row split-K one.
+  // Optional (prefill): device int4 {first row, rows <= kPrefillQueryBlock,
+  // request, first position} per query block; every row of a block belongs
+  // to one request and the rows' positions are consecutive.  With it the
+  // attention runs the tiled tensor-core kernel instead of the per-row
+  // split-K one; cache_requests (the caches' first dimension) bounds its
+  // tile copies.
   const int4* qblocks = nullptr;
   int nqblocks = 0;
+  int cache_requests = 0;
   // Optional: attend only the rows qrows[0..nq) (device), writing output row
   // i for qrows[i]; every row is still appended.  nq == 0: append only.
   const int32_t* qrows = nullptr;
   int64_t nq = 0;
 };
+constexpr int kPrefillQueryBlock = 128;
 size_t attention_ws_bytes(int64_t rows, int heads, int capacity, int act);
+tf_status launch_attn_prefill_tc(const AttnProblem& a, const void* q, cudaStream_t s);
 tf_status launch_attention(const AttnProblem& a, cudaStream_t s);
 
 }  // namespace tf

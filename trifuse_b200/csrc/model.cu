@@ -18,6 +18,7 @@
 #include <string>
 #include <cmath>
 #include <tuple>
+#include <algorithm>
 #include <vector>
 
 #include "common.cuh"
@@ -436,7 +437,7 @@ int tf_session_create(tf_model* model, int32_t max_batch, int32_t capacity, int3
     s->last_rows = k.take<int32_t>((size_t)max_batch * 4);
     s->logits = k.take<float>((size_t)max_batch * c.vocab * 4);
     s->greedy = k.take<int64_t>((size_t)max_batch * 8);
-    s->qblocks = k.take<int4>((size_t)(R / 64 + max_batch + 1) * sizeof(int4));
+    s->qblocks = k.take<int4>((size_t)(R / kPrefillQueryBlock + max_batch + 1) * sizeof(int4));
     s->attn_ws = k.take<char>(s->attn_ws_bytes);
     s->moe_ws = k.take<char>(s->moe_ws_bytes);
     s->split_partials = k.take<float>(qmm_split_partial_bytes());
@@ -635,6 +636,7 @@ tf_status forward_rows(tf_session* s, int64_t rows, bool req_ident, int max_len,
     a.ws_bytes = s->attn_ws_bytes;
     a.qblocks = nqblocks ? s->qblocks : nullptr;
     a.nqblocks = nqblocks;
+    a.cache_requests = s->max_batch;
     int64_t n = rows;  // rows past the attention
     if (lq) {
       a.qrows = last;
@@ -907,9 +909,11 @@ int tf_session_prefill(tf_session* s, const int32_t* requests, const int32_t* to
     if (n <= 0) return set_error(TF_ERR_INVALID_ARGUMENT, "prefill: request %d has %d tokens", r, n);
     const int start = s->lengths[r];
     if ((int64_t)start + n > s->capacity) return set_error(TF_ERR_CAPACITY, "absolute capacity exceeded");
-    // query blocks of up to 64 rows of this request (tiled prefill attention)
-    for (int b0 = 0; b0 < n; b0 += 64)
-      qb.push_back(make_int4((int)pos.size() + b0, n - b0 < 64 ? n - b0 : 64, r, start + b0));
+    // query blocks of up to kPrefillQueryBlock rows of this request (tiled
+    // prefill attention)
+    for (int b0 = 0; b0 < n; b0 += kPrefillQueryBlock)
+      qb.push_back(make_int4((int)pos.size() + b0, n - b0 < kPrefillQueryBlock ? n - b0 : kPrefillQueryBlock, r,
+                             start + b0));
     for (int t = 0; t < n; ++t) {
       pos.push_back(start + t);
       req.push_back(r);
@@ -917,6 +921,9 @@ int tf_session_prefill(tf_session* s, const int32_t* requests, const int32_t* to
     last[i] = (int32_t)pos.size() - 1;
     if (start + n > max_len) max_len = start + n;
   }
+  // Blocks with the most keys first, so that the longest ones do not start
+  // in the last wave.
+  std::stable_sort(qb.begin(), qb.end(), [](const int4& x, const int4& y) { return x.w + x.y > y.w + y.y; });
   const int64_t rows = (int64_t)pos.size();
   if (rows > s->max_rows)
     return set_error(TF_ERR_CAPACITY, "prefill: %lld rows exceed the session's %d", (long long)rows, s->max_rows);

@@ -65,6 +65,7 @@
 
 #include "common.cuh"
 #include "internal.h"
+#include "tc_ptx.cuh"
 
 namespace tf {
 
@@ -103,9 +104,6 @@ constexpr int kACols = kKStep / 2;   // TMEM columns of one k-step of A (two f16
 // Fixed limit of the waits that drain a block's own copies and MMAs before
 // it exits (not shortened by tf_set_wait_limit: copies in flight always land).
 constexpr long long kDrainCycles = 2000000000LL;
-// try_wait suspends the thread until the phase completes or this many ns
-// pass, so a waiting role takes no issue slots from the dequant warps.
-constexpr uint32_t kSuspendNs = 1000000;
 
 // A block's work item: chunks [kc0, kc1) (a chunk is kSK k-steps) of one
 // tile (expert e, token slots s0 .. s0 + cnt, row block rb).  Segments with
@@ -146,30 +144,6 @@ struct Params {
   int* counters;
 };
 
-__device__ __forceinline__ uint32_t smem_addr(const void* p) {
-  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count));
-}
-__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
-}
-__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)), "r"(bytes)
-               : "memory");
-}
-__device__ __forceinline__ bool mbar_try(uint64_t* bar, uint32_t parity, uint32_t suspend_ns = kSuspendNs) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(smem_addr(bar)), "r"(parity), "r"(suspend_ns)
-      : "memory");
-  return ok != 0;
-}
 // Shared-memory wait control of a block: the abort flag every role polls,
 // and the limit and suspend hint of its bounded waits (a test limit below
 // the default polls without suspending, so it can expire).
@@ -210,101 +184,6 @@ __device__ __forceinline__ void mbar_drain(uint64_t* bar, uint32_t parity) {
 __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, WaitCtl* w, int code) {
   return __all_sync(0xffffffffu, mbar_wait(bar, parity, w, code));
 }
-__device__ __forceinline__ void tma_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
-          smem_addr(dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_addr(bar))
-      : "memory");
-}
-__device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
-__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-
-// K-major, 128-byte swizzled operand descriptor (rows of 128 B, 8-row groups
-// 1024 B apart; start address advanced by 32 B per K=16 slice).
-__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
-  uint64_t d = 0;
-  d |= (uint64_t)((saddr >> 4) & 0x3FFFu);  // start address
-  d |= (uint64_t)1 << 16;                   // leading byte offset (unused for SW128 K-major)
-  d |= (uint64_t)(1024u >> 4) << 32;        // stride byte offset
-  d |= (uint64_t)1 << 46;                   // descriptor version (sm100)
-  d |= (uint64_t)2 << 61;                   // SWIZZLE_128B
-  return d;
-}
-// kind::f16 instruction descriptor: f16 x f16 -> f32, K-major A and B.
-__device__ __forceinline__ uint32_t idesc_f16(int m, int n) {
-  return (1u << 4) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
-}
-// One lane of a converged warp (elect.sync picks the same lane every time).
-// The MMA warp runs its loop with all 32 lanes so that descriptors and
-// indices stay warp-uniform; only the elected lane issues tcgen05 work, and
-// tcgen05.commit tracks the MMAs that this same lane issued.
-__device__ __forceinline__ uint32_t elect_one() {
-  uint32_t e;
-  asm volatile(
-      "{\n\t.reg .pred e;\n\t"
-      "elect.sync _|e, 0xffffffff;\n\t"
-      "selp.u32 %0, 1, 0, e;\n\t}"
-      : "=r"(e));
-  return e;
-}
-__device__ __forceinline__ void mma_f16(uint32_t leader, uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc,
-                                        uint32_t acc) {
-  asm volatile(
-      "{\n\t.reg .pred p, e;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "setp.ne.b32 e, %5, 0;\n\t"
-      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
-      "l"(a), "l"(b), "r"(idesc), "r"(acc), "r"(leader)
-      : "memory");
-}
-__device__ __forceinline__ void mma_commit(uint32_t leader, uint64_t* bar) {
-  asm volatile(
-      "{\n\t.reg .pred e;\n\t"
-      "setp.ne.b32 e, %1, 0;\n\t"
-      "@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}" ::"r"(smem_addr(bar)),
-      "r"(leader)
-      : "memory");
-}
-// The destination registers of tcgen05.ld are valid only after
-// tcgen05.wait::ld; both sit in one asm statement so that no use of the
-// outputs can be scheduled between them.
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
-  uint32_t r[16];
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];\n\t"
-      "tcgen05.wait::ld.sync.aligned;"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-      : "r"(taddr)
-      : "memory");
-#pragma unroll
-  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
-}
-
-// 16 consecutive TMEM columns of this warp's 32 lanes <- v (warp-wide).
-__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t* v) {
-  asm volatile(
-      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
-          taddr),
-      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
-      "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
-      : "memory");
-}
-__device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
-// D (TMEM) += A (TMEM) * B (shared memory descriptor).
-__device__ __forceinline__ void mma_f16_ts(uint32_t leader, uint32_t tmem_d, uint32_t tmem_a, uint64_t b,
-                                           uint32_t idesc, uint32_t acc) {
-  asm volatile(
-      "{\n\t.reg .pred p, e;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "setp.ne.b32 e, %5, 0;\n\t"
-      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(tmem_d),
-      "r"(tmem_a), "l"(b), "r"(idesc), "r"(acc), "r"(leader)
-      : "memory");
-}
-
 // Eight codes of one packed word (code i at bits 4i) -> eight f16 weights
 // fp16(code*s + b).  The f16 halves of
 //   t0 = w & 0x000F000F | 0x6400 (1024 + c0, 1024 + c4)
@@ -382,6 +261,31 @@ struct Layout {
   static_assert((2 * PK + 2 * SA + 2 * SB + 9) * 8 + 8 <= 448, "barrier block fits below the wait control");
 };
 
+// Residual values of the 8 tokens c0 .. c0 + 7 of TMEM lane q's row (0 past
+// the segment or the matrix).  The epilogue loads them 8 tokens ahead of
+// their use, so the loads overlap the previous tokens' stores; a load always
+// precedes the store of the same element, so y may alias residual.
+template <typename T>
+__device__ __forceinline__ void epi_residual(const Params& p, const Seg& sg, int q, int c0, float* res) {
+  const int f = sg.rb * kM + q;
+  const int n = f < p.out ? sg.cnt - c0 : 0;  // valid tokens from c0
+  const T* r = static_cast<const T*>(p.residual) + ((int64_t)(sg.s0 + c0) * p.residual_stride + f);
+#pragma unroll
+  for (int i = 0; i < 8; ++i, r += p.residual_stride) res[i] = i < n ? to_f(*r) : 0.f;
+}
+
+// y = act(residual + act(acc)) for the 8 tokens c0 .. c0 + 7 of lane q's row.
+template <typename T>
+__device__ __forceinline__ void epi_residual_store(const Params& p, const Seg& sg, int q, int c0, const float* v,
+                                                   const float* res) {
+  const int f = sg.rb * kM + q;
+  const int n = f < p.out ? sg.cnt - c0 : 0;
+  T* y = static_cast<T*>(p.y) + ((int64_t)(sg.s0 + c0) * p.y_stride + f);
+#pragma unroll
+  for (int i = 0; i < 8; ++i, y += p.y_stride)
+    if (i < n) *y = from_f<T>(res[i] + round_act<T>(v[i]));
+}
+
 // Epilogue of 16 accumulator columns (tokens c0 .. c0 + 15 of the segment's
 // tile) held by TMEM lane q.
 template <typename T, int EPI>
@@ -419,35 +323,26 @@ __device__ __forceinline__ void epi_apply(const Params& p, const Seg& sg, int q,
     // The f16 operand of the down projection: a bf16 value beyond the f16
     // range became inf there, which records device error 5.
     if (wide) atomicCAS(&g_tc_error, 0, 5);
+  } else if (EPI == EPI_RESIDUAL) {
+#pragma unroll
+    for (int h = 0; h < 16; h += 8) {
+      float res[8];
+      epi_residual<T>(p, sg, q, c0 + h, res);
+      epi_residual_store<T>(p, sg, q, c0 + h, v + h, res);
+    }
   } else {
     const int f = sg.rb * kM + q;
 #pragma unroll
-    for (int i0 = 0; i0 < 16; i0 += 8) {
-      float res[8];
-      if (EPI == EPI_RESIDUAL) {
-        // All 8 residual loads before any store (y may alias residual).
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const int tok = c0 + i0 + i;
-          res[i] = tok < sg.cnt && f < p.out
-                       ? to_f(static_cast<const T*>(p.residual)[(int64_t)(sg.s0 + tok) * p.residual_stride + f])
-                       : 0.f;
-        }
-      }
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const int tok = c0 + i0 + i;
-        const float vi = v[i0 + i];
-        if (tok < sg.cnt && f < p.out) {
-          const int64_t slot = sg.s0 + tok;
-          if (EPI == EPI_F32) {
-            static_cast<float*>(p.y)[slot * p.y_stride + f] = round_act<T>(vi);
-          } else if (EPI == EPI_RESIDUAL) {
-            static_cast<T*>(p.y)[slot * p.y_stride + f] = from_f<T>(res[i] + round_act<T>(vi));
-          } else {
-            const int64_t orow = p.y_index ? (int64_t)p.y_index[slot] : slot;
-            static_cast<T*>(p.y)[orow * p.y_stride + f] = from_f<T>(vi);
-          }
+    for (int i = 0; i < 16; ++i) {
+      const int tok = c0 + i;
+      const float vi = v[i];
+      if (tok < sg.cnt && f < p.out) {
+        const int64_t slot = sg.s0 + tok;
+        if (EPI == EPI_F32) {
+          static_cast<float*>(p.y)[slot * p.y_stride + f] = round_act<T>(vi);
+        } else {
+          const int64_t orow = p.y_index ? (int64_t)p.y_index[slot] : slot;
+          static_cast<T*>(p.y)[orow * p.y_stride + f] = from_f<T>(vi);
         }
       }
     }
@@ -837,10 +732,29 @@ __global__ void __launch_bounds__(Roles<G * H, BPS>::kThreads, BPS)
       const int n_mma = (sg.cnt + 15) / 16 * 16;
       const uint32_t taddr = tmem + ((uint32_t)(wq * 32) << 16) + (uint32_t)(buf * NT);
       if (sg.slot < 0) {
-        for (int c0 = 0; c0 < n_mma; c0 += 16) {
-          float v[16];
-          tmem_ld16(taddr + c0, v);
-          epi_apply<T, EPI>(p, sg, q, c0, v);
+        if (EPI == EPI_RESIDUAL) {
+          // Residual tiles: each 8 tokens' residual loads issue before the
+          // previous 8 tokens' stores.
+          float res[8];
+          epi_residual<T>(p, sg, q, 0, res);
+          for (int c0 = 0; c0 < n_mma; c0 += 16) {
+            float v[16];
+            tmem_ld16(taddr + c0, v);
+#pragma unroll
+            for (int h = 0; h < 16; h += 8) {
+              float nres[8];
+              if (c0 + h + 8 < n_mma) epi_residual<T>(p, sg, q, c0 + h + 8, nres);
+              epi_residual_store<T>(p, sg, q, c0 + h, v + h, res);
+#pragma unroll
+              for (int i = 0; i < 8; ++i) res[i] = nres[i];
+            }
+          }
+        } else {
+          for (int c0 = 0; c0 < n_mma; c0 += 16) {
+            float v[16];
+            tmem_ld16(taddr + c0, v);
+            epi_apply<T, EPI>(p, sg, q, c0, v);
+          }
         }
         tc_fence_before();
         __syncwarp();
@@ -1002,8 +916,9 @@ tf_status launch_cfg(tc::Params& p, const QmmProblem& q, int64_t tiles_bound, cu
   // Split schedule: every block slot takes an equal run of (tile, chunk)
   // units.  It needs a partial slot pair per block, a counter per tile, and
   // a segment table that holds a block's tiles.
-  // Only grouped (expert) problems split: a dense problem has too few tiles
-  // for the units of a block to keep its tiles in one or two parts.
+  // Only grouped (expert) problems split.  Dense decode projections (fewer
+  // tiles than block slots) measured slower split than whole: qkv at B=64
+  // 48 vs 23 us per layer.
   p.split = p.grouped && q.partials && q.counters && 4 * tiles_bound <= q.counter_cap &&
             tiles_bound * 16 * slots < 2147483647LL &&
             (size_t)2 * slots * tc::kM * NT * sizeof(float) <= q.partial_bytes &&
@@ -1152,6 +1067,17 @@ tf_status launch_bf16_to_f16(const void* x, int64_t n, void* y, int permute, cud
   if (n == 0) return TF_OK;
   if (n % 2048) return set_error(TF_ERR_SHAPE, "bf16_to_f16: count %lld not a multiple of 2048", (long long)n);
   return launch_gather_f16(x, 2048, TF_DTYPE_BF16, nullptr, 1, n / 2048, 2048, y, permute, s);
+}
+
+tf_status make_tma_2d(CUtensorMap* m, const void* base, CUtensorMapDataType dt, int esize, int64_t cols,
+                      int64_t rows, int64_t row_pitch_bytes, int bx, int by, CUtensorMapSwizzle sw) {
+  return make_map(m, base, dt, esize, cols, rows, row_pitch_bytes, bx, by, sw);
+}
+
+tf_status tc_flags(int** error, long long** wait_cycles) {
+  TF_CUDA(cudaGetSymbolAddress(reinterpret_cast<void**>(error), g_tc_error));
+  TF_CUDA(cudaGetSymbolAddress(reinterpret_cast<void**>(wait_cycles), g_wait_cycles));
+  return TF_OK;
 }
 
 tf_status set_wait_limit(long long cycles) {

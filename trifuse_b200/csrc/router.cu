@@ -150,6 +150,144 @@ __global__ void __launch_bounds__(kRouterBlockWarps * 32)
   }
 }
 
+// Router for prefill-sized batches: a block of kRouterWideWarps warps owns
+// kRouterWideTokens tokens, so each weight chunk is decoded once per 16
+// tokens, and the per-token arithmetic runs on packed fp32 pairs
+// (mul.rn.f32x2 / add.rn.f32x2: two tokens' products and sums per
+// instruction, each lane of the pair rounded as the scalar op).  The order
+// per (token, expert) is router_kernel's: lane l, chunks l + 32j (j outer),
+// the 8 elements of a chunk in order, separate multiply and add, then the
+// xor butterfly, so the logits are bit-identical.  Shared layout: token pair
+// p, element pair q of chunk c at float4 [(4p + q) * C + c] = (x[2p][8c+2q],
+// x[2p+1][8c+2q], x[2p][8c+2q+1], x[2p+1][8c+2q+1]); a warp's lanes read 32
+// consecutive float4 (no bank conflicts).
+constexpr int kRouterWideWarps = 16;
+constexpr int kRouterWideTokens = 16;
+
+__device__ __forceinline__ uint64_t f32x2_pack(float a, float b) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ void f32x2_unpack(uint64_t v, float& a, float& b) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(v));
+}
+// acc + x * w, two lanes, each rounded as __fmul_rn then __fadd_rn.
+__device__ __forceinline__ uint64_t f32x2_mul_add(uint64_t acc, uint64_t x, uint64_t w) {
+  uint64_t prod, r;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(prod) : "l"(x), "l"(w));
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(acc), "l"(prod));
+  return r;
+}
+
+template <int J>
+constexpr size_t router_wide_smem() {
+  return (size_t)kRouterWideTokens * J * 256 * sizeof(float) + (size_t)kRouterWideTokens * 64 * sizeof(float);
+}
+
+template <typename T, bool DENSE, int J>
+__global__ void __launch_bounds__(kRouterWideWarps * 32, 1)
+    router_wide_kernel(const T* __restrict__ x, int64_t tokens, const T* __restrict__ wd,
+                       const uint32_t* __restrict__ wq, const __half* __restrict__ ws,
+                       const __half* __restrict__ wb, int E, int K, T* logits, int32_t* idx, T* gates) {
+  constexpr int H = J * 256, C = H / 8, TP = kRouterWideTokens / 2;
+  extern __shared__ float4 xs4[];
+  float* xsf = reinterpret_cast<float*>(xs4);
+  float* ls = xsf + (size_t)kRouterWideTokens * H;  // [tokens][64]
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int64_t t0 = (int64_t)blockIdx.x * kRouterWideTokens;
+  static_assert(kRouterWideTokens * C % (kRouterWideWarps * 32) == 0, "whole fill rounds");
+#pragma unroll
+  for (int i = threadIdx.x; i < kRouterWideTokens * C; i += kRouterWideWarps * 32) {
+    const int t = i / C, c = i % C;
+    float f[8];
+    if (t0 + t < tokens) {
+      unpack8<T>(ld_v4(x + (t0 + t) * H + 8 * c), f);
+    } else {
+#pragma unroll
+      for (int k = 0; k < 8; ++k) f[k] = 0.f;
+    }
+    const int pr = t >> 1, sl = t & 1;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      float* d = xsf + ((size_t)(4 * pr + q) * C + c) * 4;
+      d[sl] = f[2 * q];
+      d[2 + sl] = f[2 * q + 1];
+    }
+  }
+  __syncthreads();
+  for (int e = warp; e < E; e += kRouterWideWarps) {
+    uint64_t acc[TP];
+#pragma unroll
+    for (int p = 0; p < TP; ++p) acc[p] = 0ull;  // (+0.f, +0.f)
+    // The next chunk's weights are loaded while this one is multiplied.
+    uint4 nd = make_uint4(0, 0, 0, 0);
+    uint32_t nword = 0;
+    __half nsc = __float2half(0.f), nbi = nsc;
+    auto fetch = [&](int j) {
+      const int c = lane + 32 * j;
+      if (DENSE) {
+        nd = ld_v4(wd + (int64_t)e * H + 8 * c);
+      } else {
+        nword = wq[(int64_t)e * (H / 8) + c];
+        nsc = ws[(int64_t)e * (H / 64) + c / 8];
+        nbi = wb[(int64_t)e * (H / 64) + c / 8];
+      }
+    };
+    fetch(0);
+#pragma unroll 1
+    for (int j = 0; j < J; ++j) {
+      const int c = lane + 32 * j;
+      float wf[8];
+      if (DENSE) {
+        unpack8<T>(nd, wf);
+      } else {
+        const uint32_t word = nword;
+        const float sc = __half2float(nsc);
+        const float bi = __half2float(nbi);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float code = (float)((word >> (4 * i)) & 0xFu);
+          wf[i] = __half2float(__float2half_rn(__fadd_rn(__fmul_rn(code, sc), bi)));
+        }
+      }
+      if (j + 1 < J) fetch(j + 1);
+      uint64_t w2[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) w2[i] = f32x2_pack(wf[i], wf[i]);
+#pragma unroll
+      for (int p = 0; p < TP; ++p) {
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const float4 v = xs4[(size_t)(4 * p + q) * C + c];
+          acc[p] = f32x2_mul_add(acc[p], f32x2_pack(v.x, v.y), w2[2 * q]);
+          acc[p] = f32x2_mul_add(acc[p], f32x2_pack(v.z, v.w), w2[2 * q + 1]);
+        }
+      }
+    }
+#pragma unroll
+    for (int p = 0; p < TP; ++p) {
+      float a0, a1;
+      f32x2_unpack(acc[p], a0, a1);
+      const float l0 = round_act<T>(warp_sum_butterfly(a0));
+      const float l1 = round_act<T>(warp_sum_butterfly(a1));
+      if (lane == 0) {
+        const int t = 2 * p;
+        ls[t * 64 + e] = l0;
+        ls[(t + 1) * 64 + e] = l1;
+        if (logits && t0 + t < tokens) logits[(t0 + t) * E + e] = from_f<T>(l0);
+        if (logits && t0 + t + 1 < tokens) logits[(t0 + t + 1) * E + e] = from_f<T>(l1);
+      }
+    }
+  }
+  __syncthreads();
+  if (idx && warp < kRouterWideTokens && t0 + warp < tokens) {
+    const float la0 = lane < E ? ls[warp * 64 + lane] : 0.f;
+    const float la1 = lane + 32 < E ? ls[warp * 64 + lane + 32] : 0.f;
+    route_token<T>(lane, la0, la1, E, K, t0 + warp, (T*)nullptr, idx, gates);
+  }
+}
+
 // Router for small batches (decode): a cluster of kRouterCluster CTAs per
 // token, each computing ceil(E / kRouterCluster) experts (one warp per
 // expert, the same fixed order as router_kernel), so the 64 dot products of
@@ -277,6 +415,37 @@ static tf_status router_dispatch_tpc(const void* x, int64_t tokens, int hidden,
   return check_launch("router");
 }
 
+template <typename T, bool DENSE, int J>
+static tf_status router_wide_launch(const void* x, int64_t tokens, const tf_router_weight& r, int E, int K,
+                                    void* logits, int32_t* idx, void* gates, cudaStream_t s) {
+  constexpr size_t smem = router_wide_smem<J>();
+  static PerDeviceOnce attr;
+  int dev = 0;
+  if (attr.needed(&dev)) {
+    TF_CUDA(cudaFuncSetAttribute(router_wide_kernel<T, DENSE, J>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)smem));
+    attr.mark(dev);
+  }
+  const unsigned blocks = (unsigned)((tokens + kRouterWideTokens - 1) / kRouterWideTokens);
+  router_wide_kernel<T, DENSE, J><<<blocks, kRouterWideWarps * 32, smem, s>>>(
+      (const T*)x, tokens, (const T*)r.dense, r.affine.q, (const __half*)r.affine.scales,
+      (const __half*)r.affine.biases, E, K, (T*)logits, idx, (T*)gates);
+  return check_launch("router_wide");
+}
+
+template <typename T, bool DENSE>
+static tf_status router_dispatch_wide(const void* x, int64_t tokens, int hidden, const tf_router_weight& r,
+                                      int E, int K, void* logits, int32_t* idx, void* gates, cudaStream_t s) {
+  switch (hidden / 256) {
+    case 1: return router_wide_launch<T, DENSE, 1>(x, tokens, r, E, K, logits, idx, gates, s);
+    case 2: return router_wide_launch<T, DENSE, 2>(x, tokens, r, E, K, logits, idx, gates, s);
+    case 4: return router_wide_launch<T, DENSE, 4>(x, tokens, r, E, K, logits, idx, gates, s);
+    case 8: return router_wide_launch<T, DENSE, 8>(x, tokens, r, E, K, logits, idx, gates, s);
+    default:
+      return set_error(TF_ERR_UNSUPPORTED, "router: hidden %d not in {256,512,1024,2048}", hidden);
+  }
+}
+
 template <typename T, bool DENSE>
 static tf_status router_dispatch_cluster(const void* x, int64_t tokens, int hidden, const tf_router_weight& r,
                                          int E, int K, void* logits, int32_t* idx, void* gates, cudaStream_t s) {
@@ -303,7 +472,7 @@ static tf_status router_dispatch_cluster(const void* x, int64_t tokens, int hidd
 }
 
 // Decode-sized batches: a cluster of 8 CTAs per token.  Up to 2048 tokens:
-// one token per block; beyond, four (weights decoded once per four tokens).
+// one token per block; beyond, sixteen per block on packed fp32 pairs.
 template <typename T, bool DENSE>
 static tf_status router_dispatch(const void* x, int64_t tokens, int hidden,
                                  const tf_router_weight& r, int E, int K, void* logits,
@@ -312,7 +481,7 @@ static tf_status router_dispatch(const void* x, int64_t tokens, int hidden,
     return router_dispatch_cluster<T, DENSE>(x, tokens, hidden, r, E, K, logits, idx, gates, s);
   if (tokens <= 2048)
     return router_dispatch_tpc<T, DENSE, 1>(x, tokens, hidden, r, E, K, logits, idx, gates, s);
-  return router_dispatch_tpc<T, DENSE, 4>(x, tokens, hidden, r, E, K, logits, idx, gates, s);
+  return router_dispatch_wide<T, DENSE>(x, tokens, hidden, r, E, K, logits, idx, gates, s);
 }
 
 tf_status launch_router(const void* x, int64_t tokens, int hidden, const tf_router_weight& r,
