@@ -410,6 +410,9 @@ def main():
     ap.add_argument("--layers", type=int, default=16, help="model depth (profiling small cases)")
     ap.add_argument("--ncu", action="store_true",
                     help="profiling run: warm up, then one decode step between cudaProfilerStart/Stop")
+    ap.add_argument("--ncu-prefill", action="store_true",
+                    help="profiling run: one warm-up config-3 prefill (8 x 2048), then one between "
+                         "cudaProfilerStart/Stop")
     args = ap.parse_args()
     rank, local_rank, world = env_rank()
     if args.impl == "reference":
@@ -441,6 +444,28 @@ def main():
     B, L = args.batch, args.kv_len
     cap = max(L + 2 * (args.warmup + args.steps) + 8, 2048 + 64)
     cfg, model = build_model(cap, local_rank, args.layers)
+    if args.ncu_prefill:
+        from trifuse_b200.model import Session
+        T, n = 2048, 8
+        g = torch.Generator()
+        g.manual_seed(20260103)
+        ids_dev = torch.randint(0, cfg.vocab, (n * T,), generator=g).cuda(local_rank)
+        logits_dev = torch.empty((n, cfg.vocab), dtype=torch.float32, device="cuda")
+        psess = Session(model, max_batch=n, capacity=T + 64, max_prefill_tokens=n * T)
+        for profiled in (False, True):
+            psess.reset()
+            torch.cuda.synchronize()
+            if profiled:
+                torch.cuda.profiler.start()
+            psess.prefill_device(list(range(n)), [T] * n, ids_dev, logits_dev)
+            torch.cuda.synchronize()
+            if profiled:
+                torch.cuda.profiler.stop()
+        if rank == 0:
+            print(json.dumps({"ncu_prefill": True, "sequences": n, "tokens": T, "layers": args.layers}))
+        psess.close()
+        model.close()
+        return
     sess = decode_session(model, B, L, cap, local_rank)
     stream = torch.cuda.current_stream()
     g = torch.Generator(device="cuda")

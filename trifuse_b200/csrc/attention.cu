@@ -65,9 +65,12 @@ __global__ void __launch_bounds__(kAttnThreads)
                        __half* k_cache, __half* v_cache, int cap, T* __restrict__ q_out) {
   __shared__ float tot_s[64];
   __shared__ float bcast;
+  __shared__ float inv_s[kHeadDim / 2];  // RoPE inverse frequencies theta^(-2d/D)
   const int64_t r = blockIdx.x;
   const int t = threadIdx.x;
   const int W = heads * kHeadDim;
+  for (int d = t; d < kHeadDim / 2; d += kAttnThreads)
+    inv_s[d] = (float)pow((double)theta, -2.0 * (double)d / (double)kHeadDim);  // (synced below)
   const T* qrow = qkv + r * 3 * W;
   const T* krow = qrow + W;
   const T* vrow = qrow + 2 * W;
@@ -79,7 +82,7 @@ __global__ void __launch_bounds__(kAttnThreads)
   for (int i = t; i < W / 2; i += kAttnThreads) {
     const int h = i / (kHeadDim / 2), d = i % (kHeadDim / 2);
     const int i1 = h * kHeadDim + d, i2 = i1 + kHeadDim / 2;
-    const float inv = (float)pow((double)theta, -2.0 * (double)d / (double)kHeadDim);
+    const float inv = inv_s[d];
     float sn, cs;
     sincosf(__fmul_rn(fp, inv), &sn, &cs);
     {

@@ -129,6 +129,47 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+// 64 consecutive TMEM columns of this warp's 32 lanes (wait included).
+__device__ __forceinline__ void tmem_ld64(uint32_t taddr, float* v) {
+  uint32_t r[64];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x64.b32 {"
+      "%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,"
+      "%32,%33,%34,%35,%36,%37,%38,%39,%40,%41,%42,%43,%44,%45,%46,%47,"
+      "%48,%49,%50,%51,%52,%53,%54,%55,%56,%57,%58,%59,%60,%61,%62,%63}, [%64];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31]),
+        "=r"(r[32]), "=r"(r[33]), "=r"(r[34]), "=r"(r[35]), "=r"(r[36]), "=r"(r[37]), "=r"(r[38]), "=r"(r[39]),
+        "=r"(r[40]), "=r"(r[41]), "=r"(r[42]), "=r"(r[43]), "=r"(r[44]), "=r"(r[45]), "=r"(r[46]), "=r"(r[47]),
+        "=r"(r[48]), "=r"(r[49]), "=r"(r[50]), "=r"(r[51]), "=r"(r[52]), "=r"(r[53]), "=r"(r[54]), "=r"(r[55]),
+        "=r"(r[56]), "=r"(r[57]), "=r"(r[58]), "=r"(r[59]), "=r"(r[60]), "=r"(r[61]), "=r"(r[62]), "=r"(r[63])
+      : "r"(taddr)
+      : "memory");
+#pragma unroll
+  for (int i = 0; i < 64; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// 2^x for x <= 8 on the FMA pipe (x below -127 gives 0): Cody-Waite split
+// x = n + f, n = floor(x) (an add with round-down against 1.5 * 2^23 leaves n
+// in the low mantissa bits), 2^f on [0, 1) by a cubic fitted here by
+// weighted least squares for relative error (max 8.6e-5, below the f16
+// rounding of P), and 2^n added to the exponent field.  Takes half of the
+// exponentials off the special-function unit.
+__device__ __forceinline__ float poly_exp2(float x) {
+  x = fmaxf(x, -127.f);
+  const float t = __fadd_rd(x, 12582912.f);
+  const float n = __fsub_rn(t, 12582912.f);
+  const float f = __fsub_rn(x, n);
+  float p = fmaf(f, 0.07706641f, 0.22764570f);
+  p = fmaf(f, p, 0.69511662f);
+  p = fmaf(f, p, 1.f);
+  return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
+}
+
 __device__ __forceinline__ float fast_exp2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
@@ -295,16 +336,21 @@ __global__ void __launch_bounds__(kFaThreads, 1) attn_prefill_tc_kernel(const __
       if (!(ok = fa_warp_wait(&s_full[st], (uint32_t)((j >> 1) & 1), ctl, err, 66))) break;
       tc_fence_after();
       float sc[128];
-#pragma unroll
-      for (int c = 0; c < 128; c += 32) tmem_ld32(lane_base + kColS + st * 128 + c, sc + c);
+      tmem_ld64(lane_base + kColS + st * 128, sc);
+      tmem_ld64(lane_base + kColS + st * 128 + 64, sc + 64);
       const int lim = pr - j * kFaKeys;  // keys c > lim of this tile are masked
-      float mx = -INFINITY;
+      // Eight independent partial maxima and sums keep the chains short.
+      float mp[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) mp[i] = -INFINITY;
 #pragma unroll
       for (int c = 0; c < 128; ++c) {
         const float t = c > lim ? -INFINITY : sc[c] * p.scale_log2;
         sc[c] = t;
-        mx = fmaxf(mx, t);
+        mp[c & 7] = fmaxf(mp[c & 7], t);
       }
+      const float mx = fmaxf(fmaxf(fmaxf(mp[0], mp[1]), fmaxf(mp[2], mp[3])),
+                             fmaxf(fmaxf(mp[4], mp[5]), fmaxf(mp[6], mp[7])));
       float factor = 1.f;  // O and l scale when the max moves
       if (j == 0) {
         m_used = mx;  // finite: key 0 is attended by every row
@@ -314,14 +360,16 @@ __global__ void __launch_bounds__(kFaThreads, 1) attn_prefill_tc_kernel(const __
         l *= factor;
       }
       uint32_t pk[64];
-      float sum = 0.f;
+      float sp[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) sp[i] = 0.f;
 #pragma unroll
       for (int c = 0; c < 64; ++c) {
-        const float a = fast_exp2(sc[2 * c] - m_used), b = fast_exp2(sc[2 * c + 1] - m_used);
-        sum += a + b;
+        const float a = fast_exp2(sc[2 * c] - m_used), b = poly_exp2(sc[2 * c + 1] - m_used);
+        sp[c & 7] += a + b;
         pk[c] = pack_half2(a, b);
       }
-      l += sum;
+      l += ((sp[0] + sp[1]) + (sp[2] + sp[3])) + ((sp[4] + sp[5]) + (sp[6] + sp[7]));
       if (j >= 1) {
         // P V of the previous tile is done: O is stable and this P buffer
         // (last read two tiles ago) is free.

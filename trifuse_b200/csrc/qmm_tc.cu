@@ -100,6 +100,7 @@ constexpr int kKStep = 64;
 constexpr int kSK = 8;          // k-steps per scale slot (16 bytes of f16 per row) = one work chunk
 constexpr int kMaxSegs = 128;   // per-block segment table
 constexpr int kMaxExperts = 256;
+constexpr int kFixupParts = 2;  // partial tiles read per round trip in the split fixup
 constexpr int kACols = kKStep / 2;   // TMEM columns of one k-step of A (two f16 per column)
 // Fixed limit of the waits that drain a block's own copies and MMAs before
 // it exits (not shortened by tf_set_wait_limit: copies in flight always land).
@@ -794,23 +795,34 @@ __global__ void __launch_bounds__(Roles<G * H, BPS>::kThreads, BPS)
         const int qr = q;
 #pragma unroll 1
         for (int c0 = 0; c0 < n_mma; c0 += 16) {
+          // Parts in block (= k) order, the loads of up to kFixupParts of
+          // them in flight together; an empty run adds +0.
           float v[16];
-          bool first = true;
-#pragma unroll 1
-          for (int b = b_lo; b <= b_hi; ++b) {
-            const int ub = unit_start(b, U, grid);
-            if (unit_start(b + 1, U, grid) == ub) continue;
-            const float* part = p.partials + ((size_t)(2 * b + (sg.tile == ub / cpt ? 0 : 1)) * kM + qr) * NT + c0;
 #pragma unroll
-            for (int i = 0; i < 16; i += 4) {
-              const float4 f = __ldcg(reinterpret_cast<const float4*>(part + i));
-              if (first) {
-                v[i] = f.x, v[i + 1] = f.y, v[i + 2] = f.z, v[i + 3] = f.w;
-              } else {
-                v[i] += f.x, v[i + 1] += f.y, v[i + 2] += f.z, v[i + 3] += f.w;
-              }
+          for (int i = 0; i < 16; ++i) v[i] = 0.f;
+#pragma unroll 1
+          for (int b0 = b_lo; b0 <= b_hi; b0 += kFixupParts) {
+            float4 f[kFixupParts][4];
+#pragma unroll
+            for (int k = 0; k < kFixupParts; ++k) {
+              const int b = b0 + k;
+              const int ub = unit_start(b, U, grid);
+              const bool has = b <= b_hi && unit_start(b + 1, U, grid) > ub;
+              const float* part =
+                  p.partials + ((size_t)(2 * b + (has && sg.tile == ub / cpt ? 0 : 1)) * kM + qr) * NT + c0;
+#pragma unroll
+              for (int i = 0; i < 4; ++i)
+                f[k][i] = has ? __ldcg(reinterpret_cast<const float4*>(part + 4 * i)) : make_float4(0.f, 0.f, 0.f, 0.f);
             }
-            first = false;
+#pragma unroll
+            for (int k = 0; k < kFixupParts; ++k)
+#pragma unroll
+              for (int i = 0; i < 4; ++i) {
+                v[4 * i] += f[k][i].x;
+                v[4 * i + 1] += f[k][i].y;
+                v[4 * i + 2] += f[k][i].z;
+                v[4 * i + 3] += f[k][i].w;
+              }
           }
           epi_apply<T, EPI>(p, sg, qr, c0, v);
         }

@@ -152,7 +152,9 @@ __global__ void __launch_bounds__(kRouterBlockWarps * 32)
 
 // Router for prefill-sized batches: a block of kRouterWideWarps warps owns
 // kRouterWideTokens tokens, so each weight chunk is decoded once per 16
-// tokens, and the per-token arithmetic runs on packed fp32 pairs
+// tokens; each warp takes kRouterWideExperts experts at a time, so each
+// activation pair read from shared memory feeds four experts; the per-token
+// arithmetic runs on packed fp32 pairs
 // (mul.rn.f32x2 / add.rn.f32x2: two tokens' products and sums per
 // instruction, each lane of the pair rounded as the scalar op).  The order
 // per (token, expert) is router_kernel's: lane l, chunks l + 32j (j outer),
@@ -161,8 +163,9 @@ __global__ void __launch_bounds__(kRouterBlockWarps * 32)
 // p, element pair q of chunk c at float4 [(4p + q) * C + c] = (x[2p][8c+2q],
 // x[2p+1][8c+2q], x[2p][8c+2q+1], x[2p+1][8c+2q+1]); a warp's lanes read 32
 // consecutive float4 (no bank conflicts).
-constexpr int kRouterWideWarps = 16;
+constexpr int kRouterWideWarps = 8;
 constexpr int kRouterWideTokens = 16;
+constexpr int kRouterWideExperts = 4;
 
 __device__ __forceinline__ uint64_t f32x2_pack(float a, float b) {
   uint64_t r;
@@ -216,75 +219,98 @@ __global__ void __launch_bounds__(kRouterWideWarps * 32, 1)
     }
   }
   __syncthreads();
-  for (int e = warp; e < E; e += kRouterWideWarps) {
-    uint64_t acc[TP];
+  // A warp computes kRouterWideExperts experts at once, so each activation
+  // pair read from shared memory feeds that many products (shared-memory
+  // bandwidth, not the FP pipes, bounds the one-expert-per-warp form).
+  constexpr int EB = kRouterWideExperts;
+  for (int e0 = warp * EB; e0 < E; e0 += kRouterWideWarps * EB) {
+    uint64_t acc[EB][TP];
 #pragma unroll
-    for (int p = 0; p < TP; ++p) acc[p] = 0ull;  // (+0.f, +0.f)
+    for (int k = 0; k < EB; ++k)
+#pragma unroll
+      for (int p = 0; p < TP; ++p) acc[k][p] = 0ull;  // (+0.f, +0.f)
     // The next chunk's weights are loaded while this one is multiplied.
-    uint4 nd = make_uint4(0, 0, 0, 0);
-    uint32_t nword = 0;
-    __half nsc = __float2half(0.f), nbi = nsc;
+    uint4 nd[EB];
+    uint32_t nword[EB];
+    __half nsc[EB], nbi[EB];
     auto fetch = [&](int j) {
       const int c = lane + 32 * j;
-      if (DENSE) {
-        nd = ld_v4(wd + (int64_t)e * H + 8 * c);
-      } else {
-        nword = wq[(int64_t)e * (H / 8) + c];
-        nsc = ws[(int64_t)e * (H / 64) + c / 8];
-        nbi = wb[(int64_t)e * (H / 64) + c / 8];
+#pragma unroll
+      for (int k = 0; k < EB; ++k) {
+        const int e = e0 + k < E ? e0 + k : E - 1;  // past E: a valid row, results dropped
+        if (DENSE) {
+          nd[k] = ld_v4(wd + (int64_t)e * H + 8 * c);
+        } else {
+          nword[k] = wq[(int64_t)e * (H / 8) + c];
+          nsc[k] = ws[(int64_t)e * (H / 64) + c / 8];
+          nbi[k] = wb[(int64_t)e * (H / 64) + c / 8];
+        }
       }
     };
     fetch(0);
 #pragma unroll 1
     for (int j = 0; j < J; ++j) {
       const int c = lane + 32 * j;
-      float wf[8];
-      if (DENSE) {
-        unpack8<T>(nd, wf);
-      } else {
-        const uint32_t word = nword;
-        const float sc = __half2float(nsc);
-        const float bi = __half2float(nbi);
+      uint64_t w2[EB][8];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const float code = (float)((word >> (4 * i)) & 0xFu);
-          wf[i] = __half2float(__float2half_rn(__fadd_rn(__fmul_rn(code, sc), bi)));
+      for (int k = 0; k < EB; ++k) {
+        float wf[8];
+        if (DENSE) {
+          unpack8<T>(nd[k], wf);
+        } else {
+          const uint32_t word = nword[k];
+          const float sc = __half2float(nsc[k]);
+          const float bi = __half2float(nbi[k]);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const float code = (float)((word >> (4 * i)) & 0xFu);
+            wf[i] = __half2float(__float2half_rn(__fadd_rn(__fmul_rn(code, sc), bi)));
+          }
         }
+#pragma unroll
+        for (int i = 0; i < 8; ++i) w2[k][i] = f32x2_pack(wf[i], wf[i]);
       }
       if (j + 1 < J) fetch(j + 1);
-      uint64_t w2[8];
-#pragma unroll
-      for (int i = 0; i < 8; ++i) w2[i] = f32x2_pack(wf[i], wf[i]);
 #pragma unroll
       for (int p = 0; p < TP; ++p) {
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
           const float4 v = xs4[(size_t)(4 * p + q) * C + c];
-          acc[p] = f32x2_mul_add(acc[p], f32x2_pack(v.x, v.y), w2[2 * q]);
-          acc[p] = f32x2_mul_add(acc[p], f32x2_pack(v.z, v.w), w2[2 * q + 1]);
+          const uint64_t lo = f32x2_pack(v.x, v.y), hi = f32x2_pack(v.z, v.w);
+#pragma unroll
+          for (int k = 0; k < EB; ++k) {
+            acc[k][p] = f32x2_mul_add(acc[k][p], lo, w2[k][2 * q]);
+            acc[k][p] = f32x2_mul_add(acc[k][p], hi, w2[k][2 * q + 1]);
+          }
         }
       }
     }
 #pragma unroll
-    for (int p = 0; p < TP; ++p) {
-      float a0, a1;
-      f32x2_unpack(acc[p], a0, a1);
-      const float l0 = round_act<T>(warp_sum_butterfly(a0));
-      const float l1 = round_act<T>(warp_sum_butterfly(a1));
-      if (lane == 0) {
-        const int t = 2 * p;
-        ls[t * 64 + e] = l0;
-        ls[(t + 1) * 64 + e] = l1;
-        if (logits && t0 + t < tokens) logits[(t0 + t) * E + e] = from_f<T>(l0);
-        if (logits && t0 + t + 1 < tokens) logits[(t0 + t + 1) * E + e] = from_f<T>(l1);
+    for (int k = 0; k < EB; ++k) {
+      const int e = e0 + k;
+#pragma unroll
+      for (int p = 0; p < TP; ++p) {
+        float a0, a1;
+        f32x2_unpack(acc[k][p], a0, a1);
+        const float l0 = round_act<T>(warp_sum_butterfly(a0));
+        const float l1 = round_act<T>(warp_sum_butterfly(a1));
+        if (lane == 0 && e < E) {
+          const int t = 2 * p;
+          ls[t * 64 + e] = l0;
+          ls[(t + 1) * 64 + e] = l1;
+          if (logits && t0 + t < tokens) logits[(t0 + t) * E + e] = from_f<T>(l0);
+          if (logits && t0 + t + 1 < tokens) logits[(t0 + t + 1) * E + e] = from_f<T>(l1);
+        }
       }
     }
   }
   __syncthreads();
-  if (idx && warp < kRouterWideTokens && t0 + warp < tokens) {
-    const float la0 = lane < E ? ls[warp * 64 + lane] : 0.f;
-    const float la1 = lane + 32 < E ? ls[warp * 64 + lane + 32] : 0.f;
-    route_token<T>(lane, la0, la1, E, K, t0 + warp, (T*)nullptr, idx, gates);
+  if (idx) {
+    for (int t = warp; t < kRouterWideTokens && t0 + t < tokens; t += kRouterWideWarps) {
+      const float la0 = lane < E ? ls[t * 64 + lane] : 0.f;
+      const float la1 = lane + 32 < E ? ls[t * 64 + lane + 32] : 0.f;
+      route_token<T>(lane, la0, la1, E, K, t0 + t, (T*)nullptr, idx, gates);
+    }
   }
 }
 
