@@ -409,7 +409,8 @@ static tf_status check_moe(const tf_moe_args* a) {
 // counters_zero: the caller guarantees the split counters are zero (a
 // session's scratch, zeroed once and left zero by every completed launch);
 // otherwise they are cleared first.
-static tf_status run_moe(const tf_moe_args* a, const MoePlan& p, cudaStream_t s, bool counters_zero = false) {
+static tf_status run_moe(const tf_moe_args* a, const MoePlan& p, cudaStream_t s, bool counters_zero = false,
+                         const MoeNextNorm* next = nullptr) {
   const int64_t N = a->tokens * a->top_k;
   if (p.counters && !counters_zero)
     TF_CUDA(cudaMemsetAsync(p.counters, 0, (size_t)kQmmSplitCounters * sizeof(int), s));
@@ -476,7 +477,7 @@ static tf_status run_moe(const tf_moe_args* a, const MoePlan& p, cudaStream_t s,
   trace(PH_DOWN, false, s);
   trace(PH_COMBINE, true, s);
   TF_TRY(launch_combine(p.y, p.inverse, p.gates, a->residual, a->tokens, a->top_k, a->hidden, a->act,
-                        a->out, s));
+                        a->out, s, next ? next->w : nullptr, next ? next->eps : 0.f, next ? next->out : nullptr));
   trace(PH_COMBINE, false, s);
   return TF_OK;
 }
@@ -485,12 +486,13 @@ static tf_status run_moe(const tf_moe_args* a, const MoePlan& p, cudaStream_t s,
 
 namespace tf {
 size_t moe_workspace_bytes(const tf_moe_args* a, bool with_split) { return plan_moe(a, nullptr, 0, with_split).used; }
-tf_status moe_run(const tf_moe_args* a, void* ws, size_t ws_bytes, cudaStream_t s, bool counters_zero) {
+tf_status moe_run(const tf_moe_args* a, void* ws, size_t ws_bytes, cudaStream_t s, bool counters_zero,
+                  const MoeNextNorm* next) {
   if (a->tokens == 0) return TF_OK;
   const bool split = plan_moe(a, nullptr, 0, true).used <= ws_bytes;
   const MoePlan p = plan_moe(a, ws, ws_bytes, split);
   if (p.used > ws_bytes) return set_error(TF_ERR_INVALID_ARGUMENT, "moe: workspace too small");
-  return run_moe(a, p, s, counters_zero);
+  return run_moe(a, p, s, counters_zero, next);
 }
 }  // namespace tf
 

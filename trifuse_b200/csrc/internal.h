@@ -206,9 +206,12 @@ tf_status launch_gather_rows(const void* x, int64_t x_stride, const int32_t* idx
                              int act, void* y, cudaStream_t s);
 
 // ---------------------------------------------------------------- combine
+// With norm_out, also norm_out = RMSNorm(out) * norm_w (the next layer's
+// input norm, in rms_norm_kernel's order, bit-identical to it).
 tf_status launch_combine(const void* y_sorted, const int32_t* inverse, const void* gates,
                          const void* residual, int64_t tokens, int k, int hidden, int act,
-                         void* out, cudaStream_t s);
+                         void* out, cudaStream_t s, const void* norm_w = nullptr, float eps = 0.f,
+                         void* norm_out = nullptr);
 
 // ---------------------------------------------------------------- MoE block
 // with_split adds the tensor-core split buffers (about 10 MB).
@@ -216,7 +219,14 @@ size_t moe_workspace_bytes(const tf_moe_args* a, bool with_split = true);
 // Runs the block on a workspace of at least moe_workspace_bytes(a, false),
 // with the split schedule when it holds moe_workspace_bytes(a, true).
 // counters_zero: the workspace's split counters are known to be zero.
-tf_status moe_run(const tf_moe_args* a, void* ws, size_t ws_bytes, cudaStream_t s, bool counters_zero = false);
+// The next layer's input RMSNorm fused into the block's combine.
+struct MoeNextNorm {
+  const void* w = nullptr;
+  float eps = 0.f;
+  void* out = nullptr;
+};
+tf_status moe_run(const tf_moe_args* a, void* ws, size_t ws_bytes, cudaStream_t s, bool counters_zero = false,
+                  const MoeNextNorm* next = nullptr);
 
 // ---------------------------------------------------------------- attention
 // Row r (one query token) of request req[r] (r when req == NULL) at absolute

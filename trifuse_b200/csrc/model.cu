@@ -594,14 +594,18 @@ tf_status forward_rows(tf_session* s, int64_t rows, bool req_ident, int max_len,
   trace(PH_EMBED, true, st);
   TF_TRY(launch_embedding(s->ids, rows, m->embed, c.act, s->h0, st));
   trace(PH_EMBED, false, st);
+  bool normed = false;  // s->xn already holds this layer's input norm (fused into the previous combine)
   for (int l = 0; l < c.layers; ++l) {
     if (s->cancelled.load()) return set_error(TF_ERR_CANCELLED, "cancelled before layer %d", l);
     const LayerW& L = m->layers[l];
     // Last layer of a prefill: queries of the requests' last rows only.
     const bool lq = last && nlast < rows && l == c.layers - 1;
-    trace(PH_INPUT_NORM, true, st);
-    TF_TRY(launch_rms_norm(s->h0, rows, H, L.input_norm, c.rms_eps, c.act, s->xn, st));
-    trace(PH_INPUT_NORM, false, st);
+    if (!normed) {
+      trace(PH_INPUT_NORM, true, st);
+      TF_TRY(launch_rms_norm(s->h0, rows, H, L.input_norm, c.rms_eps, c.act, s->xn, st));
+      trace(PH_INPUT_NORM, false, st);
+    }
+    normed = false;
     QmmProblem q;
     q.mode = QMM_DENSE;
     q.act = c.act;
@@ -687,7 +691,17 @@ tf_status forward_rows(tf_session* s, int64_t rows, bool req_ident, int max_len,
     ma.down_proj = L.down;
     const bool capture = rows <= s->capture_rows;
     if (capture && s->route_capture) ma.indices = s->route_capture + (size_t)l * rows * c.top_k;
-    TF_TRY(moe_run(&ma, s->moe_ws, s->moe_ws_bytes, st, /*counters_zero=*/true));
+    // The next layer's input norm runs in this block's combine when this
+    // block produced every row (not the last-query-only layer).
+    MoeNextNorm nn;
+    const bool fuse = l + 1 < c.layers && n == rows && H % 256 == 0 && H <= 8192;
+    if (fuse) {
+      nn.w = m->layers[l + 1].input_norm;
+      nn.eps = c.rms_eps;
+      nn.out = s->xn;
+    }
+    TF_TRY(moe_run(&ma, s->moe_ws, s->moe_ws_bytes, st, /*counters_zero=*/true, fuse ? &nn : nullptr));
+    normed = fuse;
     if (capture && s->hidden_capture)
       TF_CUDA(cudaMemcpyAsync(static_cast<char*>(s->hidden_capture) + (size_t)l * rows * H * act_bytes(c.act), s->h0,
                               (size_t)n * H * act_bytes(c.act), cudaMemcpyDeviceToDevice, st));

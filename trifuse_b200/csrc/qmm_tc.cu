@@ -136,6 +136,9 @@ struct Params {
   int y_f16;
   const void* residual;
   int64_t residual_stride;
+  // Outputs (and residual) allow 16-byte vector access: the epilogue stages
+  // each warp's 32 rows x 16 tokens in shared memory and stores vectors.
+  int vec_out;
   // Split schedule (stream-K over chunks): each block takes an equal run of
   // the (tile, chunk) sequence; a tile split across blocks is finished by
   // the last of them to arrive (counters[tile], zero at launch and left zero)
@@ -249,7 +252,8 @@ struct Layout {
   static constexpr int kOffS = (kHead + 1023) / 1024 * 1024;
   static constexpr int kOffP = (kOffS + 2 * kS + 1023) / 1024 * 1024;
   static constexpr int kOffB = kOffP + PK * kP;
-  static constexpr int kBytes = kOffB + SB * kB + 1024;  // + alignment slack
+  static constexpr int kOffE = kOffB + SB * kB;  // epilogue staging: 4 warps x 2 KB
+  static constexpr int kBytes = kOffE + 4 * 2048 + 1024;  // + alignment slack
   // TMEM columns: accumulators [0, 2 NT), A stages from 2 NT on.
   static constexpr int kAStage = KS * kACols;
   static constexpr int kACol0 = 2 * NT;
@@ -350,6 +354,106 @@ __device__ __forceinline__ void epi_apply(const Params& p, const Seg& sg, int q,
   }
 }
 
+// Staged epilogue of 16 accumulator columns (tokens c0 .. c0 + 15) of the
+// warp's 32 TMEM lanes: the values go through the warp's 2 KB of shared
+// memory so that each lane then stores 16-byte vectors of consecutive
+// outputs of one token (the direct form stores one value per token and row;
+// at 192-token tiles its per-output instructions starved the epilogue warps
+// of issue slots and bounded the whole tile).  Same values as epi_apply.
+// res: EPI_RESIDUAL only, the residual vectors of this lane's two (token,
+// 8-row) pieces, loaded ahead by the caller (epi_residual_vec).
+template <typename T>
+__device__ __forceinline__ void epi_residual_vec(const Params& p, const Seg& sg, int wq, int lane, int c0, uint4* res) {
+  const int f0 = sg.rb * kM + wq * 32;
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const int k = lane + 32 * h, t = k >> 2, g = k & 3;
+    res[h] = make_uint4(0, 0, 0, 0);
+    if (c0 + t < sg.cnt && f0 + 8 * g < p.out)
+      res[h] = ld_v4(static_cast<const T*>(p.residual) + ((int64_t)(sg.s0 + c0 + t) * p.residual_stride + f0 + 8 * g));
+  }
+}
+
+template <typename T, int EPI>
+__device__ __forceinline__ void epi_staged(const Params& p, const Seg& sg, int wq, int lane, int c0, const float* v,
+                                           uint8_t* stage, const uint4* res) {
+  if (EPI == EPI_SWIGLU) {
+    // 16 features (lane pairs) x 16 tokens; the even lane of a pair finishes
+    // tokens 0-7, the odd one 8-15 (as epi_apply).
+    const int base = sg.rb * (kM / 2) + wq * 16;  // the warp's first feature (a multiple of 8)
+    const int f = base + (lane >> 1);
+    const int col = (p.y_f16 ? perm_col(f) : f) - base;
+    const int odd = lane & 1;
+    bool wide = false;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float mine = odd ? v[8 + i] : v[i];
+      const float theirs = __shfl_xor_sync(0xffffffffu, odd ? v[i] : v[8 + i], 1);
+      const float gg = round_act<T>(odd ? theirs : mine);
+      const float uu = round_act<T>(odd ? mine : theirs);
+      const float sl = round_act<T>(__fdividef(gg, 1.0f + __expf(-gg)));
+      const float hv = round_act<T>(sl * uu);
+      const int t = i + 8 * odd;
+      if (p.y_f16) {
+        wide |= c0 + t < sg.cnt && f < p.out && fabsf(hv) > 65504.f;
+        reinterpret_cast<__half*>(stage)[t * 16 + col] = __float2half_rn(hv);
+      } else {
+        reinterpret_cast<T*>(stage)[t * 16 + col] = from_f<T>(hv);
+      }
+    }
+    __syncwarp();
+    const int t = lane >> 1, g = lane & 1;
+    const uint4 val = *reinterpret_cast<const uint4*>(stage + (t * 16 + 8 * g) * 2);
+    if (c0 + t < sg.cnt && base + 8 * g < p.out)
+      *reinterpret_cast<uint4*>(static_cast<uint8_t*>(p.y) +
+                                ((int64_t)(sg.s0 + c0 + t) * p.y_stride + base + 8 * g) * 2) = val;
+    __syncwarp();
+    // The f16 operand of the down projection: a bf16 value beyond the f16
+    // range became inf there, which records device error 5.
+    if (wide) atomicCAS(&g_tc_error, 0, 5);
+  } else if (EPI == EPI_F32) {
+    float* st = reinterpret_cast<float*>(stage);
+#pragma unroll
+    for (int i = 0; i < 16; ++i) st[i * 32 + lane] = round_act<T>(v[i]);
+    __syncwarp();
+    const int f0 = sg.rb * kM + wq * 32;
+#pragma unroll
+    for (int h = 0; h < 4; ++h) {
+      const int k = lane + 32 * h, t = k >> 3, g = k & 7;
+      const float4 val = *reinterpret_cast<const float4*>(st + t * 32 + 4 * g);
+      if (c0 + t < sg.cnt && f0 + 4 * g < p.out)
+        *reinterpret_cast<float4*>(static_cast<float*>(p.y) + ((int64_t)(sg.s0 + c0 + t) * p.y_stride + f0 + 4 * g)) =
+            val;
+    }
+    __syncwarp();
+  } else {
+    T* st = reinterpret_cast<T*>(stage);
+#pragma unroll
+    for (int i = 0; i < 16; ++i) st[i * 32 + lane] = from_f<T>(v[i]);  // act(acc)
+    __syncwarp();
+    const int f0 = sg.rb * kM + wq * 32;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int k = lane + 32 * h, t = k >> 2, g = k & 3;
+      uint4 val = *reinterpret_cast<const uint4*>(st + t * 32 + 8 * g);
+      if (c0 + t < sg.cnt && f0 + 8 * g < p.out) {
+        const int64_t slot = sg.s0 + c0 + t;
+        if (EPI == EPI_RESIDUAL) {
+          float a[8], r[8];
+          unpack8<T>(val, a);
+          unpack8<T>(res[h], r);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) a[i] = r[i] + a[i];
+          val = pack8<T>(a);
+        }
+        const int64_t orow = EPI == EPI_PLAIN && p.y_index ? (int64_t)p.y_index[slot] : slot;
+        *reinterpret_cast<uint4*>(static_cast<T*>(p.y) + (orow * p.y_stride + f0 + 8 * g)) = val;
+      }
+    }
+    __syncwarp();
+  }
+}
+
 template <typename T, int EPI, bool PERM, int NT, int KS, int PK, int SA, int SB, int G, int H, int BPS>
 __global__ void __launch_bounds__(Roles<G * H, BPS>::kThreads, BPS)
     qmm_tc_kernel(const __grid_constant__ Params p) {
@@ -381,6 +485,7 @@ __global__ void __launch_bounds__(Roles<G * H, BPS>::kThreads, BPS)
   uint8_t* ring_s = base + L::kOffS;  // [2 slots][s | b][kM rows][8 k-steps] f16
   uint8_t* ring_p = base + L::kOffP;
   uint8_t* ring_b = base + L::kOffB;
+  uint8_t* ring_e = base + L::kOffE;
   const int nk = p.in / kKStep;  // a multiple of 8
   const int cpt = nk / kSK;      // chunks per tile
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -732,6 +837,24 @@ __global__ void __launch_bounds__(Roles<G * H, BPS>::kThreads, BPS)
       tc_fence_after();
       const int n_mma = (sg.cnt + 15) / 16 * 16;
       const uint32_t taddr = tmem + ((uint32_t)(wq * 32) << 16) + (uint32_t)(buf * NT);
+      if (sg.slot < 0 && p.vec_out) {
+        uint8_t* stage = ring_e + wq * 2048;
+        uint4 res[2], nres[2];
+        if (EPI == EPI_RESIDUAL) epi_residual_vec<T>(p, sg, wq, lane, 0, nres);
+        for (int c0 = 0; c0 < n_mma; c0 += 16) {
+          float v[16];
+          tmem_ld16(taddr + c0, v);
+          if (EPI == EPI_RESIDUAL) {
+            res[0] = nres[0], res[1] = nres[1];
+            if (c0 + 16 < n_mma) epi_residual_vec<T>(p, sg, wq, lane, c0 + 16, nres);
+          }
+          epi_staged<T, EPI>(p, sg, wq, lane, c0, v, stage, res);
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&acc_empty[buf]);
+        continue;
+      }
       if (sg.slot < 0) {
         if (EPI == EPI_RESIDUAL) {
           // Residual tiles: each 8 tokens' residual loads issue before the
@@ -824,7 +947,13 @@ __global__ void __launch_bounds__(Roles<G * H, BPS>::kThreads, BPS)
                 v[4 * i + 3] += f[k][i].w;
               }
           }
-          epi_apply<T, EPI>(p, sg, qr, c0, v);
+          if (p.vec_out) {
+            uint4 res[2];
+            if (EPI == EPI_RESIDUAL) epi_residual_vec<T>(p, sg, wq, lane, c0, res);
+            epi_staged<T, EPI>(p, sg, wq, lane, c0, v, ring_e + wq * 2048, res);
+          } else {
+            epi_apply<T, EPI>(p, sg, qr, c0, v);
+          }
         }
       }
       if (lane == 0) *counter = 0;  // left at zero for the next launch
@@ -1012,6 +1141,14 @@ tf_status launch_qmm_tc(const QmmProblem& q, cudaStream_t s) {
   p.y_f16 = q.y_f16;
   p.residual = q.residual;
   p.residual_stride = q.residual_stride;
+  {
+    const int eb = q.epilogue == EPI_F32 ? 4 : (q.epilogue == EPI_SWIGLU && q.y_f16) ? 2 : act_bytes(q.act);
+    const int vw = 16 / eb;  // elements per 16-byte vector
+    bool ok = (reinterpret_cast<uintptr_t>(q.y) & 15) == 0 && q.y_stride % vw == 0 && out % vw == 0;
+    if (q.epilogue == EPI_RESIDUAL)
+      ok = ok && (reinterpret_cast<uintptr_t>(q.residual) & 15) == 0 && q.residual_stride % vw == 0;
+    p.vec_out = ok ? 1 : 0;
+  }
   // Token tile: about the tokens each weight matrix serves.
   const int64_t per_matrix = p.grouped ? (q.n + experts - 1) / experts : q.n;
   const int nt = per_matrix <= 24 ? 32 : per_matrix <= 64 ? 64 : 192;
