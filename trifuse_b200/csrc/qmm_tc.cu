@@ -100,7 +100,8 @@ constexpr int kKStep = 64;
 constexpr int kSK = 8;          // k-steps per scale slot (16 bytes of f16 per row) = one work chunk
 constexpr int kMaxSegs = 128;   // per-block segment table
 constexpr int kMaxExperts = 256;
-constexpr int kFixupParts = 2;  // partial tiles read per round trip in the split fixup
+constexpr int kFixupParts = 2;
+constexpr int kSS = 3;  // scale slots: the loader fetches a chunk's scales one chunk ahead of its codes  // partial tiles read per round trip in the split fixup
 constexpr int kACols = kKStep / 2;   // TMEM columns of one k-step of A (two f16 per column)
 // Fixed limit of the waits that drain a block's own copies and MMAs before
 // it exits (not shortened by tf_set_wait_limit: copies in flight always land).
@@ -250,7 +251,7 @@ struct Layout {
   static constexpr int kOffSeg = 1024;
   static constexpr int kHead = kOffSeg + kMaxSegs * (int)sizeof(Seg);
   static constexpr int kOffS = (kHead + 1023) / 1024 * 1024;
-  static constexpr int kOffP = (kOffS + 2 * kS + 1023) / 1024 * 1024;
+  static constexpr int kOffP = (kOffS + kSS * kS + 1023) / 1024 * 1024;
   static constexpr int kOffB = kOffP + PK * kP;
   static constexpr int kOffE = kOffB + SB * kB;  // epilogue staging: 4 warps x 2 KB
   static constexpr int kBytes = kOffE + 4 * 2048 + 1024;  // + alignment slack
@@ -263,7 +264,7 @@ struct Layout {
   static_assert(4 * (kMaxExperts + 1) * 4 <= PK * kP, "setup expert table fits the code ring");
   static_assert(H == 1 || H == 2, "one or two threads per weight row and k-step");
   // mbarriers (then the TMEM slot and segment count) below the wait control at 448.
-  static_assert((2 * PK + 2 * SA + 2 * SB + 9) * 8 + 8 <= 448, "barrier block fits below the wait control");
+  static_assert((2 * PK + 2 * SA + 2 * SB + 2 * kSS + 5) * 8 + 8 <= 448, "barrier block fits below the wait control");
 };
 
 // Residual values of the 8 tokens c0 .. c0 + 7 of TMEM lane q's row (0 past
@@ -469,8 +470,8 @@ __global__ void __launch_bounds__(Roles<G * H, BPS>::kThreads, BPS)
   uint64_t* p_full = reinterpret_cast<uint64_t*>(base);
   uint64_t* p_empty = p_full + PK;
   uint64_t* s_full = p_empty + PK;
-  uint64_t* s_empty = s_full + 2;
-  uint64_t* a_full = s_empty + 2;  // A stage in TMEM written (dequant warps of one group)
+  uint64_t* s_empty = s_full + kSS;
+  uint64_t* a_full = s_empty + kSS;  // A stage in TMEM written (dequant warps of one group)
   uint64_t* a_empty = a_full + SA;  // A stage read by its MMAs (commit)
   uint64_t* b_full = a_empty + SA;  // activation stage landed (TMA)
   uint64_t* b_empty = b_full + SB;  // activation stage read by its MMAs (commit)
@@ -482,7 +483,7 @@ __global__ void __launch_bounds__(Roles<G * H, BPS>::kThreads, BPS)
   int* nsegs_s = reinterpret_cast<int*>(tmem_slot + 1);
   int* units_s = reinterpret_cast<int*>(base + 512);
   Seg* segs = reinterpret_cast<Seg*>(base + L::kOffSeg);
-  uint8_t* ring_s = base + L::kOffS;  // [2 slots][s | b][kM rows][8 k-steps] f16
+  uint8_t* ring_s = base + L::kOffS;  // [kSS slots][s | b][kM rows][8 k-steps] f16
   uint8_t* ring_p = base + L::kOffP;
   uint8_t* ring_b = base + L::kOffB;
   uint8_t* ring_e = base + L::kOffE;
@@ -496,9 +497,11 @@ __global__ void __launch_bounds__(Roles<G * H, BPS>::kThreads, BPS)
       mbar_init(&p_full[i], 1);
       mbar_init(&p_empty[i], kGroupWarps);
     }
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < kSS; ++i) {
       mbar_init(&s_full[i], 1);
       mbar_init(&s_empty[i], kDeqWarps);  // every group uses every scale block
+    }
+    for (int i = 0; i < 2; ++i) {
       mbar_init(&acc_full[i], 1);
       mbar_init(&acc_empty[i], kEpiWarps);
     }
@@ -658,23 +661,43 @@ __global__ void __launch_bounds__(Roles<G * H, BPS>::kThreads, BPS)
     // dequant warps) and the scales of every chunk.  Activation tiles have
     // their own warp, so the weight stream never waits on the MMA.
     if (lane == 0) {
-      int g = 0, gs = 0;  // stage and scale-block counters (< 2^31 per block)
+      int g = 0;  // stage counter (< 2^31 per block)
       bool ok = true;
+      // Scale cursor: the next chunk (segment sj, chunk sc) whose scales to
+      // fetch, gsi chunks fetched so far.  Scales run one chunk ahead of the
+      // codes, so a group's first stage of a chunk never waits for them
+      // behind the previous chunk's code stages.
+      int sj = 0, sc = nsegs > 0 ? segs[0].kc0 : 0, gsi = 0;
+      auto fetch_scales = [&]() -> bool {
+        while (sj < nsegs && sc >= segs[sj].kc1) {
+          ++sj;
+          if (sj < nsegs) sc = segs[sj].kc0;
+        }
+        if (sj >= nsegs) return true;
+        const Seg& ssg = segs[sj];
+        const int row0s = ssg.e * p.out + ssg.rb * kTileRows;
+        const int k8 = sc * kSK;
+        const int ss = gsi % kSS;
+        if (gsi >= kSS && !mbar_wait(&s_empty[ss], (uint32_t)(((gsi / kSS) - 1) & 1), wctl, 11)) return false;
+        uint8_t* sdst = ring_s + (size_t)ss * L::kS;
+        mbar_expect_tx(&s_full[ss], (uint32_t)L::kS);
+        tma_2d(sdst, &p.tm_s0, k8, row0s, &s_full[ss]);
+        tma_2d(sdst + kM * kSK * 2, &p.tm_b0, k8, row0s, &s_full[ss]);
+        if (kSw) {
+          tma_2d(sdst + 64 * kSK * 2, &p.tm_s1, k8, row0s, &s_full[ss]);
+          tma_2d(sdst + kM * kSK * 2 + 64 * kSK * 2, &p.tm_b1, k8, row0s, &s_full[ss]);
+        }
+        ++sc;
+        ++gsi;
+        return true;
+      };
+      ok = fetch_scales();
       for (int j = 0; j < nsegs && ok; ++j) {
         const Seg sg = segs[j];
         const int row0 = sg.e * p.out + sg.rb * kTileRows;
-        for (int c = sg.kc0; c < sg.kc1 && ok; ++c, ++gs) {
+        for (int c = sg.kc0; c < sg.kc1 && ok; ++c) {
           const int k8 = c * kSK;
-          const int ss = gs & 1;
-          if (gs >= 2 && !(ok = mbar_wait(&s_empty[ss], (uint32_t)(((gs >> 1) - 1) & 1), wctl, 11))) break;
-          uint8_t* sdst = ring_s + (size_t)ss * L::kS;
-          mbar_expect_tx(&s_full[ss], (uint32_t)L::kS);
-          tma_2d(sdst, &p.tm_s0, k8, row0, &s_full[ss]);
-          tma_2d(sdst + kM * kSK * 2, &p.tm_b0, k8, row0, &s_full[ss]);
-          if (kSw) {
-            tma_2d(sdst + 64 * kSK * 2, &p.tm_s1, k8, row0, &s_full[ss]);
-            tma_2d(sdst + kM * kSK * 2 + 64 * kSK * 2, &p.tm_b1, k8, row0, &s_full[ss]);
-          }
+          if (!(ok = fetch_scales())) break;  // the next chunk's
           for (int ks = 0; ks < kSK && ok; ks += KS, ++g) {
             const int ps = g % PK;
             if (g >= PK && !(ok = mbar_wait(&p_empty[ps], (uint32_t)(((g / PK) - 1) & 1), wctl, 12))) break;
@@ -688,7 +711,7 @@ __global__ void __launch_bounds__(Roles<G * H, BPS>::kThreads, BPS)
       // Every copy issued into the rings lands before the block may exit
       // (after an expired wait the consumers are gone but the copies are not).
       for (int i = g - 1; i >= 0 && i >= g - PK; --i) mbar_drain(&p_full[i % PK], (uint32_t)((i / PK) & 1));
-      for (int i = gs - 1; i >= 0 && i >= gs - 2; --i) mbar_drain(&s_full[i & 1], (uint32_t)((i >> 1) & 1));
+      for (int i = gsi - 1; i >= 0 && i >= gsi - kSS; --i) mbar_drain(&s_full[i % kSS], (uint32_t)((i / kSS) & 1));
     }
   } else if (warp == kActWarp) {
     // ---- activation loader: lane 0 streams each stage's activation tiles
@@ -736,8 +759,8 @@ __global__ void __launch_bounds__(Roles<G * H, BPS>::kThreads, BPS)
       const int sb = g % kSpb;
       const int blk = g / kSpb;
       if (sb == grp % kSpb) {  // this group's first stage of a scale block
-        if (!(ok = warp_wait(&s_full[blk & 1], (uint32_t)((blk >> 1) & 1), wctl, 21))) break;
-        const uint8_t* sslot = ring_s + (size_t)(blk & 1) * L::kS;
+        if (!(ok = warp_wait(&s_full[blk % kSS], (uint32_t)((blk / kSS) & 1), wctl, 21))) break;
+        const uint8_t* sslot = ring_s + (size_t)(blk % kSS) * L::kS;
         sv = *reinterpret_cast<const uint4*>(sslot + pr * 16);
         bv = *reinterpret_cast<const uint4*>(sslot + kM * kSK * 2 + pr * 16);
       }
@@ -784,7 +807,7 @@ __global__ void __launch_bounds__(Roles<G * H, BPS>::kThreads, BPS)
       if (lane == 0) {
         mbar_arrive(&a_full[as]);
         mbar_arrive(&p_empty[ps]);
-        if (sb + G >= kSpb) mbar_arrive(&s_empty[blk & 1]);
+        if (sb + G >= kSpb) mbar_arrive(&s_empty[blk % kSS]);
       }
     }
   } else if (warp == kMmaWarp) {
