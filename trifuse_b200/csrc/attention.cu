@@ -57,20 +57,34 @@ __device__ float block_row_sumsq(const T* row, int W, float* tot_s, float* bcast
   return v;
 }
 
+// RoPE angles of every position below `positions`: tab[p][d] = (cos, sin)
+// of fp32(p * theta^(-2d/D)), the values the append kernel computes.
+__global__ void rope_table_kernel(float theta, int positions, float2* __restrict__ tab) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (int64_t)positions * (kHeadDim / 2)) return;
+  const int p = (int)(i / (kHeadDim / 2)), d = (int)(i % (kHeadDim / 2));
+  const float inv = (float)pow((double)theta, -2.0 * (double)d / (double)kHeadDim);
+  float sn, cs;
+  sincosf(__fmul_rn((float)p, inv), &sn, &cs);
+  tab[i] = make_float2(cs, sn);
+}
+
 template <typename T>
 __global__ void __launch_bounds__(kAttnThreads)
     attn_append_kernel(const T* __restrict__ qkv, int heads, const __half* __restrict__ qn,
                        const __half* __restrict__ kn, float eps, float theta,
                        const int32_t* __restrict__ pos, const int32_t* __restrict__ req,
-                       __half* k_cache, __half* v_cache, int cap, T* __restrict__ q_out) {
+                       __half* k_cache, __half* v_cache, int cap, T* __restrict__ q_out,
+                       const float2* __restrict__ rope) {
   __shared__ float tot_s[64];
   __shared__ float bcast;
   __shared__ float inv_s[kHeadDim / 2];  // RoPE inverse frequencies theta^(-2d/D)
   const int64_t r = blockIdx.x;
   const int t = threadIdx.x;
   const int W = heads * kHeadDim;
-  for (int d = t; d < kHeadDim / 2; d += kAttnThreads)
-    inv_s[d] = (float)pow((double)theta, -2.0 * (double)d / (double)kHeadDim);  // (synced below)
+  if (!rope)
+    for (int d = t; d < kHeadDim / 2; d += kAttnThreads)
+      inv_s[d] = (float)pow((double)theta, -2.0 * (double)d / (double)kHeadDim);  // (synced below)
   const T* qrow = qkv + r * 3 * W;
   const T* krow = qrow + W;
   const T* vrow = qrow + 2 * W;
@@ -82,9 +96,13 @@ __global__ void __launch_bounds__(kAttnThreads)
   for (int i = t; i < W / 2; i += kAttnThreads) {
     const int h = i / (kHeadDim / 2), d = i % (kHeadDim / 2);
     const int i1 = h * kHeadDim + d, i2 = i1 + kHeadDim / 2;
-    const float inv = inv_s[d];
     float sn, cs;
-    sincosf(__fmul_rn(fp, inv), &sn, &cs);
+    if (rope) {
+      const float2 a = rope[(int64_t)p * (kHeadDim / 2) + d];
+      cs = a.x, sn = a.y;
+    } else {
+      sincosf(__fmul_rn(fp, inv_s[d]), &sn, &cs);
+    }
     {
       const float x1 = round_act<T>(__fmul_rn(__fmul_rn(to_f(qrow[i1]), rq), __half2float(qn[i1])));
       const float x2 = round_act<T>(__fmul_rn(__fmul_rn(to_f(qrow[i2]), rq), __half2float(qn[i2])));
@@ -250,6 +268,13 @@ __global__ void __launch_bounds__(kHeadDim)
 }
 
 // ---------------------------------------------------------------------------
+tf_status launch_rope_table(float theta, int positions, void* tab, cudaStream_t s) {
+  const int64_t n = (int64_t)positions * (kHeadDim / 2);
+  if (n == 0) return TF_OK;
+  rope_table_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(theta, positions, (float2*)tab);
+  return check_launch("rope_table");
+}
+
 size_t attention_ws_bytes(int64_t rows, int heads, int capacity, int act) {
   const int64_t nsplit = (capacity + kSplit - 1) / kSplit;
   const int64_t parts = rows * heads * nsplit;
@@ -273,7 +298,7 @@ static tf_status attention_impl(const AttnProblem& a, cudaStream_t s) {
   float* po = c.take<float>(parts * kHeadDim * 4);
   attn_append_kernel<T><<<(unsigned)a.rows, kAttnThreads, 0, s>>>(
       (const T*)a.qkv, a.heads, (const __half*)a.q_norm, (const __half*)a.k_norm, a.eps, a.theta,
-      a.pos, a.req, (__half*)a.k_cache, (__half*)a.v_cache, a.capacity, qr);
+      a.pos, a.req, (__half*)a.k_cache, (__half*)a.v_cache, a.capacity, qr, (const float2*)a.rope);
   TF_TRY(check_launch("attn_append"));
   // Queries: every row, or only the rows a.qrows lists (output row i for
   // a.qrows[i]); none when a.nq == 0 (the rows only extend the cache).

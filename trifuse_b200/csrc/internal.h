@@ -240,6 +240,10 @@ struct AttnProblem {
   const void* k_norm = nullptr;
   float eps = 1e-5f;
   float theta = 10000.f;
+  // Optional: (cos, sin) of every position below capacity, [capacity][64]
+  // float2 from launch_rope_table with the same theta (bit-identical to the
+  // kernel's own sincosf).
+  const void* rope = nullptr;
   const int32_t* pos = nullptr;  // device [rows]
   const int32_t* req = nullptr;  // device [rows] or NULL
   int max_len = 0;               // >= pos[r] + 1 for every row (host bound)
@@ -268,6 +272,7 @@ struct AttnProblem {
 constexpr int kPrefillQueryBlock = 128;
 size_t attention_ws_bytes(int64_t rows, int heads, int capacity, int act);
 tf_status launch_attn_prefill_tc(const AttnProblem& a, const void* q, cudaStream_t s);
+tf_status launch_rope_table(float theta, int positions, void* tab, cudaStream_t s);
 tf_status launch_attention(const AttnProblem& a, cudaStream_t s);
 
 }  // namespace tf

@@ -151,6 +151,7 @@ struct tf_session {
   int64_t* greedy = nullptr;  // [max_batch] greedy tokens before a host copy
   int4* qblocks = nullptr;    // prefill query blocks {row, rows, request, position}
   void* attn_ws = nullptr;
+  void* rope = nullptr;  // float2 [capacity][head_dim / 2] RoPE (cos, sin)
   size_t attn_ws_bytes = 0;
   void* moe_ws = nullptr;
   size_t moe_ws_bytes = 0;
@@ -439,6 +440,7 @@ int tf_session_create(tf_model* model, int32_t max_batch, int32_t capacity, int3
     s->greedy = k.take<int64_t>((size_t)max_batch * 8);
     s->qblocks = k.take<int4>((size_t)(R / kPrefillQueryBlock + max_batch + 1) * sizeof(int4));
     s->attn_ws = k.take<char>(s->attn_ws_bytes);
+    s->rope = k.take<float>((size_t)capacity * (c.head_dim / 2) * 8);
     s->moe_ws = k.take<char>(s->moe_ws_bytes);
     s->split_partials = k.take<float>(qmm_split_partial_bytes());
     s->split_counters = k.take<int>((size_t)kQmmSplitCounters * sizeof(int));
@@ -466,6 +468,18 @@ int tf_session_create(tf_model* model, int32_t max_batch, int32_t capacity, int3
     cudaFree(s->scratch);
     delete s;
     return set_error(TF_ERR_CUDA, "session scratch clear: %s", cudaGetErrorString(e));
+  }
+  if (c.head_dim == 128) {
+    const tf_status rs = launch_rope_table(c.rope_theta, capacity, s->rope, 0);
+    if (rs == TF_OK) e = cudaStreamSynchronize(0);
+    if (rs != TF_OK || e != cudaSuccess) {
+      cudaFree(s->kv);
+      cudaFree(s->scratch);
+      delete s;
+      return rs != TF_OK ? rs : set_error(TF_ERR_CUDA, "RoPE table: %s", cudaGetErrorString(e));
+    }
+  } else {
+    s->rope = nullptr;
   }
   for (int l = 0; l < c.layers; ++l) {
     s->k.push_back(s->kv + per_cache * (2 * l));
@@ -627,6 +641,7 @@ tf_status forward_rows(tf_session* s, int64_t rows, bool req_ident, int max_len,
     a.k_norm = L.k_norm;
     a.eps = c.rms_eps;
     a.theta = c.rope_theta;
+    a.rope = s->rope;
     a.pos = s->pos;
     a.req = req_ident ? nullptr : s->req;
     a.max_len = max_len;

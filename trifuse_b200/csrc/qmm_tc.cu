@@ -62,6 +62,7 @@
 #include <string.h>
 
 #include <mutex>
+#include <type_traits>
 
 #include "common.cuh"
 #include "internal.h"
@@ -363,6 +364,50 @@ __device__ __forceinline__ void epi_apply(const Params& p, const Seg& sg, int q,
 // of issue slots and bounded the whole tile).  Same values as epi_apply.
 // res: EPI_RESIDUAL only, the residual vectors of this lane's two (token,
 // 8-row) pieces, loaded ahead by the caller (epi_residual_vec).
+// Packed fp32 pairs (each lane rounded as the scalar operation).
+__device__ __forceinline__ uint64_t f2_pack(float a, float b) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ void f2_unpack(uint64_t v, float& a, float& b) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(v));
+}
+__device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+__device__ __forceinline__ float rcp_approx(float x) {
+  float y;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+constexpr float kLog2eF = 1.4426950408889634f;
+// Both values rounded to the activation dtype (one packed conversion).
+template <typename T>
+__device__ __forceinline__ void round2_act(float& a, float& b);
+template <>
+__device__ __forceinline__ void round2_act<__half>(float& a, float& b) {
+  const float2 f = __half22float2(__floats2half2_rn(a, b));
+  a = f.x, b = f.y;
+}
+template <>
+__device__ __forceinline__ void round2_act<__nv_bfloat16>(float& a, float& b) {
+  const float2 f = __bfloat1622float2(__floats2bfloat162_rn(a, b));
+  a = f.x, b = f.y;
+}
+
 template <typename T>
 __device__ __forceinline__ void epi_residual_vec(const Params& p, const Seg& sg, int wq, int lane, int c0, uint4* res) {
   const int f0 = sg.rb * kM + wq * 32;
@@ -380,26 +425,44 @@ __device__ __forceinline__ void epi_staged(const Params& p, const Seg& sg, int w
                                            uint8_t* stage, const uint4* res) {
   if (EPI == EPI_SWIGLU) {
     // 16 features (lane pairs) x 16 tokens; the even lane of a pair finishes
-    // tokens 0-7, the odd one 8-15 (as epi_apply).
+    // tokens 0-7, the odd one 8-15 (as epi_apply), two tokens at a time on
+    // packed fp32 pairs (the same operations as epi_apply: act-rounded gate
+    // and up, SiLU by the fast exponential and reciprocal, act rounding).
     const int base = sg.rb * (kM / 2) + wq * 16;  // the warp's first feature (a multiple of 8)
     const int f = base + (lane >> 1);
     const int col = (p.y_f16 ? perm_col(f) : f) - base;
     const int odd = lane & 1;
     bool wide = false;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const float mine = odd ? v[8 + i] : v[i];
-      const float theirs = __shfl_xor_sync(0xffffffffu, odd ? v[i] : v[8 + i], 1);
-      const float gg = round_act<T>(odd ? theirs : mine);
-      const float uu = round_act<T>(odd ? mine : theirs);
-      const float sl = round_act<T>(__fdividef(gg, 1.0f + __expf(-gg)));
-      const float hv = round_act<T>(sl * uu);
-      const int t = i + 8 * odd;
+    for (int k = 0; k < 4; ++k) {
+      const int i0 = 2 * k;
+      const float m0 = odd ? v[8 + i0] : v[i0], m1 = odd ? v[9 + i0] : v[i0 + 1];
+      const float x0 = odd ? v[i0] : v[8 + i0], x1 = odd ? v[i0 + 1] : v[9 + i0];
+      const float t0 = __shfl_xor_sync(0xffffffffu, x0, 1), t1 = __shfl_xor_sync(0xffffffffu, x1, 1);
+      float g0 = odd ? t0 : m0, g1 = odd ? t1 : m1;
+      float u0 = odd ? m0 : t0, u1 = odd ? m1 : t1;
+      round2_act<T>(g0, g1);
+      round2_act<T>(u0, u1);
+      const uint64_t gg = f2_pack(g0, g1);
+      float e0, e1;
+      f2_unpack(f2_mul(gg, f2_pack(-kLog2eF, -kLog2eF)), e0, e1);
+      float d0, d1;
+      f2_unpack(f2_add(f2_pack(ex2_approx(e0), ex2_approx(e1)), f2_pack(1.f, 1.f)), d0, d1);
+      float s0, s1;
+      f2_unpack(f2_mul(gg, f2_pack(rcp_approx(d0), rcp_approx(d1))), s0, s1);
+      round2_act<T>(s0, s1);
+      float h0, h1;
+      f2_unpack(f2_mul(f2_pack(s0, s1), f2_pack(u0, u1)), h0, h1);
+      round2_act<T>(h0, h1);
+      const int t = i0 + 8 * odd;
       if (p.y_f16) {
-        wide |= c0 + t < sg.cnt && f < p.out && fabsf(hv) > 65504.f;
-        reinterpret_cast<__half*>(stage)[t * 16 + col] = __float2half_rn(hv);
+        if (!std::is_same<T, __half>::value)  // bf16 values beyond the f16 range
+          wide |= f < p.out && ((c0 + t < sg.cnt && fabsf(h0) > 65504.f) || (c0 + t + 1 < sg.cnt && fabsf(h1) > 65504.f));
+        reinterpret_cast<__half*>(stage)[t * 16 + col] = __float2half_rn(h0);
+        reinterpret_cast<__half*>(stage)[(t + 1) * 16 + col] = __float2half_rn(h1);
       } else {
-        reinterpret_cast<T*>(stage)[t * 16 + col] = from_f<T>(hv);
+        reinterpret_cast<T*>(stage)[t * 16 + col] = from_f<T>(h0);
+        reinterpret_cast<T*>(stage)[(t + 1) * 16 + col] = from_f<T>(h1);
       }
     }
     __syncwarp();
