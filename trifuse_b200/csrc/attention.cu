@@ -93,34 +93,95 @@ __global__ void __launch_bounds__(kAttnThreads)
   const float rq = rms_scale(block_row_sumsq<T>(qrow, W, tot_s, &bcast), W, eps);
   const float rk = rms_scale(block_row_sumsq<T>(krow, W, tot_s, &bcast), W, eps);
   const float fp = (float)p;
-  for (int i = t; i < W / 2; i += kAttnThreads) {
-    const int h = i / (kHeadDim / 2), d = i % (kHeadDim / 2);
-    const int i1 = h * kHeadDim + d, i2 = i1 + kHeadDim / 2;
-    float sn, cs;
+  // Thread v takes 8 consecutive rotation pairs (d0 .. d0 + 7 of head h): one
+  // 16-byte load per operand half and one 16-byte store per output half.
+  const int64_t kv_row = (q_req * heads) * cap + p;  // cache row of head 0 at this position
+  for (int v = t; v < W / 16; v += kAttnThreads) {
+    const int h = v / (kHeadDim / 16), d0 = (v % (kHeadDim / 16)) * 8;
+    const int i1 = h * kHeadDim + d0, i2 = i1 + kHeadDim / 2;
+    float cs[8], sn[8];
     if (rope) {
-      const float2 a = rope[(int64_t)p * (kHeadDim / 2) + d];
-      cs = a.x, sn = a.y;
+      const float4* rp = reinterpret_cast<const float4*>(rope + (int64_t)p * (kHeadDim / 2) + d0);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const float4 a = rp[k];
+        cs[2 * k] = a.x, sn[2 * k] = a.y, cs[2 * k + 1] = a.z, sn[2 * k + 1] = a.w;
+      }
     } else {
-      sincosf(__fmul_rn(fp, inv_s[d]), &sn, &cs);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) sincosf(__fmul_rn(fp, inv_s[d0 + k]), &sn[k], &cs[k]);
     }
-    {
-      const float x1 = round_act<T>(__fmul_rn(__fmul_rn(to_f(qrow[i1]), rq), __half2float(qn[i1])));
-      const float x2 = round_act<T>(__fmul_rn(__fmul_rn(to_f(qrow[i2]), rq), __half2float(qn[i2])));
-      q_out[r * W + i1] = from_f<T>(x1 * cs - x2 * sn);
-      q_out[r * W + i2] = from_f<T>(x1 * sn + x2 * cs);
+    float a1[8], a2[8], w1[8], w2[8], o1[8], o2[8];
+    unpack8<__half>(ld_v4(qn + i1), w1);
+    unpack8<__half>(ld_v4(qn + i2), w2);
+    unpack8<T>(ld_v4(qrow + i1), a1);
+    unpack8<T>(ld_v4(qrow + i2), a2);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const float x1 = round_act<T>(__fmul_rn(__fmul_rn(a1[k], rq), w1[k]));
+      const float x2 = round_act<T>(__fmul_rn(__fmul_rn(a2[k], rq), w2[k]));
+      o1[k] = x1 * cs[k] - x2 * sn[k];
+      o2[k] = x1 * sn[k] + x2 * cs[k];
     }
-    {
-      const float x1 = round_act<T>(__fmul_rn(__fmul_rn(to_f(krow[i1]), rk), __half2float(kn[i1])));
-      const float x2 = round_act<T>(__fmul_rn(__fmul_rn(to_f(krow[i2]), rk), __half2float(kn[i2])));
-      const int64_t slot = ((q_req * heads + h) * cap + p) * kHeadDim;
-      k_cache[slot + d] = __float2half_rn(round_act<T>(x1 * cs - x2 * sn));
-      k_cache[slot + d + kHeadDim / 2] = __float2half_rn(round_act<T>(x1 * sn + x2 * cs));
+    *reinterpret_cast<uint4*>(q_out + r * W + i1) = pack8<T>(o1);
+    *reinterpret_cast<uint4*>(q_out + r * W + i2) = pack8<T>(o2);
+    unpack8<__half>(ld_v4(kn + i1), w1);
+    unpack8<__half>(ld_v4(kn + i2), w2);
+    unpack8<T>(ld_v4(krow + i1), a1);
+    unpack8<T>(ld_v4(krow + i2), a2);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const float x1 = round_act<T>(__fmul_rn(__fmul_rn(a1[k], rk), w1[k]));
+      const float x2 = round_act<T>(__fmul_rn(__fmul_rn(a2[k], rk), w2[k]));
+      o1[k] = round_act<T>(x1 * cs[k] - x2 * sn[k]);
+      o2[k] = round_act<T>(x1 * sn[k] + x2 * cs[k]);
     }
+    __half* kdst = k_cache + (kv_row + (int64_t)h * cap) * kHeadDim + d0;
+    *reinterpret_cast<uint4*>(kdst) = pack8<__half>(o1);
+    *reinterpret_cast<uint4*>(kdst + kHeadDim / 2) = pack8<__half>(o2);
   }
-  for (int i = t; i < W; i += kAttnThreads) {
-    const int h = i / kHeadDim, d = i % kHeadDim;
-    v_cache[((q_req * heads + h) * cap + p) * kHeadDim + d] = __float2half_rn(to_f(vrow[i]));
+  for (int c = t; c < W / 8; c += kAttnThreads) {
+    const int h = c / (kHeadDim / 8), d0 = (c % (kHeadDim / 8)) * 8;
+    float f[8];
+    unpack8<T>(ld_v4(vrow + 8 * c), f);
+    *reinterpret_cast<uint4*>(v_cache + (kv_row + (int64_t)h * cap) * kHeadDim + d0) = pack8<__half>(f);
   }
+}
+
+// The split blocks of one (query, head) count their arrivals; the last one
+// to arrive merges every part (the merge kernel's arithmetic, so the result
+// is the same) and leaves the counter at zero, so no separate merge launch
+// waits behind the slowest split.
+template <typename T>
+__device__ __forceinline__ void attn_merge_last(const int32_t* __restrict__ pos, int64_t r, int64_t z, int h,
+                                                int heads, int nsplit, const float* pm, const float* pl,
+                                                const float* po, int* arrivals, T* __restrict__ out, int* last_s) {
+  __syncthreads();  // this block's part is written
+  if (threadIdx.x == 0) {
+    __threadfence();
+    int* ctr = &arrivals[z * heads + h];
+    const int seen = atomicAdd(ctr, 1);
+    const int last = seen == (int)gridDim.x - 1;
+    if (last) *ctr = 0;  // left at zero for the next launch
+    *last_s = last;
+  }
+  __syncthreads();
+  if (!*last_s) return;
+  __threadfence();
+  const int d = threadIdx.x;
+  if (d >= kHeadDim) return;
+  const int L = pos[r] + 1;
+  const int ns = (L + kSplit - 1) / kSplit;
+  const int64_t base = (z * heads + h) * nsplit;
+  float M = -INFINITY;
+  for (int s = 0; s < ns; ++s) M = fmaxf(M, __ldcg(&pm[base + s]));
+  float acc = 0.f, l = 0.f;
+  for (int s = 0; s < ns; ++s) {
+    const float w = expf(__ldcg(&pm[base + s]) - M);
+    acc = fmaf(w, __ldcg(&po[(base + s) * kHeadDim + d]), acc);
+    l = fmaf(w, __ldcg(&pl[base + s]), l);
+  }
+  out[z * heads * kHeadDim + h * kHeadDim + d] = from_f<T>(acc / l);
 }
 
 template <typename T>
@@ -129,8 +190,9 @@ __global__ void __launch_bounds__(kAttnThreads)
                       const int32_t* __restrict__ req, const int32_t* __restrict__ qrows,
                       const __half* __restrict__ k_cache, const __half* __restrict__ v_cache, int cap,
                       float scale, int nsplit, float* __restrict__ pm, float* __restrict__ pl,
-                      float* __restrict__ po) {
+                      float* __restrict__ po, int* __restrict__ arrivals, T* __restrict__ out) {
   __shared__ float sc[kSplit];
+  __shared__ int last_s;
   __shared__ float red[kAttnThreads / 32];
   __shared__ float opart[kKeyGroups][kHeadDim];
   const int s = blockIdx.x, h = blockIdx.y;
@@ -145,6 +207,7 @@ __global__ void __launch_bounds__(kAttnThreads)
       pm[part] = -INFINITY;
       pl[part] = 0.f;
     }
+    attn_merge_last<T>(pos, r, z, h, heads, nsplit, pm, pl, po, arrivals, out, &last_s);
     return;
   }
   const int k1 = min(L, k0 + kSplit);
@@ -243,28 +306,7 @@ __global__ void __launch_bounds__(kAttnThreads)
     pm[part] = m;
     pl[part] = l;
   }
-}
-
-template <typename T>
-__global__ void __launch_bounds__(kHeadDim)
-    attn_merge_kernel(const int32_t* __restrict__ pos, const int32_t* __restrict__ qrows, int heads, int nsplit,
-                      const float* __restrict__ pm, const float* __restrict__ pl,
-                      const float* __restrict__ po, T* __restrict__ out) {
-  const int h = blockIdx.x, d = threadIdx.x;
-  const int64_t z = blockIdx.y;
-  const int64_t r = qrows ? qrows[z] : z;
-  const int L = pos[r] + 1;
-  const int ns = (L + kSplit - 1) / kSplit;
-  const int64_t base = (z * heads + h) * nsplit;
-  float M = -INFINITY;
-  for (int s = 0; s < ns; ++s) M = fmaxf(M, pm[base + s]);
-  float acc = 0.f, l = 0.f;
-  for (int s = 0; s < ns; ++s) {
-    const float w = expf(pm[base + s] - M);
-    acc = fmaf(w, po[(base + s) * kHeadDim + d], acc);
-    l = fmaf(w, pl[base + s], l);
-  }
-  out[z * heads * kHeadDim + h * kHeadDim + d] = from_f<T>(acc / l);
+  attn_merge_last<T>(pos, r, z, h, heads, nsplit, pm, pl, po, arrivals, out, &last_s);
 }
 
 // ---------------------------------------------------------------------------
@@ -279,6 +321,7 @@ size_t attention_ws_bytes(int64_t rows, int heads, int capacity, int act) {
   const int64_t nsplit = (capacity + kSplit - 1) / kSplit;
   const int64_t parts = rows * heads * nsplit;
   Carve c(nullptr, 0);
+  c.take<int>((size_t)rows * heads * 4);  // split arrivals first (zero between launches)
   c.take<char>((size_t)rows * heads * kHeadDim * act_bytes(act));  // roped q
   c.take<float>(parts * 4);
   c.take<float>(parts * 4);
@@ -292,10 +335,15 @@ static tf_status attention_impl(const AttnProblem& a, cudaStream_t s) {
   const int grid_splits = (a.max_len + kSplit - 1) / kSplit;
   const int64_t parts = a.rows * a.heads * nsplit;
   Carve c(a.ws, a.ws_bytes);
+  // The arrival counters sit at the start, sized for the rows the workspace
+  // was made for, so every call finds the same zeroed counters.
+  const int64_t ws_rows = a.ws_rows > a.rows ? a.ws_rows : a.rows;
+  int* arrivals = c.take<int>((size_t)ws_rows * a.heads * 4);
   T* qr = c.take<T>((size_t)a.rows * a.heads * kHeadDim * sizeof(T));
   float* pm = c.take<float>(parts * 4);
   float* pl = c.take<float>(parts * 4);
   float* po = c.take<float>(parts * kHeadDim * 4);
+  if (!a.arrivals_zero) TF_CUDA(cudaMemsetAsync(arrivals, 0, (size_t)a.rows * a.heads * 4, s));
   attn_append_kernel<T><<<(unsigned)a.rows, kAttnThreads, 0, s>>>(
       (const T*)a.qkv, a.heads, (const __half*)a.q_norm, (const __half*)a.k_norm, a.eps, a.theta,
       a.pos, a.req, (__half*)a.k_cache, (__half*)a.v_cache, a.capacity, qr, (const float2*)a.rope);
@@ -312,11 +360,8 @@ static tf_status attention_impl(const AttnProblem& a, cudaStream_t s) {
   attn_split_kernel<T><<<grid, kAttnThreads, 0, s>>>(qr, a.heads, a.pos, a.req, a.qrows,
                                                      (const __half*)a.k_cache,
                                                      (const __half*)a.v_cache, a.capacity, a.scale,
-                                                     nsplit, pm, pl, po);
-  TF_TRY(check_launch("attn_split"));
-  dim3 mgrid(a.heads, (unsigned)nq);
-  attn_merge_kernel<T><<<mgrid, kHeadDim, 0, s>>>(a.pos, a.qrows, a.heads, nsplit, pm, pl, po, (T*)a.out);
-  return check_launch("attn_merge");
+                                                     nsplit, pm, pl, po, arrivals, (T*)a.out);
+  return check_launch("attn_split");
 }
 
 tf_status launch_attention(const AttnProblem& a, cudaStream_t s) {
@@ -326,7 +371,7 @@ tf_status launch_attention(const AttnProblem& a, cudaStream_t s) {
   const int W = a.heads * kHeadDim;
   if (W % 256 != 0 || W > 256 * 64)
     return set_error(TF_ERR_UNSUPPORTED, "attention: width %d", W);
-  if (a.ws_bytes < attention_ws_bytes(a.rows, a.heads, a.capacity, a.act))
+  if (a.ws_bytes < attention_ws_bytes(a.ws_rows > a.rows ? a.ws_rows : a.rows, a.heads, a.capacity, a.act))
     return set_error(TF_ERR_INVALID_ARGUMENT, "attention workspace too small");
   if (a.max_len < 1 || a.max_len > a.capacity)
     return set_error(TF_ERR_CAPACITY, "attention: length %d outside [1, %d]", a.max_len, a.capacity);

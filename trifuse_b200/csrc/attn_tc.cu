@@ -157,8 +157,8 @@ __device__ __forceinline__ void tmem_ld64(uint32_t taddr, float* v) {
 // x = n + f, n = floor(x) (an add with round-down against 1.5 * 2^23 leaves n
 // in the low mantissa bits), 2^f on [0, 1) by a cubic fitted here by
 // weighted least squares for relative error (max 8.6e-5, below the f16
-// rounding of P), and 2^n added to the exponent field.  Takes half of the
-// exponentials off the special-function unit.
+// rounding of P), and 2^n added to the exponent field.  Takes a quarter of
+// the exponentials off the special-function unit.
 __device__ __forceinline__ float poly_exp2(float x) {
   x = fmaxf(x, -127.f);
   const float t = __fadd_rd(x, 12582912.f);
@@ -340,17 +340,25 @@ __global__ void __launch_bounds__(kFaThreads, 1) attn_prefill_tc_kernel(const __
       tmem_ld64(lane_base + kColS + st * 128 + 64, sc + 64);
       const int lim = pr - j * kFaKeys;  // keys c > lim of this tile are masked
       // Eight independent partial maxima and sums keep the chains short.
+      // The max is taken on the raw scores (the scale is positive) and the
+      // scale is folded into the exponent's FMA; only tiles that reach past
+      // the block's first row need the causal mask.
       float mp[8];
 #pragma unroll
       for (int i = 0; i < 8; ++i) mp[i] = -INFINITY;
+      if ((j + 1) * kFaKeys > pos0 + 1) {
 #pragma unroll
-      for (int c = 0; c < 128; ++c) {
-        const float t = c > lim ? -INFINITY : sc[c] * p.scale_log2;
-        sc[c] = t;
-        mp[c & 7] = fmaxf(mp[c & 7], t);
+        for (int c = 0; c < 128; ++c) {
+          const float t = c > lim ? -INFINITY : sc[c];
+          sc[c] = t;
+          mp[c & 7] = fmaxf(mp[c & 7], t);
+        }
+      } else {
+#pragma unroll
+        for (int c = 0; c < 128; ++c) mp[c & 7] = fmaxf(mp[c & 7], sc[c]);
       }
       const float mx = fmaxf(fmaxf(fmaxf(mp[0], mp[1]), fmaxf(mp[2], mp[3])),
-                             fmaxf(fmaxf(mp[4], mp[5]), fmaxf(mp[6], mp[7])));
+                             fmaxf(fmaxf(mp[4], mp[5]), fmaxf(mp[6], mp[7]))) * p.scale_log2;
       float factor = 1.f;  // O and l scale when the max moves
       if (j == 0) {
         m_used = mx;  // finite: key 0 is attended by every row
@@ -359,13 +367,17 @@ __global__ void __launch_bounds__(kFaThreads, 1) attn_prefill_tc_kernel(const __
         m_used = mx;
         l *= factor;
       }
+      // One exponential in four on the FMA pipe (the special-function unit
+      // takes eight cycles per warp instruction; the cubic nine issue slots).
+      const float nm = -m_used, sl2 = p.scale_log2;
       uint32_t pk[64];
       float sp[8];
 #pragma unroll
       for (int i = 0; i < 8; ++i) sp[i] = 0.f;
 #pragma unroll
       for (int c = 0; c < 64; ++c) {
-        const float a = fast_exp2(sc[2 * c] - m_used), b = poly_exp2(sc[2 * c + 1] - m_used);
+        const float x0 = fmaf(sc[2 * c], sl2, nm), x1 = fmaf(sc[2 * c + 1], sl2, nm);
+        const float a = fast_exp2(x0), b = (c & 1) ? poly_exp2(x1) : fast_exp2(x1);
         sp[c & 7] += a + b;
         pk[c] = pack_half2(a, b);
       }

@@ -244,6 +244,10 @@ struct AttnProblem {
   // float2 from launch_rope_table with the same theta (bit-identical to the
   // kernel's own sincosf).
   const void* rope = nullptr;
+  // The workspace's split-arrival counters are zero (a session's workspace,
+  // cleared once and left zero by every launch); else they are cleared.
+  bool arrivals_zero = false;
+  int64_t ws_rows = 0;  // rows the workspace was sized for (attention_ws_bytes); 0: rows
   const int32_t* pos = nullptr;  // device [rows]
   const int32_t* req = nullptr;  // device [rows] or NULL
   int max_len = 0;               // >= pos[r] + 1 for every row (host bound)

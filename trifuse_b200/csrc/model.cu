@@ -642,6 +642,8 @@ tf_status forward_rows(tf_session* s, int64_t rows, bool req_ident, int max_len,
     a.eps = c.rms_eps;
     a.theta = c.rope_theta;
     a.rope = s->rope;
+    a.arrivals_zero = true;
+    a.ws_rows = s->max_rows;
     a.pos = s->pos;
     a.req = req_ident ? nullptr : s->req;
     a.max_len = max_len;
