@@ -356,6 +356,18 @@ static MoePlan plan_moe(const tf_moe_args* a, void* ws, size_t ws_bytes, bool wi
   const int ab = act_bytes(a->act);
   Carve c(ws, ws_bytes);
   MoePlan p;
+  // The arrival counters (split tiles, route sort) come first, at an offset
+  // that does not depend on the token count: a workspace reused by calls of
+  // different sizes (a session's prefill, then its decode steps) finds them
+  // where the last call left them at zero, never on another call's data.
+  p.partials = nullptr;
+  p.partial_bytes = 0;
+  p.counters = nullptr;
+  if (with_split) {
+    p.counters = c.take<int>((size_t)(kQmmSplitCounters + 1) * sizeof(int));  // + the router's arrivals
+    p.partial_bytes = qmm_split_partial_bytes();
+    p.partials = c.take<float>(p.partial_bytes);
+  }
   p.logits = a->logits ? a->logits : c.take<char>((size_t)T * a->experts * ab);
   p.idx = a->indices ? a->indices : c.take<int32_t>((size_t)N * 4);
   p.gates = a->gates ? a->gates : c.take<char>((size_t)N * ab);
@@ -369,14 +381,6 @@ static MoePlan plan_moe(const tf_moe_args* a, void* ws, size_t ws_bytes, bool wi
   p.h = c.take<char>((size_t)N * a->intermediate * ab);
   p.y = c.take<char>((size_t)N * a->hidden * ab);
   p.op16 = c.take<char>((size_t)N * (a->hidden > a->intermediate ? a->hidden : a->intermediate) * 2);
-  p.partials = nullptr;
-  p.partial_bytes = 0;
-  p.counters = nullptr;
-  if (with_split) {
-    p.partial_bytes = qmm_split_partial_bytes();
-    p.partials = c.take<float>(p.partial_bytes);
-    p.counters = c.take<int>((size_t)kQmmSplitCounters * sizeof(int));
-  }
   p.used = c.used;
   return p;
 }
@@ -413,15 +417,25 @@ static tf_status run_moe(const tf_moe_args* a, const MoePlan& p, cudaStream_t s,
                          const MoeNextNorm* next = nullptr) {
   const int64_t N = a->tokens * a->top_k;
   if (p.counters && !counters_zero)
-    TF_CUDA(cudaMemsetAsync(p.counters, 0, (size_t)kQmmSplitCounters * sizeof(int), s));
+    TF_CUDA(cudaMemsetAsync(p.counters, 0, (size_t)(kQmmSplitCounters + 1) * sizeof(int), s));
+  RouteSortOut so;
+  so.order = p.order;
+  so.inverse = p.inverse;
+  so.offsets = p.offsets;
+  so.active = p.active;
+  so.active_count = p.active_count;
+  so.arrivals = p.counters ? p.counters + kQmmSplitCounters : nullptr;
+  bool sorted = false;
   trace(PH_ROUTER, true, s);
   TF_TRY(launch_router(a->x, a->tokens, a->hidden, a->router, a->experts, a->top_k, a->act,
-                       p.logits, p.idx, p.gates, s));
+                       p.logits, p.idx, p.gates, s, &so, &sorted));
   trace(PH_ROUTER, false, s);
-  trace(PH_SORT, true, s);
-  TF_TRY(launch_route_sort(p.idx, N, a->experts, p.order, p.inverse, p.offsets, p.active,
-                           p.active_count, p.sort_ws, p.sort_ws_bytes, s));
-  trace(PH_SORT, false, s);
+  if (!sorted) {
+    trace(PH_SORT, true, s);
+    TF_TRY(launch_route_sort(p.idx, N, a->experts, p.order, p.inverse, p.offsets, p.active,
+                             p.active_count, p.sort_ws, p.sort_ws_bytes, s));
+    trace(PH_SORT, false, s);
+  }
   QmmProblem up;
   up.mode = QMM_GROUPED;
   up.epilogue = EPI_SWIGLU;

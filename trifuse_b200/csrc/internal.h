@@ -100,9 +100,22 @@ tf_status launch_embedding(const int64_t* ids, int64_t n, const tf_affine_weight
                            void* y, cudaStream_t s);
 
 // ---------------------------------------------------------------- router
+// Route-sort outputs for the router to produce itself (decode-sized
+// batches): the last token's cluster to finish sorts every route in one CTA.
+// arrivals: an int that is zero before the launch (left zero after it).
+struct RouteSortOut {
+  int32_t* order = nullptr;
+  int32_t* inverse = nullptr;
+  int32_t* offsets = nullptr;
+  int32_t* active = nullptr;
+  int32_t* active_count = nullptr;
+  int* arrivals = nullptr;
+};
+// With `sort` the router also sorts the routes when it can (*sorted = true);
+// otherwise the caller runs launch_route_sort.
 tf_status launch_router(const void* x, int64_t tokens, int hidden, const tf_router_weight& r,
                         int experts, int k, int act, void* logits, int32_t* idx, void* gates,
-                        cudaStream_t s);
+                        cudaStream_t s, const RouteSortOut* sort = nullptr, bool* sorted = nullptr);
 tf_status launch_route(const void* logits, int64_t tokens, int experts, int k, int act,
                        void* probs, int32_t* idx, void* gates, cudaStream_t s);
 tf_status launch_topk(const void* probs, int64_t rows, int experts, int k, int act,

@@ -545,11 +545,13 @@ int tf_session_reset(tf_session* s) {
   DeviceGuard g(s->m->device);
   if (s->invalid) {
     // After a dispatched failure: wait for the device, clear its error flags
-    // and the split counters a stopped launch may have left behind.
+    // and the arrival counters a stopped launch may have left behind (split
+    // tiles and route sort in the MoE workspace, split attention).
     TF_CUDA(cudaDeviceSynchronize());
     read_tc_error(true);
     read_embed_error(true);
     TF_CUDA(cudaMemset(s->moe_ws, 0, s->moe_ws_bytes));
+    TF_CUDA(cudaMemset(s->attn_ws, 0, s->attn_ws_bytes));
     TF_CUDA(cudaMemset(s->split_counters, 0, (size_t)kQmmSplitCounters * sizeof(int)));
     s->invalid = false;
   }

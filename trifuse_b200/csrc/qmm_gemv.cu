@@ -92,7 +92,7 @@ __global__ void __launch_bounds__(kGemvWarps * 32) qmm_gemv_kernel(GemvArgs a) {
   int64_t nseg;
   if (MODE == QMM_DENSE) nseg = 1;
   else if (MODE == QMM_PER_ROUTE) nseg = a.n;
-  else nseg = *a.active_count;
+  else nseg = min(max(*a.active_count, 0), a.experts);
   const int64_t items = nseg * nrb;
   constexpr int NW = EPI == EPI_SWIGLU ? 2 : 1;
   // Pre-scale factors 16^-j for code position j of a word (j = i % 8).
@@ -108,7 +108,10 @@ __global__ void __launch_bounds__(kGemvWarps * 32) qmm_gemv_kernel(GemvArgs a) {
     } else if (MODE == QMM_PER_ROUTE) {
       e = a.indices[seg]; s0 = seg; s1 = seg + 1;
     } else {
-      e = a.active[seg]; s0 = a.offsets[e]; s1 = a.offsets[e + 1];
+      // Clamped to [0, n] (see the tensor-core kernel's setup).
+      e = min(max(a.active[seg], 0), a.experts - 1);
+      s0 = min(max((int64_t)a.offsets[e], (int64_t)0), a.n);
+      s1 = min(max((int64_t)a.offsets[e + 1], s0), a.n);
     }
     const int row0 = rb * kGemvRows + warp * kRowsPerWarp;
     for (int64_t tb = s0; tb < s1; tb += TB) {

@@ -630,7 +630,10 @@ __global__ void __launch_bounds__(Roles<G * H, BPS>::kThreads, BPS)
         const int i = c0 + lane;
         int nb = 0;
         if (i < na) {
-          const int lo = lo_r[r], hi = hi_r[r];
+          // Offsets outside [0, n] (a caller's corrupted sort output) are
+          // clamped: wrong rows at worst, never an address past the operands.
+          const int nrows = (int)p.n;
+          const int lo = min(max(lo_r[r], 0), nrows), hi = min(max(hi_r[r], lo), nrows);
           nb = (hi - lo + NT - 1) / NT;
           ex_id[i] = i;
           ex_lo[i] = lo;

@@ -322,11 +322,76 @@ __global__ void __launch_bounds__(kRouterWideWarps * 32, 1)
 // shared memory); after the cluster barrier CTA 0's first warp ranks them.
 constexpr int kRouterCluster = 8;
 
+// The one-tile route sort (sort_one_tile_kernel's algorithm and output: a
+// stable counting sort by expert) run by one 256-thread CTA over n <= 1024
+// routes: route i = pass * 256 + thread is the 1024-thread kernel's thread i,
+// so the per-warp counts, offsets and placement are the same.
+constexpr int kFusedSortRoutes = 1024;
+__device__ void sort_routes_cta(const int32_t* ids, int n, int E, const RouteSortOut& so) {
+  __shared__ int32_t warp_cnt[kFusedSortRoutes / 32][64];
+  __shared__ int32_t total[64];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  constexpr int kPasses = kFusedSortRoutes / (kRouterBlockWarps * 32);
+  for (int i = tid; i < (kFusedSortRoutes / 32) * E; i += blockDim.x) warp_cnt[i / E][i % E] = 0;
+  __syncthreads();
+  int ev[kPasses], rk[kPasses];
+#pragma unroll
+  for (int ps = 0; ps < kPasses; ++ps) {
+    const int i = ps * kRouterBlockWarps * 32 + tid;
+    const bool valid = i < n;
+    const int e = valid ? __ldcg(&ids[i]) : -1;
+    const unsigned peers = __match_any_sync(0xffffffffu, e);
+    const int rank = __popc(peers & ((1u << lane) - 1u));
+    if (valid && rank == 0) warp_cnt[ps * kRouterBlockWarps + warp][e] = __popc(peers);
+    ev[ps] = e;
+    rk[ps] = rank;
+  }
+  __syncthreads();
+  for (int x = tid; x < E; x += blockDim.x) {
+    int32_t sum = 0;
+    for (int w = 0; w < kFusedSortRoutes / 32; ++w) sum += warp_cnt[w][x];
+    total[x] = sum;
+  }
+  __syncthreads();
+  if (tid == 0) {
+    int32_t run = 0, na = 0;
+    for (int x = 0; x < E; ++x) {
+      so.offsets[x] = run;
+      const int32_t c = total[x];
+      total[x] = run;
+      run += c;
+      if (c > 0) so.active[na++] = x;
+    }
+    so.offsets[E] = run;
+    *so.active_count = na;
+  }
+  __syncthreads();
+  for (int x = tid; x < E; x += blockDim.x) {
+    int32_t run = total[x];
+    for (int w = 0; w < kFusedSortRoutes / 32; ++w) {
+      const int32_t c = warp_cnt[w][x];
+      warp_cnt[w][x] = run;
+      run += c;
+    }
+  }
+  __syncthreads();
+#pragma unroll
+  for (int ps = 0; ps < kPasses; ++ps) {
+    const int i = ps * kRouterBlockWarps * 32 + tid;
+    if (i < n) {
+      const int32_t pos = warp_cnt[ps * kRouterBlockWarps + warp][ev[ps]] + rk[ps];
+      so.order[pos] = i;
+      so.inverse[i] = pos;
+    }
+  }
+}
+
 template <typename T, bool DENSE, int J>
 __global__ void __cluster_dims__(kRouterCluster, 1, 1) __launch_bounds__(kRouterBlockWarps * 32)
     router_cluster_kernel(const T* __restrict__ x, int64_t tokens, const T* __restrict__ wd,
                           const uint32_t* __restrict__ wq, const __half* __restrict__ ws,
-                          const __half* __restrict__ wb, int E, int K, T* logits, int32_t* idx, T* gates) {
+                          const __half* __restrict__ wb, int E, int K, T* logits, int32_t* idx, T* gates,
+                          const RouteSortOut so) {
   constexpr int H = J * 256;
   __shared__ float ls[64];
   namespace cg = cooperative_groups;
@@ -369,6 +434,23 @@ __global__ void __cluster_dims__(kRouterCluster, 1, 1) __launch_bounds__(kRouter
     const float la0 = lane < E ? ls[lane] : 0.f;
     const float la1 = lane + 32 < E ? ls[lane + 32] : 0.f;
     route_token<T>(lane, la0, la1, E, K, t, (T*)nullptr, idx, gates);
+  }
+  if (so.arrivals && part == 0) {
+    // The last token's CTA to finish sorts every route (ids written by the
+    // other clusters are read from L2 after the fences).
+    __shared__ int last_s;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      __threadfence();
+      const int last = atomicAdd(so.arrivals, 1) == (int)tokens - 1;
+      if (last) *so.arrivals = 0;  // left at zero for the next launch
+      last_s = last;
+    }
+    __syncthreads();
+    if (last_s) {
+      __threadfence();
+      sort_routes_cta(idx, (int)tokens * K, E, so);
+    }
   }
 }
 
@@ -474,7 +556,8 @@ static tf_status router_dispatch_wide(const void* x, int64_t tokens, int hidden,
 
 template <typename T, bool DENSE>
 static tf_status router_dispatch_cluster(const void* x, int64_t tokens, int hidden, const tf_router_weight& r,
-                                         int E, int K, void* logits, int32_t* idx, void* gates, cudaStream_t s) {
+                                         int E, int K, void* logits, int32_t* idx, void* gates, cudaStream_t s,
+                                         const RouteSortOut& so) {
   const unsigned blocks = (unsigned)(tokens * kRouterCluster);
   const T* wd = (const T*)r.dense;
   const uint32_t* wq = r.affine.q;
@@ -483,7 +566,7 @@ static tf_status router_dispatch_cluster(const void* x, int64_t tokens, int hidd
 #define TF_ROUTER_CCASE(JJ)                                                                  \
   case JJ:                                                                                   \
     router_cluster_kernel<T, DENSE, JJ><<<blocks, kRouterBlockWarps * 32, 0, s>>>(            \
-        (const T*)x, tokens, wd, wq, wsc, wbi, E, K, (T*)logits, idx, (T*)gates);            \
+        (const T*)x, tokens, wd, wq, wsc, wbi, E, K, (T*)logits, idx, (T*)gates, so);        \
     break;
   switch (hidden / 256) {
     TF_ROUTER_CCASE(1)
@@ -502,9 +585,17 @@ static tf_status router_dispatch_cluster(const void* x, int64_t tokens, int hidd
 template <typename T, bool DENSE>
 static tf_status router_dispatch(const void* x, int64_t tokens, int hidden,
                                  const tf_router_weight& r, int E, int K, void* logits,
-                                 int32_t* idx, void* gates, cudaStream_t s) {
-  if (tokens <= 256)
-    return router_dispatch_cluster<T, DENSE>(x, tokens, hidden, r, E, K, logits, idx, gates, s);
+                                 int32_t* idx, void* gates, cudaStream_t s, const RouteSortOut* sort,
+                                 bool* sorted) {
+  if (tokens <= 256) {
+    // The route sort rides along when one CTA can take every route.
+    RouteSortOut so;
+    if (sort && sort->arrivals && idx && tokens * K <= kFusedSortRoutes && E <= 64) {
+      so = *sort;
+      if (sorted) *sorted = true;
+    }
+    return router_dispatch_cluster<T, DENSE>(x, tokens, hidden, r, E, K, logits, idx, gates, s, so);
+  }
   if (tokens <= 2048)
     return router_dispatch_tpc<T, DENSE, 1>(x, tokens, hidden, r, E, K, logits, idx, gates, s);
   return router_dispatch_wide<T, DENSE>(x, tokens, hidden, r, E, K, logits, idx, gates, s);
@@ -512,15 +603,17 @@ static tf_status router_dispatch(const void* x, int64_t tokens, int hidden,
 
 tf_status launch_router(const void* x, int64_t tokens, int hidden, const tf_router_weight& r,
                         int E, int K, int act, void* logits, int32_t* idx, void* gates,
-                        cudaStream_t s) {
+                        cudaStream_t s, const RouteSortOut* sort, bool* sorted) {
+  if (sorted) *sorted = false;
   if (tokens == 0) return TF_OK;
   const bool dense = r.dense != nullptr;
   if (act == TF_DTYPE_F16)
-    return dense ? router_dispatch<__half, true>(x, tokens, hidden, r, E, K, logits, idx, gates, s)
-                 : router_dispatch<__half, false>(x, tokens, hidden, r, E, K, logits, idx, gates, s);
-  return dense
-             ? router_dispatch<__nv_bfloat16, true>(x, tokens, hidden, r, E, K, logits, idx, gates, s)
-             : router_dispatch<__nv_bfloat16, false>(x, tokens, hidden, r, E, K, logits, idx, gates, s);
+    return dense ? router_dispatch<__half, true>(x, tokens, hidden, r, E, K, logits, idx, gates, s, sort, sorted)
+                 : router_dispatch<__half, false>(x, tokens, hidden, r, E, K, logits, idx, gates, s, sort, sorted);
+  return dense ? router_dispatch<__nv_bfloat16, true>(x, tokens, hidden, r, E, K, logits, idx, gates, s, sort,
+                                                      sorted)
+               : router_dispatch<__nv_bfloat16, false>(x, tokens, hidden, r, E, K, logits, idx, gates, s, sort,
+                                                       sorted);
 }
 
 tf_status launch_route(const void* logits, int64_t tokens, int E, int K, int act, void* probs,
