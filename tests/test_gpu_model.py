@@ -77,6 +77,46 @@ def test_prefill_then_decode_matches_oracle(tiny):
     assert lg.device.type == "cpu" and lg.shape == (2, cfg.vocab)
 
 
+def test_decode_after_large_prefill_matches_oracle():
+    """A 16-request prefill (1024 rows: the MoE workspace laid out for 2048
+    routes), then decode steps of all 16 requests (32 routes: tensor-core
+    expert tiles on the split schedule with the route sort fused into the
+    router).  The arrival counters those use must not sit on the prefill's
+    data: every decode row matches the oracle."""
+    import dataclasses
+
+    from trifuse_b200.model import Model, Session
+    from trifuse_b200.quant import synthetic_olmoe
+    cfg = dataclasses.replace(tiny_cfg(), capacity=128)
+    w = synthetic_olmoe(cfg, seed=29, device="cuda")
+    ow = oracle_weights(w, cfg)
+    ocfg = oracle.OLMoEConfig(layers=cfg.layers, hidden=cfg.hidden, heads=cfg.heads, head_dim=cfg.head_dim,
+                              intermediate=cfg.intermediate, vocab=cfg.vocab, experts=cfg.experts,
+                              top_k=cfg.top_k, capacity=128, act="f16")
+    model = Model(cfg, w)
+    B, T = 16, 64
+    sess = Session(model, max_batch=B, capacity=128, max_prefill_tokens=B * T)
+    rng = np.random.default_rng(31)
+    prompts = [rng.integers(0, cfg.vocab, size=T) for _ in range(B)]
+    caches = [([np.zeros((cfg.heads, 128, cfg.head_dim), np.float32) for _ in range(cfg.layers)],
+               [np.zeros((cfg.heads, 128, cfg.head_dim), np.float32) for _ in range(cfg.layers)])
+              for _ in range(B)]
+    try:
+        lg = host(sess.prefill(list(range(B)), prompts))
+        for r in range(B):
+            ref = oracle.model_forward(prompts[r], ow, ocfg, caches[r][0], caches[r][1], 0)
+            assert_logits_close(lg[r], ref, "f16")
+        for step in range(2):
+            toks = rng.integers(0, cfg.vocab, size=B)
+            lg = host(sess.decode(torch.tensor(toks, dtype=torch.int64, device="cuda")))
+            for r in range(B):
+                ref = oracle.model_forward(toks[r:r + 1], ow, ocfg, caches[r][0], caches[r][1], T + step)
+                assert_logits_close(lg[r], ref, "f16")
+    finally:
+        sess.close()
+        model.close()
+
+
 def test_session_admission_rules(tiny):
     from trifuse_b200 import TriFuseError
     cfg, model, sess, ow, ocfg = tiny

@@ -69,82 +69,110 @@ __global__ void rope_table_kernel(float theta, int positions, float2* __restrict
   tab[i] = make_float2(cs, sn);
 }
 
+// One warp per row (8 rows per block, no block barriers): Q/K RMSNorm,
+// RoPE, K/V append.  Lane l holds the 8-element chunks c = l + 32 m of a
+// row, so group m of 32 chunks is one warp butterfly, and the group totals
+// add in m order: the sum of squares is rms_norm_kernel's order (chunk sums,
+// butterflies over 32 chunks, group totals in order), bit-identical.  A
+// chunk's RoPE partner (the same head's other half, chunk c + 8) sits in
+// lane l ^ 8.  The row's width is W = heads * 128 <= 256 * 64.
+constexpr int kAppendRows = 8;
+constexpr int kAppendMaxGroups = 64;  // W / 256
+
 template <typename T>
-__global__ void __launch_bounds__(kAttnThreads)
-    attn_append_kernel(const T* __restrict__ qkv, int heads, const __half* __restrict__ qn,
-                       const __half* __restrict__ kn, float eps, float theta,
-                       const int32_t* __restrict__ pos, const int32_t* __restrict__ req,
-                       __half* k_cache, __half* v_cache, int cap, T* __restrict__ q_out,
-                       const float2* __restrict__ rope) {
-  __shared__ float tot_s[64];
-  __shared__ float bcast;
-  __shared__ float inv_s[kHeadDim / 2];  // RoPE inverse frequencies theta^(-2d/D)
-  const int64_t r = blockIdx.x;
-  const int t = threadIdx.x;
+__device__ __forceinline__ float warp_row_sumsq(const T* row, int groups, int lane, float (*f)[8]) {
+  float tot = 0.f;
+  for (int m = 0; m < groups; ++m) {
+    const float v = warp_sum_butterfly(chunk_sumsq8(f[m]));
+    tot = m == 0 ? v : __fadd_rn(tot, v);
+  }
+  return tot;
+}
+
+template <typename T, int G>
+__global__ void __launch_bounds__(kAppendRows * 32)
+    attn_append_kernel(const T* __restrict__ qkv, int64_t rows, int heads, const __half* __restrict__ qn,
+                       const __half* __restrict__ kn, float eps, float theta, const int32_t* __restrict__ pos,
+                       const int32_t* __restrict__ req, __half* k_cache, __half* v_cache, int cap,
+                       T* __restrict__ q_out, const float2* __restrict__ rope) {
+  __shared__ float inv_s[kHeadDim / 2];  // RoPE inverse frequencies theta^(-2d/D) (no table)
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if (!rope) {
+    for (int d = threadIdx.x; d < kHeadDim / 2; d += blockDim.x)
+      inv_s[d] = (float)pow((double)theta, -2.0 * (double)d / (double)kHeadDim);
+    __syncthreads();
+  }
+  const int64_t r = (int64_t)blockIdx.x * kAppendRows + warp;
+  if (r >= rows) return;
   const int W = heads * kHeadDim;
-  if (!rope)
-    for (int d = t; d < kHeadDim / 2; d += kAttnThreads)
-      inv_s[d] = (float)pow((double)theta, -2.0 * (double)d / (double)kHeadDim);  // (synced below)
   const T* qrow = qkv + r * 3 * W;
   const T* krow = qrow + W;
   const T* vrow = qrow + 2 * W;
   const int p = pos[r];
   const int64_t q_req = req ? req[r] : r;
-  const float rq = rms_scale(block_row_sumsq<T>(qrow, W, tot_s, &bcast), W, eps);
-  const float rk = rms_scale(block_row_sumsq<T>(krow, W, tot_s, &bcast), W, eps);
-  const float fp = (float)p;
-  // Thread v takes 8 consecutive rotation pairs (d0 .. d0 + 7 of head h): one
-  // 16-byte load per operand half and one 16-byte store per output half.
   const int64_t kv_row = (q_req * heads) * cap + p;  // cache row of head 0 at this position
-  for (int v = t; v < W / 16; v += kAttnThreads) {
-    const int h = v / (kHeadDim / 16), d0 = (v % (kHeadDim / 16)) * 8;
-    const int i1 = h * kHeadDim + d0, i2 = i1 + kHeadDim / 2;
-    float cs[8], sn[8];
-    if (rope) {
-      const float4* rp = reinterpret_cast<const float4*>(rope + (int64_t)p * (kHeadDim / 2) + d0);
+  const bool first = (lane & 8) == 0;                // this lane's chunks are a head's first half
+  const int dh = (lane & 7) * 8;                     // rotation index of the chunk's element 0
+  float cs[8], sn[8];
+  if (rope) {
+    const float4* rp = reinterpret_cast<const float4*>(rope + (int64_t)p * (kHeadDim / 2) + dh);
 #pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        const float4 a = rp[k];
-        cs[2 * k] = a.x, sn[2 * k] = a.y, cs[2 * k + 1] = a.z, sn[2 * k + 1] = a.w;
-      }
-    } else {
-#pragma unroll
-      for (int k = 0; k < 8; ++k) sincosf(__fmul_rn(fp, inv_s[d0 + k]), &sn[k], &cs[k]);
+    for (int k = 0; k < 4; ++k) {
+      const float4 a = rp[k];
+      cs[2 * k] = a.x, sn[2 * k] = a.y, cs[2 * k + 1] = a.z, sn[2 * k + 1] = a.w;
     }
-    float a1[8], a2[8], w1[8], w2[8], o1[8], o2[8];
-    unpack8<__half>(ld_v4(qn + i1), w1);
-    unpack8<__half>(ld_v4(qn + i2), w2);
-    unpack8<T>(ld_v4(qrow + i1), a1);
-    unpack8<T>(ld_v4(qrow + i2), a2);
+  } else {
 #pragma unroll
-    for (int k = 0; k < 8; ++k) {
-      const float x1 = round_act<T>(__fmul_rn(__fmul_rn(a1[k], rq), w1[k]));
-      const float x2 = round_act<T>(__fmul_rn(__fmul_rn(a2[k], rq), w2[k]));
-      o1[k] = x1 * cs[k] - x2 * sn[k];
-      o2[k] = x1 * sn[k] + x2 * cs[k];
-    }
-    *reinterpret_cast<uint4*>(q_out + r * W + i1) = pack8<T>(o1);
-    *reinterpret_cast<uint4*>(q_out + r * W + i2) = pack8<T>(o2);
-    unpack8<__half>(ld_v4(kn + i1), w1);
-    unpack8<__half>(ld_v4(kn + i2), w2);
-    unpack8<T>(ld_v4(krow + i1), a1);
-    unpack8<T>(ld_v4(krow + i2), a2);
-#pragma unroll
-    for (int k = 0; k < 8; ++k) {
-      const float x1 = round_act<T>(__fmul_rn(__fmul_rn(a1[k], rk), w1[k]));
-      const float x2 = round_act<T>(__fmul_rn(__fmul_rn(a2[k], rk), w2[k]));
-      o1[k] = round_act<T>(x1 * cs[k] - x2 * sn[k]);
-      o2[k] = round_act<T>(x1 * sn[k] + x2 * cs[k]);
-    }
-    __half* kdst = k_cache + (kv_row + (int64_t)h * cap) * kHeadDim + d0;
-    *reinterpret_cast<uint4*>(kdst) = pack8<__half>(o1);
-    *reinterpret_cast<uint4*>(kdst + kHeadDim / 2) = pack8<__half>(o2);
+    for (int k = 0; k < 8; ++k) sincosf(__fmul_rn((float)p, inv_s[dh + k]), &sn[k], &cs[k]);
   }
-  for (int c = t; c < W / 8; c += kAttnThreads) {
+  float f[G][8];
+  // q: norm, rotate, store
+#pragma unroll
+  for (int m = 0; m < G; ++m) unpack8<T>(ld_v4(qrow + 8 * (lane + 32 * m)), f[m]);
+  const float rq = rms_scale(warp_row_sumsq<T>(qrow, G, lane, f), W, eps);
+#pragma unroll
+  for (int m = 0; m < G; ++m) {
+    const int c = lane + 32 * m;
+    float w[8], x[8], o[8];
+    unpack8<__half>(ld_v4(qn + 8 * c), w);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) x[k] = round_act<T>(__fmul_rn(__fmul_rn(f[m][k], rq), w[k]));
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const float y = __shfl_xor_sync(0xffffffffu, x[k], 8);  // the partner half
+      const float x1 = first ? x[k] : y, x2 = first ? y : x[k];
+      o[k] = first ? x1 * cs[k] - x2 * sn[k] : x1 * sn[k] + x2 * cs[k];
+    }
+    *reinterpret_cast<uint4*>(q_out + r * W + 8 * c) = pack8<T>(o);
+  }
+  // k: norm, rotate, append
+#pragma unroll
+  for (int m = 0; m < G; ++m) unpack8<T>(ld_v4(krow + 8 * (lane + 32 * m)), f[m]);
+  const float rk = rms_scale(warp_row_sumsq<T>(krow, G, lane, f), W, eps);
+#pragma unroll
+  for (int m = 0; m < G; ++m) {
+    const int c = lane + 32 * m;
+    float w[8], x[8], o[8];
+    unpack8<__half>(ld_v4(kn + 8 * c), w);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) x[k] = round_act<T>(__fmul_rn(__fmul_rn(f[m][k], rk), w[k]));
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const float y = __shfl_xor_sync(0xffffffffu, x[k], 8);
+      const float x1 = first ? x[k] : y, x2 = first ? y : x[k];
+      o[k] = round_act<T>(first ? x1 * cs[k] - x2 * sn[k] : x1 * sn[k] + x2 * cs[k]);
+    }
     const int h = c / (kHeadDim / 8), d0 = (c % (kHeadDim / 8)) * 8;
-    float f[8];
-    unpack8<T>(ld_v4(vrow + 8 * c), f);
-    *reinterpret_cast<uint4*>(v_cache + (kv_row + (int64_t)h * cap) * kHeadDim + d0) = pack8<__half>(f);
+    *reinterpret_cast<uint4*>(k_cache + (kv_row + (int64_t)h * cap) * kHeadDim + d0) = pack8<__half>(o);
+  }
+  // v: append
+#pragma unroll
+  for (int m = 0; m < G; ++m) {
+    const int c = lane + 32 * m;
+    float v[8];
+    unpack8<T>(ld_v4(vrow + 8 * c), v);
+    const int h = c / (kHeadDim / 8), d0 = (c % (kHeadDim / 8)) * 8;
+    *reinterpret_cast<uint4*>(v_cache + (kv_row + (int64_t)h * cap) * kHeadDim + d0) = pack8<__half>(v);
   }
 }
 
@@ -344,9 +372,22 @@ static tf_status attention_impl(const AttnProblem& a, cudaStream_t s) {
   float* pl = c.take<float>(parts * 4);
   float* po = c.take<float>(parts * kHeadDim * 4);
   if (!a.arrivals_zero) TF_CUDA(cudaMemsetAsync(arrivals, 0, (size_t)a.rows * a.heads * 4, s));
-  attn_append_kernel<T><<<(unsigned)a.rows, kAttnThreads, 0, s>>>(
-      (const T*)a.qkv, a.heads, (const __half*)a.q_norm, (const __half*)a.k_norm, a.eps, a.theta,
-      a.pos, a.req, (__half*)a.k_cache, (__half*)a.v_cache, a.capacity, qr, (const float2*)a.rope);
+  {
+    const unsigned blocks = (unsigned)((a.rows + kAppendRows - 1) / kAppendRows);
+#define TF_APPEND(GG)                                                                                        \
+  attn_append_kernel<T, GG><<<blocks, kAppendRows * 32, 0, s>>>(                                            \
+      (const T*)a.qkv, a.rows, a.heads, (const __half*)a.q_norm, (const __half*)a.k_norm, a.eps, a.theta,   \
+      a.pos, a.req, (__half*)a.k_cache, (__half*)a.v_cache, a.capacity, qr, (const float2*)a.rope)
+    switch (a.heads * kHeadDim / 256) {
+      case 1: TF_APPEND(1); break;
+      case 2: TF_APPEND(2); break;
+      case 4: TF_APPEND(4); break;
+      case 8: TF_APPEND(8); break;
+      case 16: TF_APPEND(16); break;
+      default: return set_error(TF_ERR_UNSUPPORTED, "attention: width %d", a.heads * kHeadDim);
+    }
+#undef TF_APPEND
+  }
   TF_TRY(check_launch("attn_append"));
   // Queries: every row, or only the rows a.qrows lists (output row i for
   // a.qrows[i]); none when a.nq == 0 (the rows only extend the cache).
