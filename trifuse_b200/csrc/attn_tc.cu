@@ -1,26 +1,28 @@
 // Prefill attention on the sm_100a tensor cores (tcgen05, TMEM, TMA).
 //
-// One block per (query block of up to 128 consecutive rows of one request,
-// head): causal softmax(Q K^T * scale) V over keys 0 .. pos of the request's
-// own cache, FlashAttention-style in 128-key tiles.  Replaces the reference's
-// prefill SDPA (MLXNativeGraniteMoEPrefill.h:446-483, kvcache
-// update_and_attend over the whole chunk with a causal mask).
+// One block per (query block of up to 256 consecutive rows of one request,
+// head), split into two halves A (rows 0-127) and B (rows 128-255), each with
+// its own softmax warpgroup, so the tensor core computes one half's products
+// while the other half's softmax runs: causal softmax(Q K^T * scale) V over
+// keys 0 .. pos of the request's own cache, FlashAttention-style in 128-key
+// tiles.  Replaces the reference's prefill SDPA (MLXNativeGraniteMoEPrefill.h:
+// 446-483, kvcache update_and_attend over the whole chunk with a causal mask).
 //
-// Roles (192 threads):
-//   warps 0-3  softmax: thread r owns query row r = TMEM lane r.  They write
-//              the f16 Q tile into shared memory, then per key tile read the
-//              fp32 scores S from TMEM, mask, take the running max, write
-//              P = 2^(S*log2e*scale - m) as f16 into TMEM and add the row sum;
-//              at the end they read O from TMEM and write O / l.
-//   warp 4     loader: TMA of the K and V tiles (two 64-column boxes each,
+// Roles (320 threads):
+//   warps 0-3 / 4-7  softmax of half A / B: thread r owns the half's query
+//              row r = TMEM lane r.  They write their f16 Q tile into shared
+//              memory, then per key tile read the fp32 scores S from TMEM,
+//              mask, take the running max, write P = 2^(S*log2e*scale - m)
+//              as f16 into TMEM over S's first 64 columns and add the row
+//              sum; at the end they read O from TMEM and write O / l.
+//   warp 8     loader: TMA of the K and V tiles (two 64-column boxes each,
 //              128-byte swizzle) into a two-stage ring.
-//   warp 5     MMA: allocates TMEM; one elected lane issues
-//                S_j = Q K_j^T  (A = Q, B = K_j, both K-major in shared memory)
-//                O  += P_j V_j  (A = P_j in TMEM, B = V_j MN-major in shared memory)
-//              issuing S_{j+1} before waiting for P_j, so the next scores
-//              are computed while the softmax of this tile runs.
-// TMEM columns: O [0,128), S buffers [128,256) and [256,384), P buffers
-// [384,448) and [448,512) (two f16 per column).
+//   warp 9     MMA: allocates TMEM; one elected lane issues, per key tile,
+//                S_A = Q_A K^T, S_B = Q_B K^T   (Q, K K-major in shared memory)
+//                O_A += P_A V, O_B += P_B V      (P in TMEM, V MN-major)
+//              a half's next S only after its previous P V has completed
+//              (P overlays S).
+// TMEM columns: O_A [0,128), O_B [128,256), S_A [256,384), S_B [384,512).
 //
 // The running max is refreshed lazily: a row keeps the max it used for P
 // until a tile raises it by more than 8 (log2 units), so P <= 256 and O is
@@ -29,8 +31,9 @@
 //
 // Keys past the block's last row hold whatever the cache slot holds (the
 // tile reads whole 128-key rows); their scores are masked, and the softmax
-// threads zero those V rows in shared memory before the P V product (a
-// masked P of 0 times a non-finite stale value would be NaN).
+// threads of the half whose P V of that tile runs first zero those V rows in
+// shared memory before it (a masked P of 0 times a non-finite stale value
+// would be NaN).
 //
 // Every wait is bounded; an expired wait records a code in the tensor-core
 // error flag (61-69) and the block winds down without hanging.
@@ -50,26 +53,26 @@ namespace {
 
 using namespace tc;
 
-constexpr int kFaRows = 128;   // query rows per block
+constexpr int kFaRows = 128;   // query rows per half
 constexpr int kFaKeys = 128;   // keys per tile
 constexpr int kFaD = 128;      // head dim
-constexpr int kFaThreads = 192;
-constexpr int kFaLoadWarp = 4, kFaMmaWarp = 5;
+constexpr int kFaThreads = 320;
+constexpr int kFaLoadWarp = 8, kFaMmaWarp = 9;
 constexpr int kTileBytes = kFaKeys * kFaD * 2;  // 32 KB: [2 column halves][128 rows][128 B]
 constexpr int kHalfBytes = kTileBytes / 2;
-constexpr int kOffQ = 0;
-constexpr int kOffK = kTileBytes;                  // stage s at kOffK + s * 2 * kTileBytes
-constexpr int kOffV = 2 * kTileBytes;              // stage s at kOffV + s * 2 * kTileBytes
-constexpr int kOffBar = 5 * kTileBytes;            // 160 KB
+constexpr int kOffQ = 0;                           // half X's Q at kOffQ + X * kTileBytes
+constexpr int kOffK = 2 * kTileBytes;              // stage s at kOffK + s * 2 * kTileBytes
+constexpr int kOffV = 3 * kTileBytes;              // stage s at kOffV + s * 2 * kTileBytes
+constexpr int kOffBar = 6 * kTileBytes;            // 192 KB
 constexpr int kFaSmem = kOffBar + 256 + 1024;      // + barrier block + alignment slack
-constexpr uint32_t kColO = 0, kColS = 128, kColP = 384;
+constexpr uint32_t kColO = 0, kColS = 256;         // half X: O at kColO + 128 X, S (and P) at kColS + 128 X
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kRescale = 8.f;
 
 struct FaParams {
   CUtensorMap tm_k, tm_v;  // f16 [requests * heads * capacity][128], box {64, 128}, 128B swizzle
   const void* q;           // act [rows][heads * 128], roped
-  const int4* blocks;      // {first row, rows <= 128, request, first position}
+  const int4* blocks;      // {first row, rows <= 256, request, first position}
   void* out;               // act [rows][heads * 128]
   int heads, cap;
   float scale_log2;        // scale * log2(e)
@@ -170,6 +173,25 @@ __device__ __forceinline__ float poly_exp2(float x) {
   return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
 }
 
+__device__ __forceinline__ uint64_t f2_pack(float a, float b) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ void f2_unpack(uint64_t v, float& a, float& b) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(v));
+}
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+
 __device__ __forceinline__ float fast_exp2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
@@ -186,16 +208,16 @@ __global__ void __launch_bounds__(kFaThreads, 1) attn_prefill_tc_kernel(const __
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(base + kOffBar);
-  uint64_t* q_full = bars;          // 128 softmax threads wrote Q
-  uint64_t* k_full = bars + 1;      // [2] TMA
-  uint64_t* v_full = bars + 3;      // [2] TMA
-  uint64_t* kv_empty = bars + 5;    // [2] MMA commit after P V
-  uint64_t* s_full = bars + 7;      // [2] MMA commit after Q K^T
-  uint64_t* p_full = bars + 9;      // [2] 128 softmax threads wrote P (and rescaled O)
-  uint64_t* o_done = bars + 11;     // MMA commit after each P V
-  uint64_t* drain = bars + 12;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 13);
-  FaCtl* ctl = reinterpret_cast<FaCtl*>(base + kOffBar + 128);
+  uint64_t* q_full = bars;          // [2] a half's 128 softmax threads wrote its Q
+  uint64_t* k_full = bars + 2;      // [2 stages] TMA
+  uint64_t* v_full = bars + 4;      // [2 stages] TMA
+  uint64_t* kv_empty = bars + 6;    // [2 stages] MMA commit after the tile's P V products
+  uint64_t* s_full = bars + 8;      // [2 halves] MMA commit after Q K^T
+  uint64_t* p_full = bars + 10;     // [2 halves] 128 softmax threads wrote P (and rescaled O)
+  uint64_t* o_done = bars + 12;     // [2 halves] MMA commit after each P V
+  uint64_t* drain = bars + 14;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 15);
+  FaCtl* ctl = reinterpret_cast<FaCtl*>(base + kOffBar + 192);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int4 blk = p.blocks[blockIdx.x];
@@ -204,18 +226,23 @@ __global__ void __launch_bounds__(kFaThreads, 1) attn_prefill_tc_kernel(const __
   const int W = p.heads * kFaD;
   const int kend = pos0 + nrows;  // keys [0, kend) exist
   const int ntiles = (kend + kFaKeys - 1) / kFaKeys;
+  // Half X: rows [128 X, 128 X + n_x), key tiles [0, nt_x).
+  const int n_a = nrows < kFaRows ? nrows : kFaRows, n_b = nrows - n_a;
+  const int nt_a = (pos0 + n_a + kFaKeys - 1) / kFaKeys, nt_b = n_b > 0 ? ntiles : 0;
+  // The half whose P V of the last tile runs first zeroes its V rows past kend.
+  const int zero_half = nt_a == ntiles ? 0 : 1;
   int* err = p.err;
 
   if (tid == 0) {
-    mbar_init(q_full, 128);
     for (int i = 0; i < 2; ++i) {
+      mbar_init(&q_full[i], 128);
       mbar_init(&k_full[i], 1);
       mbar_init(&v_full[i], 1);
       mbar_init(&kv_empty[i], 1);
       mbar_init(&s_full[i], 1);
       mbar_init(&p_full[i], 128);
+      mbar_init(&o_done[i], 1);
     }
-    mbar_init(o_done, 1);
     mbar_init(drain, 1);
     const long long lim = *p.wait_cycles;
     ctl->abort = 0;
@@ -265,88 +292,92 @@ __global__ void __launch_bounds__(kFaThreads, 1) attn_prefill_tc_kernel(const __
     const uint32_t leader = elect_one();
     const uint32_t id_qk = idesc_f16(kFaRows, kFaKeys);
     const uint32_t id_pv = idesc_f16(kFaRows, kFaD) | (1u << 16);  // B (V) MN-major
-    const uint32_t qa = smem_addr(base + kOffQ);
-    auto issue_qk = [&](int j) {
-      const int st = j & 1;
-      const uint32_t ka = smem_addr(base + kOffK + st * 2 * kTileBytes);
-      const uint32_t d = tmem + kColS + (uint32_t)(st * 128);
-#pragma unroll
-      for (int s = 0; s < kFaD / 16; ++s) {
-        const uint32_t off = (uint32_t)((s >> 2) * kHalfBytes + (s & 3) * 32);
-        mma_f16(leader, d, sw128_desc(qa + off), sw128_desc(ka + off), id_qk, s > 0 ? 1u : 0u);
-      }
-      mma_commit(leader, &s_full[st]);
-    };
-    bool ok = fa_warp_wait(q_full, 0, ctl, err, 62) && fa_warp_wait(&k_full[0], 0, ctl, err, 63);
-    if (ok) {
-      tc_fence_after();
-      issue_qk(0);
-    }
+    bool ok = fa_warp_wait(&q_full[0], 0, ctl, err, 62) && (nt_b == 0 || fa_warp_wait(&q_full[1], 0, ctl, err, 62));
     for (int j = 0; j < ntiles && ok; ++j) {
       const int st = j & 1;
-      if (j + 1 < ntiles) {
-        if (!(ok = fa_warp_wait(&k_full[(j + 1) & 1], (uint32_t)(((j + 1) >> 1) & 1), ctl, err, 63))) break;
+      if (!(ok = fa_warp_wait(&k_full[st], (uint32_t)((j >> 1) & 1), ctl, err, 63))) break;
+      const uint32_t ka = smem_addr(base + kOffK + st * 2 * kTileBytes);
+      for (int x = 0; x < 2 && ok; ++x) {
+        if (j >= (x == 0 ? nt_a : nt_b)) continue;
+        // P of the half's previous tile overlays S: its P V has completed.
+        if (j >= 1 && !(ok = fa_warp_wait(&o_done[x], (uint32_t)((j - 1) & 1), ctl, err, 64))) break;
         tc_fence_after();
-        issue_qk(j + 1);
-      }
-      if (!(ok = fa_warp_wait(&p_full[st], (uint32_t)((j >> 1) & 1), ctl, err, 64))) break;
-      if (!(ok = fa_warp_wait(&v_full[st], (uint32_t)((j >> 1) & 1), ctl, err, 65))) break;
-      tc_fence_after();
-      const uint32_t va = smem_addr(base + kOffV + st * 2 * kTileBytes);
-      const uint32_t pa = tmem + kColP + (uint32_t)(st * 64);
+        const uint32_t qa = smem_addr(base + kOffQ + x * kTileBytes);
+        const uint32_t d = tmem + kColS + (uint32_t)(x * 128);
 #pragma unroll
-      for (int s = 0; s < kFaKeys / 16; ++s)
-        mma_f16_ts(leader, tmem + kColO, pa + 8 * s, sw128_mn_desc(va + s * 2048, kHalfBytes, 1024), id_pv,
-                   (j > 0 || s > 0) ? 1u : 0u);
-      mma_commit(leader, &kv_empty[st]);
-      mma_commit(leader, o_done);
+        for (int s = 0; s < kFaD / 16; ++s) {
+          const uint32_t off = (uint32_t)((s >> 2) * kHalfBytes + (s & 3) * 32);
+          mma_f16(leader, d, sw128_desc(qa + off), sw128_desc(ka + off), id_qk, s > 0 ? 1u : 0u);
+        }
+        mma_commit(leader, &s_full[x]);
+      }
+      if (!ok) break;
+      if (!(ok = fa_warp_wait(&v_full[st], (uint32_t)((j >> 1) & 1), ctl, err, 65))) break;
+      const uint32_t va = smem_addr(base + kOffV + st * 2 * kTileBytes);
+      for (int x = 0; x < 2 && ok; ++x) {
+        if (j >= (x == 0 ? nt_a : nt_b)) continue;
+        if (!(ok = fa_warp_wait(&p_full[x], (uint32_t)(j & 1), ctl, err, 66))) break;
+        tc_fence_after();
+        const uint32_t pa = tmem + kColS + (uint32_t)(x * 128);
+#pragma unroll
+        for (int s = 0; s < kFaKeys / 16; ++s)
+          mma_f16_ts(leader, tmem + kColO + (uint32_t)(x * 128), pa + 8 * s,
+                     sw128_mn_desc(va + s * 2048, kHalfBytes, 1024), id_pv, (j > 0 || s > 0) ? 1u : 0u);
+        mma_commit(leader, &o_done[x]);
+      }
+      if (ok) mma_commit(leader, &kv_empty[st]);
     }
     // Every MMA issued by this warp completes before TMEM is released.
     mma_commit(leader, drain);
     fa_drain(drain, 0, err);
   } else {
-    // ---- softmax warps 0-3: thread r = query row r = TMEM lane r.
-    const int r = tid;
-    const uint32_t lane_base = tmem + ((uint32_t)(warp * 32) << 16);
+    // ---- softmax warps: half x = warp / 4, thread r = the half's query row r = TMEM lane r.
+    const int x = warp >> 2;
+    const int r = tid - x * 128;
+    const int n_x = x == 0 ? n_a : n_b, nt_x = x == 0 ? nt_a : nt_b;
+    const int pos_x = pos0 + x * kFaRows;  // position of the half's row 0
+    const uint32_t lane_base = tmem + ((uint32_t)((warp & 3) * 32) << 16);
+    const uint32_t col_o = kColO + (uint32_t)(x * 128), col_s = kColS + (uint32_t)(x * 128);
     // Q tile -> f16, K-major 128-byte swizzle: row r at r * 128 of each
     // 64-column half, 16-byte chunk c at (c ^ (r & 7)) * 16.
     {
-      const T* qrow = static_cast<const T*>(p.q) + (int64_t)(row0 + r) * W + h * kFaD;
+      const T* qrow = static_cast<const T*>(p.q) + (int64_t)(row0 + x * kFaRows + r) * W + h * kFaD;
+      uint8_t* qs = base + kOffQ + x * kTileBytes;
 #pragma unroll 4
       for (int c = 0; c < 16; ++c) {
         uint4 v = make_uint4(0, 0, 0, 0);
-        if (r < nrows) {
+        if (r < n_x) {
           float f[8];
           unpack8<T>(ld_v4(qrow + 8 * c), f);
           v = pack8<__half>(f);
         }
         const int cc = c & 7;
-        *reinterpret_cast<uint4*>(base + kOffQ + (c >> 3) * kHalfBytes + r * 128 + ((cc ^ (r & 7)) << 4)) = v;
+        *reinterpret_cast<uint4*>(qs + (c >> 3) * kHalfBytes + r * 128 + ((cc ^ (r & 7)) << 4)) = v;
       }
       fence_proxy_async();
-      mbar_arrive(q_full);
+      mbar_arrive(&q_full[x]);
     }
-    // Rows past the block attend as its last row (their output is dropped).
-    const int pr = pos0 + (r < nrows ? r : nrows - 1);
+    // Rows past the half attend as the block's last row (their output is dropped).
+    const int pr = pos_x + (r < n_x ? r : (n_x > 0 ? n_x - 1 : 0));
     float m_used = -INFINITY, l = 0.f;
     bool ok = true;
     int j = 0;
-    for (; j < ntiles && ok; ++j) {
+    for (; j < nt_x && ok; ++j) {
       const int st = j & 1;
-      if (!(ok = fa_warp_wait(&s_full[st], (uint32_t)((j >> 1) & 1), ctl, err, 66))) break;
+      if (!(ok = fa_warp_wait(&s_full[x], (uint32_t)(j & 1), ctl, err, 67))) break;
       tc_fence_after();
       float sc[128];
-      tmem_ld64(lane_base + kColS + st * 128, sc);
-      tmem_ld64(lane_base + kColS + st * 128 + 64, sc + 64);
+      tmem_ld64(lane_base + col_s, sc);
+      tmem_ld64(lane_base + col_s + 64, sc + 64);
       const int lim = pr - j * kFaKeys;  // keys c > lim of this tile are masked
       // Eight independent partial maxima and sums keep the chains short.
       // The max is taken on the raw scores (the scale is positive) and the
       // scale is folded into the exponent's FMA; only tiles that reach past
-      // the block's first row need the causal mask.
+      // the half's first row need the causal mask.
       float mp[8];
 #pragma unroll
       for (int i = 0; i < 8; ++i) mp[i] = -INFINITY;
-      if ((j + 1) * kFaKeys > pos0 + 1) {
+      if ((j + 1) * kFaKeys > pos_x + 1) {
 #pragma unroll
         for (int c = 0; c < 128; ++c) {
           const float t = c > lim ? -INFINITY : sc[c];
@@ -367,45 +398,56 @@ __global__ void __launch_bounds__(kFaThreads, 1) attn_prefill_tc_kernel(const __
         m_used = mx;
         l *= factor;
       }
-      // One exponential in four on the FMA pipe (the special-function unit
-      // takes eight cycles per warp instruction; the cubic nine issue slots).
-      const float nm = -m_used, sl2 = p.scale_log2;
-      uint32_t pk[64];
-      float sp[8];
-#pragma unroll
-      for (int i = 0; i < 8; ++i) sp[i] = 0.f;
-#pragma unroll
-      for (int c = 0; c < 64; ++c) {
-        const float x0 = fmaf(sc[2 * c], sl2, nm), x1 = fmaf(sc[2 * c + 1], sl2, nm);
-        const float a = fast_exp2(x0), b = (c & 1) ? poly_exp2(x1) : fast_exp2(x1);
-        sp[c & 7] += a + b;
-        pk[c] = pack_half2(a, b);
-      }
-      l += ((sp[0] + sp[1]) + (sp[2] + sp[3])) + ((sp[4] + sp[5]) + (sp[6] + sp[7]));
       if (j >= 1) {
-        // P V of the previous tile is done: O is stable and this P buffer
-        // (last read two tiles ago) is free.
-        if (!(ok = fa_warp_wait(o_done, (uint32_t)((j - 1) & 1), ctl, err, 67))) break;
+        // The previous tile's P V is done: O is stable and P may overlay S.
+        if (!(ok = fa_warp_wait(&o_done[x], (uint32_t)((j - 1) & 1), ctl, err, 68))) break;
         tc_fence_after();
         if (__any_sync(0xffffffffu, factor != 1.f)) {
 #pragma unroll 1
           for (int c = 0; c < 128; c += 32) {
             float o[32];
-            tmem_ld32(lane_base + kColO + c, o);
+            tmem_ld32(lane_base + col_o + c, o);
             uint32_t w[32];
 #pragma unroll
             for (int i = 0; i < 32; ++i) w[i] = __float_as_uint(o[i] * factor);
-            tmem_st16(lane_base + kColO + c, w);
-            tmem_st16(lane_base + kColO + c + 16, w + 16);
+            tmem_st16(lane_base + col_o + c, w);
+            tmem_st16(lane_base + col_o + c + 16, w + 16);
           }
         }
       }
+      // P in two halves of 64 keys (32 TMEM columns each) over S's first 64
+      // columns; one exponential in four on the FMA pipe (the special-function
+      // unit takes eight cycles per warp instruction; the cubic nine issue
+      // slots).
+      // The exponent arguments and the row sums run on packed fp32 pairs
+      // (fma.rn / add.rn .f32x2, each lane rounded as the scalar op).
+      const uint64_t sl2 = f2_pack(p.scale_log2, p.scale_log2), nm = f2_pack(-m_used, -m_used);
+      uint64_t sp[4];
 #pragma unroll
-      for (int c = 0; c < 64; c += 16) tmem_st16(lane_base + kColP + st * 64 + c, pk + c);
+      for (int i = 0; i < 4; ++i) sp[i] = 0ull;  // (+0, +0)
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        uint32_t pk[32];
+#pragma unroll
+        for (int c = 0; c < 32; ++c) {
+          const int k0 = 64 * half + 2 * c;
+          float x0, x1;
+          f2_unpack(f2_fma(f2_pack(sc[k0], sc[k0 + 1]), sl2, nm), x0, x1);
+          const float a = fast_exp2(x0), b = (c & 1) ? poly_exp2(x1) : fast_exp2(x1);
+          sp[c & 3] = f2_add(sp[c & 3], f2_pack(a, b));
+          pk[c] = pack_half2(a, b);
+        }
+        tmem_st16(lane_base + col_s + 32 * half, pk);
+        tmem_st16(lane_base + col_s + 32 * half + 16, pk + 16);
+      }
+      float s8[8];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) f2_unpack(sp[i], s8[2 * i], s8[2 * i + 1]);
+      l += ((s8[0] + s8[1]) + (s8[2] + s8[3])) + ((s8[4] + s8[5]) + (s8[6] + s8[7]));
       tmem_st_wait();
-      if ((j + 1) * kFaKeys > kend) {
+      if (x == zero_half && j == ntiles - 1 && (j + 1) * kFaKeys > kend) {
         // Last tile: zero the V rows of keys that do not exist yet.
-        if (!(ok = fa_warp_wait(&v_full[st], (uint32_t)((j >> 1) & 1), ctl, err, 68))) break;
+        if (!(ok = fa_warp_wait(&v_full[st], (uint32_t)((j >> 1) & 1), ctl, err, 69))) break;
         if (j * kFaKeys + r >= kend) {
           uint8_t* vrow = base + kOffV + st * 2 * kTileBytes + r * 128;
 #pragma unroll
@@ -417,17 +459,17 @@ __global__ void __launch_bounds__(kFaThreads, 1) attn_prefill_tc_kernel(const __
         fence_proxy_async();
       }
       tc_fence_before();
-      mbar_arrive(&p_full[st]);
+      mbar_arrive(&p_full[x]);
     }
-    if (ok && fa_warp_wait(o_done, (uint32_t)((ntiles - 1) & 1), ctl, err, 67)) {
+    if (ok && nt_x > 0 && fa_warp_wait(&o_done[x], (uint32_t)((nt_x - 1) & 1), ctl, err, 68)) {
       tc_fence_after();
       const float inv = 1.f / l;
-      T* orow = static_cast<T*>(p.out) + (int64_t)(row0 + r) * W + h * kFaD;
+      T* orow = static_cast<T*>(p.out) + (int64_t)(row0 + x * kFaRows + r) * W + h * kFaD;
 #pragma unroll 1
       for (int c = 0; c < 128; c += 32) {
         float o[32];
-        tmem_ld32(lane_base + kColO + c, o);
-        if (r < nrows) {
+        tmem_ld32(lane_base + col_o + c, o);
+        if (r < n_x) {
 #pragma unroll
           for (int i = 0; i < 32; i += 8) {
             float f[8];
@@ -450,7 +492,7 @@ __global__ void __launch_bounds__(kFaThreads, 1) attn_prefill_tc_kernel(const __
 
 size_t attn_prefill_tc_smem() { return kFaSmem; }
 
-// Prefill attention over query blocks of <= 128 rows (AttnProblem::qblocks)
+// Prefill attention over query blocks of <= 256 rows (AttnProblem::qblocks)
 // with the roped queries q (act [rows][heads * 128]).
 tf_status launch_attn_prefill_tc(const AttnProblem& a, const void* q, cudaStream_t s) {
   if (a.nqblocks <= 0) return TF_OK;

@@ -286,7 +286,7 @@ struct AttnProblem {
   const int32_t* qrows = nullptr;
   int64_t nq = 0;
 };
-constexpr int kPrefillQueryBlock = 128;
+constexpr int kPrefillQueryBlock = 256;
 size_t attention_ws_bytes(int64_t rows, int heads, int capacity, int act);
 tf_status launch_attn_prefill_tc(const AttnProblem& a, const void* q, cudaStream_t s);
 tf_status launch_rope_table(float theta, int positions, void* tab, cudaStream_t s);
