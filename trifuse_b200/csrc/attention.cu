@@ -13,10 +13,13 @@
 // 0..pos[r] of its request's cache, which is exactly the causal mask for a
 // prefill chunk and the full history for decode.
 //
-//   append  (one block per row)   : norms, ropes, writes q (act) to scratch
+//   append  (one warp per row)    : norms, ropes, writes q (act) to scratch
 //                                   and k/v (f16) into the cache slot pos[r];
 //   split   (split, head, query)  : kSplit keys -> unnormalised (max, sum, o);
-//   merge   (head, query)         : combines the splits in order.
+//                                   the last split block of a (head, query)
+//                                   to finish combines the splits in order.
+// Prefill rows grouped per request run the tensor-core kernel (attn_tc.cu)
+// after the append instead of split.
 // The queries are every row, or a listed subset (the last row of each
 // request in the last layer of a prefill, MLXNativeGraniteMoEPrefill.h:
 // 440-442, 471), or none (a cache-only chunk's last layer, :470).
@@ -32,30 +35,6 @@ constexpr int kHeadDim = 128;
 constexpr int kSplit = 256;
 constexpr int kAttnThreads = 256;
 constexpr int kKeyGroups = kAttnThreads / 16;  // half-warps per block
-
-// Sum of squares of a W-wide row in the canonical order (thread t owns the
-// 8-element chunks t + 256 i; each 32 consecutive chunks form one butterfly
-// group; group totals are added left to right).  Every thread gets the value.
-template <typename T>
-__device__ float block_row_sumsq(const T* row, int W, float* tot_s, float* bcast) {
-  const int t = threadIdx.x, lane = t & 31;
-  for (int c = t; 8 * c < W; c += kAttnThreads) {
-    float f[8];
-    unpack8<T>(ld_v4(row + 8 * c), f);
-    const float v = warp_sum_butterfly(chunk_sumsq8(f));
-    if (lane == 0) tot_s[c / 32] = v;
-  }
-  __syncthreads();
-  if (t == 0) {
-    float tot = tot_s[0];
-    for (int i = 1; i < W / 256; ++i) tot = __fadd_rn(tot, tot_s[i]);
-    *bcast = tot;
-  }
-  __syncthreads();
-  const float v = *bcast;
-  __syncthreads();
-  return v;
-}
 
 // RoPE angles of every position below `positions`: tab[p][d] = (cos, sin)
 // of fp32(p * theta^(-2d/D)), the values the append kernel computes.
@@ -177,8 +156,8 @@ __global__ void __launch_bounds__(kAppendRows * 32)
 }
 
 // The split blocks of one (query, head) count their arrivals; the last one
-// to arrive merges every part (the merge kernel's arithmetic, so the result
-// is the same) and leaves the counter at zero, so no separate merge launch
+// to arrive merges every part (in split order, as a separate merge launch
+// would) and leaves the counter at zero, so no separate merge launch
 // waits behind the slowest split.
 template <typename T>
 __device__ __forceinline__ void attn_merge_last(const int32_t* __restrict__ pos, int64_t r, int64_t z, int h,
