@@ -151,8 +151,10 @@ __global__ void __launch_bounds__(kRouterBlockWarps * 32)
 }
 
 // Router for prefill-sized batches: a block of kRouterWideWarps warps owns
-// kRouterWideTokens tokens, so each weight chunk is decoded once per 16
-// tokens; each warp takes kRouterWideExperts experts at a time, so each
+// kRouterWideTokens tokens, so each weight chunk is decoded once per 8
+// tokens (8 rather than 16: 66 KB of shared memory and 120 registers let two
+// blocks share an SM, measured 17% faster); each warp takes
+// kRouterWideExperts experts at a time, so each
 // activation pair read from shared memory feeds four experts; the per-token
 // arithmetic runs on packed fp32 pairs
 // (mul.rn.f32x2 / add.rn.f32x2: two tokens' products and sums per
@@ -164,7 +166,7 @@ __global__ void __launch_bounds__(kRouterBlockWarps * 32)
 // x[2p+1][8c+2q], x[2p][8c+2q+1], x[2p+1][8c+2q+1]); a warp's lanes read 32
 // consecutive float4 (no bank conflicts).
 constexpr int kRouterWideWarps = 8;
-constexpr int kRouterWideTokens = 16;
+constexpr int kRouterWideTokens = 8;
 constexpr int kRouterWideExperts = 4;
 
 __device__ __forceinline__ uint64_t f32x2_pack(float a, float b) {
@@ -189,7 +191,7 @@ constexpr size_t router_wide_smem() {
 }
 
 template <typename T, bool DENSE, int J>
-__global__ void __launch_bounds__(kRouterWideWarps * 32, 1)
+__global__ void __launch_bounds__(kRouterWideWarps * 32, 2)
     router_wide_kernel(const T* __restrict__ x, int64_t tokens, const T* __restrict__ wd,
                        const uint32_t* __restrict__ wq, const __half* __restrict__ ws,
                        const __half* __restrict__ wb, int E, int K, T* logits, int32_t* idx, T* gates) {
@@ -581,7 +583,7 @@ static tf_status router_dispatch_cluster(const void* x, int64_t tokens, int hidd
 }
 
 // Decode-sized batches: a cluster of 8 CTAs per token.  Up to 2048 tokens:
-// one token per block; beyond, sixteen per block on packed fp32 pairs.
+// one token per block; beyond, eight per block on packed fp32 pairs.
 template <typename T, bool DENSE>
 static tf_status router_dispatch(const void* x, int64_t tokens, int hidden,
                                  const tf_router_weight& r, int E, int K, void* logits,
