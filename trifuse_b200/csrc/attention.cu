@@ -56,7 +56,6 @@ __global__ void rope_table_kernel(float theta, int positions, float2* __restrict
 // chunk's RoPE partner (the same head's other half, chunk c + 8) sits in
 // lane l ^ 8.  The row's width is W = heads * 128 <= 256 * 64.
 constexpr int kAppendRows = 8;
-constexpr int kAppendMaxGroups = 64;  // W / 256
 
 template <typename T>
 __device__ __forceinline__ float warp_row_sumsq(const T* row, int groups, int lane, float (*f)[8]) {
