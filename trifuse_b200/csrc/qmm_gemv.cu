@@ -14,8 +14,9 @@
 //   GROUPED   - active expert a owns slots offsets[e] .. offsets[e+1] (the
 //               output of the route sort), so an expert's weights are read
 //               once for all of its tokens.
-// Each warp owns 4 rows; lane l owns the 16-byte weight chunks l + 32m of a
-// row (32 codes each) and keeps the matching activations in registers.
+// Each warp owns R rows, staged in shared memory by cp.async before use; lane
+// l owns the 16-byte weight chunks l + 32m of a row (32 codes each) and keeps
+// the matching activations in registers.
 //
 // Nibble decode: for code j (bits 4j) of a word w, j <= 4,
 //   float(0x4B000000 | (w & (0xF << 4j))) - 2^23 == code_j * 16^j  (exact),
@@ -27,8 +28,6 @@
 namespace tf {
 
 constexpr int kGemvWarps = 8;
-constexpr int kRowsPerWarp = 4;
-constexpr int kGemvRows = kGemvWarps * kRowsPerWarp;
 
 struct GemvArgs {
   const void* x;
@@ -82,10 +81,22 @@ __device__ __forceinline__ float chunk_dot(const uint4& wv, const float* xs) {
   return p;
 }
 
+// 16-byte global -> shared copy that bypasses L1 (weights are read once).
+__device__ __forceinline__ void cp_async16(uint4* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)),
+               "l"(src)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
+
+extern __shared__ __align__(16) uint4 gemv_smem[];
+
 __device__ __forceinline__ float silu_f(float g) { return g / (1.0f + expf(-g)); }
 
-template <typename T, int MODE, int EPI, int TB, int M>
+template <typename T, int MODE, int EPI, int TB, int M, int R>
 __global__ void __launch_bounds__(kGemvWarps * 32) qmm_gemv_kernel(GemvArgs a) {
+  constexpr int kGemvRows = kGemvWarps * R;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int nrb = (a.out + kGemvRows - 1) / kGemvRows;
   const int nchunk = a.in / 32;
@@ -113,7 +124,39 @@ __global__ void __launch_bounds__(kGemvWarps * 32) qmm_gemv_kernel(GemvArgs a) {
       s0 = min(max((int64_t)a.offsets[e], (int64_t)0), a.n);
       s1 = min(max((int64_t)a.offsets[e + 1], s0), a.n);
     }
-    const int row0 = rb * kGemvRows + warp * kRowsPerWarp;
+    const int row0 = rb * kGemvRows + warp * R;
+    // The weights of all R rows are requested before any is used, straight
+    // into this warp's shared-memory slots (16-byte cp.async, no registers
+    // held), together with their scales and biases, and before the
+    // activations, so every round trip of the item overlaps: at one or a few
+    // tokens the kernel is bound by bytes in flight, not by bandwidth. The
+    // staged rows serve every slot of the segment. Each lane reads back only
+    // the chunks it copied, so a per-thread wait suffices.
+    uint4* wbuf = gemv_smem + (size_t)warp * (R * NW * M * 32) + lane;
+    __half sr[R][NW][M], br[R][NW][M];
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      const int row = row0 + r;
+#pragma unroll
+      for (int w = 0; w < NW; ++w) {
+        const uint32_t* q = w == 0 ? a.q0 : a.q1;
+        const __half* sc = w == 0 ? a.s0 : a.s1;
+        const __half* bi = w == 0 ? a.b0 : a.b1;
+        const int64_t wrow = (int64_t)e * a.out + row;
+        const uint32_t* qrow = q + wrow * (a.in / 8);
+#pragma unroll
+        for (int m = 0; m < M; ++m) {
+          const int c = lane + 32 * m;
+          const bool ok = row < a.out && c < nchunk;
+          uint4* dst = wbuf + ((r * NW + w) * M + m) * 32;
+          if (ok) cp_async16(dst, qrow + 4 * c);
+          else *dst = make_uint4(0, 0, 0, 0);
+          sr[r][w][m] = ok ? sc[wrow * (a.in / 64) + c / 2] : __float2half(0.f);
+          br[r][w][m] = ok ? bi[wrow * (a.in / 64) + c / 2] : __float2half(0.f);
+        }
+      }
+    }
+    cp_async_commit();
     for (int64_t tb = s0; tb < s1; tb += TB) {
       // Activations of up to TB slots, pre-scaled, plus per-chunk sums.
       float xs[TB][M][32];
@@ -144,36 +187,24 @@ __global__ void __launch_bounds__(kGemvWarps * 32) qmm_gemv_kernel(GemvArgs a) {
           }
         }
       }
+      cp_async_wait_all();
 #pragma unroll
-      for (int r = 0; r < kRowsPerWarp; ++r) {
+      for (int r = 0; r < R; ++r) {
         const int row = row0 + r;
         if (row >= a.out) break;
         float acc[NW][TB];
 #pragma unroll
         for (int w = 0; w < NW; ++w) {
-          const uint32_t* q = w == 0 ? a.q0 : a.q1;
-          const __half* sc = w == 0 ? a.s0 : a.s1;
-          const __half* bi = w == 0 ? a.b0 : a.b1;
-          const int64_t wrow = (int64_t)e * a.out + row;
-          const uint32_t* qrow = q + wrow * (a.in / 8);
 #pragma unroll
           for (int tt = 0; tt < TB; ++tt) acc[w][tt] = 0.f;
-          uint4 wv[M];
 #pragma unroll
           for (int m = 0; m < M; ++m) {
-            const int c = lane + 32 * m;
-            wv[m] = c < nchunk ? ld_stream_v4(qrow + 4 * c) : make_uint4(0, 0, 0, 0);
-          }
+            const float s = __half2float(sr[r][w][m]);
+            const float b = __half2float(br[r][w][m]);
+            const uint4 wv = wbuf[((r * NW + w) * M + m) * 32];
 #pragma unroll
-          for (int m = 0; m < M; ++m) {
-            const int c = lane + 32 * m;
-            if (c < nchunk) {
-              const float s = __half2float(sc[wrow * (a.in / 64) + c / 2]);
-              const float b = __half2float(bi[wrow * (a.in / 64) + c / 2]);
-#pragma unroll
-              for (int tt = 0; tt < TB; ++tt)
-                acc[w][tt] = fmaf(s, chunk_dot(wv[m], xs[tt][m]), fmaf(b, xsum[tt][m], acc[w][tt]));
-            }
+            for (int tt = 0; tt < TB; ++tt)
+              acc[w][tt] = fmaf(s, chunk_dot(wv, xs[tt][m]), fmaf(b, xsum[tt][m], acc[w][tt]));
           }
 #pragma unroll
           for (int tt = 0; tt < TB; ++tt) acc[w][tt] = warp_sum_butterfly(acc[w][tt]);
@@ -203,21 +234,34 @@ __global__ void __launch_bounds__(kGemvWarps * 32) qmm_gemv_kernel(GemvArgs a) {
   }
 }
 
-template <typename T, int MODE, int EPI>
-static tf_status qmm_dispatch(const GemvArgs& a, cudaStream_t s) {
-  int sms = 148;
-  int64_t max_seg = MODE == QMM_DENSE ? 1 : MODE == QMM_PER_ROUTE ? a.n : a.experts;
-  const int nrb = (a.out + kGemvRows - 1) / kGemvRows;
-  int64_t items = max_seg * nrb;
+// Launch with R rows per warp. Each warp stages R x NW x M chunks of 512 bytes
+// (4 KB, 32 KB per block); fewer rows per warp when that leaves under one
+// block per SM, so a small matrix still spreads over every SM.
+template <typename T, int MODE, int EPI, int TB, int M>
+static tf_status gemv_launch(const GemvArgs& a, int64_t max_seg, cudaStream_t s) {
+  constexpr int NW = EPI == EPI_SWIGLU ? 2 : 1;
+  constexpr int RB = NW * M >= 8 ? 1 : 8 / (NW * M);
+  constexpr int sms = 148;
+  const int64_t nrb = (a.out + kGemvWarps * RB - 1) / (kGemvWarps * RB);
+  const bool big = max_seg * nrb >= sms;
+  const int rows = big ? RB : 1;
+  const int64_t items = max_seg * ((a.out + kGemvWarps * rows - 1) / (kGemvWarps * rows));
   if (items <= 0) return TF_OK;
   const unsigned grid = (unsigned)(items < (int64_t)sms * 8 ? items : (int64_t)sms * 8);
-  if (a.in <= 1024)
-    qmm_gemv_kernel<T, MODE, EPI, 2, 1><<<grid, kGemvWarps * 32, 0, s>>>(a);
-  else if (a.in <= 2048)
-    qmm_gemv_kernel<T, MODE, EPI, 1, 2><<<grid, kGemvWarps * 32, 0, s>>>(a);
+  const size_t smem = (size_t)kGemvWarps * rows * NW * M * 32 * sizeof(uint4);
+  if (big)
+    qmm_gemv_kernel<T, MODE, EPI, TB, M, RB><<<grid, kGemvWarps * 32, smem, s>>>(a);
   else
-    qmm_gemv_kernel<T, MODE, EPI, 1, 4><<<grid, kGemvWarps * 32, 0, s>>>(a);
+    qmm_gemv_kernel<T, MODE, EPI, TB, M, 1><<<grid, kGemvWarps * 32, smem, s>>>(a);
   return check_launch("qmm_gemv");
+}
+
+template <typename T, int MODE, int EPI>
+static tf_status qmm_dispatch(const GemvArgs& a, cudaStream_t s) {
+  const int64_t max_seg = MODE == QMM_DENSE ? 1 : MODE == QMM_PER_ROUTE ? a.n : a.experts;
+  if (a.in <= 1024) return gemv_launch<T, MODE, EPI, 2, 1>(a, max_seg, s);
+  if (a.in <= 2048) return gemv_launch<T, MODE, EPI, 1, 2>(a, max_seg, s);
+  return gemv_launch<T, MODE, EPI, 1, 4>(a, max_seg, s);
 }
 
 template <typename T>
