@@ -104,8 +104,12 @@ def test_qmm_and_gather_against_reference_golden(ops, golden_dir, act):
     assert_close(host(gb).reshape(5, 3, -1), bits_to_act(z[f"gather_bcast_{act}"], act))
 
 
+# The GEMV stages R rows per warp (R = 8 / 4 / 2 for 1024 / 2048 / 4096
+# inputs, 1 when that leaves under 148 blocks): the last two cases take the
+# multi-row form with a ragged last block (out not a multiple of 8 warps x R).
 @pytest.mark.parametrize("act,T,out,inn", [("f16", 1, 6144, 2048), ("bf16", 3, 2048, 2048),
-                                           ("f16", 2, 2048, 1024), ("bf16", 5, 512, 4096)])
+                                           ("f16", 2, 2048, 1024), ("bf16", 5, 512, 4096),
+                                           ("f16", 1, 9500, 1024), ("bf16", 2, 4700, 4096)])
 def test_qmm_random_against_oracle(ops, act, T, out, inn):
     rng = np.random.default_rng(4)
     x = oracle.to_act(rng.standard_normal((T, inn)).astype(np.float32), act)
