@@ -231,6 +231,9 @@ __global__ void __launch_bounds__(kGemvWarps * 32) qmm_gemv_kernel(GemvArgs a) {
         }
       }
     }
+    // An empty segment skipped the wait above; its copies must land before
+    // the next item reuses the slots.
+    cp_async_wait_all();
   }
 }
 
