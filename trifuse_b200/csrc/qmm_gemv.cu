@@ -1,4 +1,4 @@
-// MLX-affine 4-bit QMM / gather_qmm as a memory-bound warp-per-row GEMV.
+// MLX-affine 4-bit QMM / gather_qmm as a memory-bound GEMV, whole rows per warp.
 //
 // Restates native_affine_gather_qmm / native_affine_qmm
 // (overlays/executorch/backends/mlx/native_affine_ops.py:39-74) and the
