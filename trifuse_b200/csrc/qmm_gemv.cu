@@ -7,7 +7,7 @@
 // (decode).  y = act(sum_k x_k (code_k s_g + b_g)) with fp32 accumulation,
 // evaluated per 32-element half-group as s_g * sum(x*code) + b_g * sum(x).
 //
-// Work is a list of (segment, block of 32 output rows) items, grid-strided
+// Work is a list of (segment, block of 8 R output rows) items, grid-strided
 // over a fixed grid so the launch never depends on device-side routing:
 //   DENSE     - one segment (expert 0) holding every slot;
 //   PER_ROUTE - slot n is its own segment with expert indices[n];
