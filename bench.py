@@ -333,6 +333,7 @@ class CpuWorkload:
         v1 = rng.standard_normal((16, L + 1, 128), dtype=np.float32).astype(np.float16).astype(np.float32)
         self.kc, self.vc = [k1] * B, [v1] * B
         self.h = oracle.round_f16(rng.standard_normal((B, H)).astype(np.float32))
+        self.out = self.h  # the head's input until a layer has run (same shape)
         self.B, self.L = B, L
 
     def layer_s(self):
